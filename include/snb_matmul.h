@@ -1,0 +1,179 @@
+/*
+ * snb_matmul.h — C ABI of the B200 (sm_100a) dense-contraction library.
+ *
+ * This is the drop-in boundary for StaleyNET's GEMM hot path. Every entry point here replaces one entry point of
+ * the reference crate `staleynet-cuda` (paths below are relative to the reference repository):
+ *
+ *   snb_product / snb_operand   <- `Product` / `Operand`, crates/staleynet-cuda/src/kernels/matmul.rs:108-157
+ *   snb_matmul                  <- `Gpu::matmul`, crates/staleynet-cuda/src/ops/matmul.rs:144-172
+ *   snb_matmul_bf16             <- `Gpu::matmul` with bf16 operands (no reference counterpart: the reference has
+ *                                  only f32 tensors, device.rs:245-275; this is the bf16 tensor-core variant)
+ *   snb_gemm                    <- `Gpu::matmul` followed by the elementwise pass a caller runs on its output:
+ *                                  `add_row_bias` (ops/elementwise.rs, kernels/elementwise.rs:62),
+ *                                  `gelu_forward`/`gelu_backward` (kernels/elementwise.rs:139-159) and
+ *                                  `add_scaled` residual adds (kernels/elementwise.rs:37), fused into the epilogue
+ *   snb_causal_softmax          <- `Gpu::causal_softmax`, crates/staleynet-cuda/src/ops/attention.rs:61-81
+ *   snb_softmax_backward        <- `Gpu::softmax_backward`, crates/staleynet-cuda/src/ops/attention.rs:84-100
+ *
+ * Conventions shared by every entry point:
+ *   - All pointers are caller-owned device pointers; nothing is allocated or freed inside a call.
+ *   - `stream` is a cudaStream_t passed as void* (NULL = the legacy default stream). Calls are asynchronous and
+ *     ordered on that stream, like the reference's single `Gpu::stream` (device.rs:129-145).
+ *   - Lengths are element counts, the `len()` of the reference's `Tensor` (device.rs:262-265).
+ *   - Return value: SNB_OK or a positive SNB_ERR_* code. The reference panics on undersized operands
+ *     (ops/matmul.rs:147-149) and returns `DriverError` on launch failure; here both become status codes, and
+ *     snb_last_error() gives the message of the last failure on the calling thread.
+ */
+#ifndef SNB_MATMUL_H
+#define SNB_MATMUL_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#if defined(__GNUC__)
+#define SNB_API __attribute__((visibility("default")))
+#else
+#define SNB_API
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* Element (row, col) of matrix b of a batch is values[b*batch_stride + row*row_stride + col*col_stride].
+ * Same fields and order as `Operand` (kernels/matmul.rs:108-126); Rust's usize is uint64_t on LP64. */
+typedef struct snb_operand {
+    uint64_t row_stride;
+    uint64_t col_stride;
+    uint64_t batch_stride;
+} snb_operand;
+
+/* One batched product C_b = scale * A_b * B_b (+ C_b), A_b [rows, inner], B_b [inner, cols], C_b row-major
+ * [rows, cols] at b*output_batch_stride. Byte-identical to `Product` (kernels/matmul.rs:128-157): 88 bytes. */
+typedef struct snb_product {
+    uint64_t rows;
+    uint64_t cols;
+    uint64_t inner;
+    snb_operand left;
+    snb_operand right;
+    uint64_t output_batch_stride;
+    float scale;
+    uint32_t accumulate; /* 1: C += scale*A*B; 0: C = scale*A*B (`WriteMode::flag`, ops/mod.rs:36-43) */
+} snb_product;
+
+/* Arithmetic of a product. Maps `MatmulKernel` (device.rs:38-67): Naive/Tiled/Blocked compute exact f32
+ * (tolerance 1e-5) -> SNB_PRECISION_F32; TensorCore rounds inputs to TF32 (tolerance 2e-3) -> SNB_PRECISION_TF32.
+ * SNB_PRECISION_BF16 is the bf16 tensor-core path and needs bf16 operands (snb_matmul_bf16 / snb_gemm). */
+enum {
+    SNB_PRECISION_F32 = 0,
+    SNB_PRECISION_TF32 = 1,
+    SNB_PRECISION_BF16 = 2
+};
+
+/* Element types of snb_gemm operands and outputs. */
+enum {
+    SNB_TYPE_F32 = 0,
+    SNB_TYPE_BF16 = 1
+};
+
+/* Elementwise function applied in the epilogue of snb_gemm, after scale and bias. */
+enum {
+    SNB_ACTIVATION_NONE = 0,
+    SNB_ACTIVATION_GELU = 1,     /* out = gelu(x); x optionally stored to pre_activation (feed_forward.rs:55-59) */
+    SNB_ACTIVATION_GELU_GRAD = 2 /* out = x * gelu'(gelu_input) (`gelu_backward`, kernels/elementwise.rs:153) */
+};
+
+/* Status codes. */
+enum {
+    SNB_OK = 0,
+    SNB_ERR_LEFT_TOO_SMALL = 1,   /* "matmul: left operand too small" (ops/matmul.rs:147) */
+    SNB_ERR_RIGHT_TOO_SMALL = 2,  /* "matmul: right operand too small" (ops/matmul.rs:148) */
+    SNB_ERR_OUTPUT_TOO_SMALL = 3, /* "matmul: output too small" (ops/matmul.rs:149) */
+    SNB_ERR_INVALID_ARGUMENT = 4, /* null pointer, zero batch count, unknown enum value, bad shape */
+    SNB_ERR_UNSUPPORTED = 5,      /* combination this build does not implement (message says which) */
+    SNB_ERR_CUDA = 6,             /* a CUDA runtime/driver call failed (message carries the CUDA error) */
+    SNB_ERR_DEVICE_TIMEOUT = 7    /* a kernel's bounded wait gave up; see snb_device_status() */
+};
+
+/* Which kernel family ran the last successful call on this thread (for tests and tracing). */
+enum {
+    SNB_PATH_NONE = 0,
+    SNB_PATH_TENSOR_CORE = 1, /* tcgen05 + TMA persistent kernel */
+    SNB_PATH_SIMT = 2,        /* strided SIMT kernel: any strides and alignments, exact f32 FMA */
+    SNB_PATH_EMPTY = 3        /* nothing to compute (rows or cols is 0) */
+};
+
+/* Batched strided GEMM on f32 operands: replaces `Gpu::matmul` (ops/matmul.rs:146-171).
+ * `count` is `BatchStrides::count` (the reference passes it as the grid's z extent, launch.rs:28-48).
+ * precision: SNB_PRECISION_F32 or SNB_PRECISION_TF32.
+ * Checks, in the reference's order, left_len/right_len/output_len >= the elements the batch addresses. */
+SNB_API int snb_matmul(void* stream, const snb_product* product, uint64_t count,
+               const float* left, uint64_t left_len,
+               const float* right, uint64_t right_len,
+               float* output, uint64_t output_len,
+               int32_t precision);
+
+/* As snb_matmul, with bf16 operands (raw 16-bit bf16 bit patterns) and an f32 output; always bf16 tensor cores
+ * (or the SIMT kernel on bf16 inputs when strides or alignment rule out TMA). No reference counterpart. */
+SNB_API int snb_matmul_bf16(void* stream, const snb_product* product, uint64_t count,
+                    const uint16_t* left, uint64_t left_len,
+                    const uint16_t* right, uint64_t right_len,
+                    float* output, uint64_t output_len);
+
+/* A product with its caller's elementwise follow-up fused into the epilogue. For each output element
+ *   x   = scale * (A*B)[r,c] + (bias ? bias[c] : 0)
+ *   y   = activation(x)                      (pre_activation[r,c] = x when requested)
+ *   out = y + (residual ? residual[r,c] : 0) (+ out[r,c] when product->accumulate)
+ * Same meaning as `Linear::forward` (linear.rs:43-48) + `gelu_forward` + `add_scaled(1.0, residual, out)`
+ * (block.rs:182,188), done in one pass over the output. */
+typedef struct snb_gemm_args {
+    snb_product product;
+    uint64_t count;
+    int32_t left_type;   /* SNB_TYPE_F32 (with precision F32/TF32) or SNB_TYPE_BF16 (precision BF16) */
+    int32_t right_type;  /* must equal left_type */
+    int32_t output_type; /* SNB_TYPE_F32 or SNB_TYPE_BF16 (bf16 output needs accumulate == 0) */
+    int32_t precision;   /* SNB_PRECISION_* */
+    const void* left;
+    uint64_t left_len;
+    const void* right;
+    uint64_t right_len;
+    void* output;
+    uint64_t output_len;
+    const float* bias;          /* [cols] or NULL */
+    int32_t activation;         /* SNB_ACTIVATION_* */
+    int32_t aux_type;           /* element type of pre_activation / gelu_input: SNB_TYPE_F32 or SNB_TYPE_BF16 */
+    void* pre_activation;       /* GELU: receives x, laid out like the output; or NULL */
+    const void* gelu_input;     /* GELU_GRAD: the forward pre-activation, laid out like the output */
+    const void* residual;       /* laid out like the output, same type as the output; or NULL */
+} snb_gemm_args;
+
+SNB_API int snb_gemm(void* stream, const snb_gemm_args* args);
+
+/* In-place causal softmax of scores [rows, keys] (rows = matrices * queries): query q of each matrix sees keys
+ * 0..=q+query_offset, scaled by `scale`, later keys become 0. Replaces `Gpu::causal_softmax`
+ * (ops/attention.rs:61-81; kernel kernels/attention.rs:153-180). scores_len must be >= rows*keys. */
+SNB_API int snb_causal_softmax(void* stream, float* scores, uint64_t scores_len, uint64_t rows, uint64_t queries,
+                       uint64_t keys, float scale, uint64_t query_offset);
+
+/* In place on grad [rows, cols]: grad = p * (grad - sum(grad * p)) per row. Replaces `Gpu::softmax_backward`
+ * (ops/attention.rs:84-100; kernel kernels/attention.rs:190-207). */
+SNB_API int snb_softmax_backward(void* stream, const float* probabilities, float* grad, uint64_t rows, uint64_t cols);
+
+/* Message of the last failed call on the calling thread ("" if none). Valid until the next call. */
+SNB_API const char* snb_last_error(void);
+
+/* Kernel family used by the last successful snb_matmul/snb_matmul_bf16/snb_gemm call on this thread. */
+SNB_API int snb_last_path(void);
+
+/* Reads and clears the device-side status word of the current device: 0 if every bounded wait since the last
+ * read completed, else SNB_ERR_DEVICE_TIMEOUT. Synchronizes the device. */
+SNB_API int snb_device_status(void);
+
+/* Version of this ABI (major*100 + minor). */
+SNB_API int snb_abi_version(void);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* SNB_MATMUL_H */

@@ -1,0 +1,145 @@
+"""ctypes binding of the C ABI in include/snb_matmul.h (libsnb_b200.so).
+
+The structures mirror the header field for field; `Product` is byte-identical to the reference's `repr(C)`
+`Product` (crates/staleynet-cuda/src/kernels/matmul.rs:128-157). Loading fails loudly when the library has not
+been built: there is no fallback implementation.
+"""
+from __future__ import annotations
+
+import ctypes
+import threading
+from ctypes import POINTER, c_char_p, c_float, c_int, c_int32, c_uint16, c_uint32, c_uint64, c_void_p
+from pathlib import Path
+
+LIB_PATH = Path(__file__).resolve().parent / "_lib" / "libsnb_b200.so"
+
+PRECISION_F32 = 0
+PRECISION_TF32 = 1
+PRECISION_BF16 = 2
+
+TYPE_F32 = 0
+TYPE_BF16 = 1
+
+ACTIVATION_NONE = 0
+ACTIVATION_GELU = 1
+ACTIVATION_GELU_GRAD = 2
+
+OK = 0
+ERR_LEFT_TOO_SMALL = 1
+ERR_RIGHT_TOO_SMALL = 2
+ERR_OUTPUT_TOO_SMALL = 3
+ERR_INVALID_ARGUMENT = 4
+ERR_UNSUPPORTED = 5
+ERR_CUDA = 6
+ERR_DEVICE_TIMEOUT = 7
+
+PATH_NONE = 0
+PATH_TENSOR_CORE = 1
+PATH_SIMT = 2
+PATH_EMPTY = 3
+
+EXPORTED_SYMBOLS = (
+    "snb_matmul",
+    "snb_matmul_bf16",
+    "snb_gemm",
+    "snb_causal_softmax",
+    "snb_softmax_backward",
+    "snb_last_error",
+    "snb_last_path",
+    "snb_device_status",
+    "snb_abi_version",
+)
+
+
+class Operand(ctypes.Structure):
+    _fields_ = [("row_stride", c_uint64), ("col_stride", c_uint64), ("batch_stride", c_uint64)]
+
+
+class Product(ctypes.Structure):
+    _fields_ = [
+        ("rows", c_uint64),
+        ("cols", c_uint64),
+        ("inner", c_uint64),
+        ("left", Operand),
+        ("right", Operand),
+        ("output_batch_stride", c_uint64),
+        ("scale", c_float),
+        ("accumulate", c_uint32),
+    ]
+
+
+class GemmArgs(ctypes.Structure):
+    _fields_ = [
+        ("product", Product),
+        ("count", c_uint64),
+        ("left_type", c_int32),
+        ("right_type", c_int32),
+        ("output_type", c_int32),
+        ("precision", c_int32),
+        ("left", c_void_p),
+        ("left_len", c_uint64),
+        ("right", c_void_p),
+        ("right_len", c_uint64),
+        ("output", c_void_p),
+        ("output_len", c_uint64),
+        ("bias", c_void_p),
+        ("activation", c_int32),
+        ("aux_type", c_int32),
+        ("pre_activation", c_void_p),
+        ("gelu_input", c_void_p),
+        ("residual", c_void_p),
+    ]
+
+
+assert ctypes.sizeof(Operand) == 24
+assert ctypes.sizeof(Product) == 88
+
+_lock = threading.Lock()
+_lib: ctypes.CDLL | None = None
+
+
+def load() -> ctypes.CDLL:
+    """Loads libsnb_b200.so and declares every entry point's signature."""
+    global _lib
+    with _lock:
+        if _lib is not None:
+            return _lib
+        if not LIB_PATH.exists():
+            raise RuntimeError(
+                f"{LIB_PATH} is missing: build the sm_100a library with `python -m staleynet_b200.build`")
+        lib = ctypes.CDLL(str(LIB_PATH))
+        lib.snb_matmul.argtypes = [c_void_p, POINTER(Product), c_uint64, c_void_p, c_uint64, c_void_p, c_uint64,
+                                   c_void_p, c_uint64, c_int32]
+        lib.snb_matmul.restype = c_int
+        lib.snb_matmul_bf16.argtypes = [c_void_p, POINTER(Product), c_uint64, c_void_p, c_uint64, c_void_p,
+                                        c_uint64, c_void_p, c_uint64]
+        lib.snb_matmul_bf16.restype = c_int
+        lib.snb_gemm.argtypes = [c_void_p, POINTER(GemmArgs)]
+        lib.snb_gemm.restype = c_int
+        lib.snb_causal_softmax.argtypes = [c_void_p, c_void_p, c_uint64, c_uint64, c_uint64, c_uint64, c_float,
+                                           c_uint64]
+        lib.snb_causal_softmax.restype = c_int
+        lib.snb_softmax_backward.argtypes = [c_void_p, c_void_p, c_void_p, c_uint64, c_uint64]
+        lib.snb_softmax_backward.restype = c_int
+        lib.snb_last_error.argtypes = []
+        lib.snb_last_error.restype = c_char_p
+        lib.snb_last_path.argtypes = []
+        lib.snb_last_path.restype = c_int
+        lib.snb_device_status.argtypes = []
+        lib.snb_device_status.restype = c_int
+        lib.snb_abi_version.argtypes = []
+        lib.snb_abi_version.restype = c_int
+        _lib = lib
+        return lib
+
+
+def last_error() -> str:
+    msg = load().snb_last_error()
+    return msg.decode() if msg else ""
+
+
+def last_path() -> int:
+    return load().snb_last_path()
+
+
+_ = (c_uint16,)  # bf16 buffers travel as raw 16-bit words

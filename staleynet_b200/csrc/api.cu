@@ -1,0 +1,216 @@
+// api.cu — the extern "C" entry points of include/snb_matmul.h: argument checks in the reference's order
+// (crates/staleynet-cuda/src/ops/matmul.rs:146-149), choice of kernel family, and per-thread error reporting.
+#include <cuda_runtime.h>
+
+#include <mutex>
+#include <string>
+#include <vector>
+
+#include "internal.h"
+
+namespace snb {
+
+namespace {
+
+thread_local std::string t_last_error;
+thread_local int t_last_path = SNB_PATH_NONE;
+
+int fail(int code, const std::string& message) {
+    t_last_error = message;
+    return code;
+}
+
+// Elements an operand must hold: the largest index the batch addresses, plus one. For the reference's
+// RowMajor/Transposed layouts this is `MatmulSpec::required_len` (ops/matmul.rs:138-141):
+// (count-1)*batch_stride + rows*cols.
+uint64_t required_len(uint64_t count, uint64_t batch_stride, uint64_t rows, uint64_t cols, uint64_t row_stride,
+                      uint64_t col_stride) {
+    if (rows == 0 || cols == 0) return 0;
+    return (count - 1) * batch_stride + (rows - 1) * row_stride + (cols - 1) * col_stride + 1;
+}
+
+int run(cudaStream_t stream, const GemmRequest& r, uint64_t left_len, uint64_t right_len, uint64_t output_len) {
+    const snb_product& p = r.p;
+    if (r.count == 0) return fail(SNB_ERR_INVALID_ARGUMENT, "matmul: batch count must be at least 1");
+    if (left_len < required_len(r.count, p.left.batch_stride, p.rows, p.inner, p.left.row_stride, p.left.col_stride))
+        return fail(SNB_ERR_LEFT_TOO_SMALL, "matmul: left operand too small");
+    if (right_len <
+        required_len(r.count, p.right.batch_stride, p.inner, p.cols, p.right.row_stride, p.right.col_stride))
+        return fail(SNB_ERR_RIGHT_TOO_SMALL, "matmul: right operand too small");
+    if (output_len < required_len(r.count, p.output_batch_stride, p.rows, p.cols, p.cols, 1))
+        return fail(SNB_ERR_OUTPUT_TOO_SMALL, "matmul: output too small");
+    if (p.rows == 0 || p.cols == 0) {
+        t_last_path = SNB_PATH_EMPTY;
+        return SNB_OK;
+    }
+    if (r.C == nullptr) return fail(SNB_ERR_INVALID_ARGUMENT, "matmul: output pointer is null");
+    if (p.inner > 0 && (r.A == nullptr || r.B == nullptr))
+        return fail(SNB_ERR_INVALID_ARGUMENT, "matmul: operand pointer is null");
+    if (r.activation == SNB_ACTIVATION_GELU_GRAD && r.gelu_input == nullptr)
+        return fail(SNB_ERR_INVALID_ARGUMENT, "gemm: GELU_GRAD needs gelu_input");
+    if (r.pre != nullptr && r.activation != SNB_ACTIVATION_GELU)
+        return fail(SNB_ERR_INVALID_ARGUMENT, "gemm: pre_activation is only written with GELU");
+    if (r.c_type == SNB_TYPE_BF16 && p.accumulate)
+        return fail(SNB_ERR_UNSUPPORTED, "gemm: accumulating into a bf16 output is not supported");
+
+    std::string err;
+    bool launched = false;
+    int rc = tc_gemm_try(stream, r, &launched, &err);
+    if (rc != SNB_OK) return fail(rc, err);
+    if (launched) {
+        t_last_path = SNB_PATH_TENSOR_CORE;
+        return SNB_OK;
+    }
+    rc = simt_gemm(stream, r, &err);
+    if (rc != SNB_OK) return fail(rc, err);
+    t_last_path = SNB_PATH_SIMT;
+    return SNB_OK;
+}
+
+std::mutex g_info_mu;
+std::vector<DeviceInfo> g_info;
+
+}  // namespace
+
+std::string cuda_message(const char* what, cudaError_t e) {
+    return std::string(what) + ": " + cudaGetErrorName(e) + " (" + cudaGetErrorString(e) + ")";
+}
+
+int current_device_info(DeviceInfo* info, std::string* err) {
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) {
+        *err = cuda_message("cudaGetDevice", e);
+        return SNB_ERR_CUDA;
+    }
+    std::lock_guard<std::mutex> lock(g_info_mu);
+    for (const DeviceInfo& d : g_info) {
+        if (d.device == dev) {
+            *info = d;
+            return SNB_OK;
+        }
+    }
+    DeviceInfo d{dev, 0, 0, 0};
+    if ((e = cudaDeviceGetAttribute(&d.sm_count, cudaDevAttrMultiProcessorCount, dev)) != cudaSuccess ||
+        (e = cudaDeviceGetAttribute(&d.major, cudaDevAttrComputeCapabilityMajor, dev)) != cudaSuccess ||
+        (e = cudaDeviceGetAttribute(&d.minor, cudaDevAttrComputeCapabilityMinor, dev)) != cudaSuccess) {
+        *err = cuda_message("cudaDeviceGetAttribute", e);
+        return SNB_ERR_CUDA;
+    }
+    g_info.push_back(d);
+    *info = d;
+    return SNB_OK;
+}
+
+}  // namespace snb
+
+using namespace snb;
+
+extern "C" {
+
+int snb_abi_version(void) { return 100; }
+
+const char* snb_last_error(void) { return t_last_error.c_str(); }
+
+int snb_last_path(void) { return t_last_path; }
+
+int snb_matmul(void* stream, const snb_product* product, uint64_t count, const float* left, uint64_t left_len,
+               const float* right, uint64_t right_len, float* output, uint64_t output_len, int32_t precision) {
+    t_last_path = SNB_PATH_NONE;
+    if (product == nullptr) return fail(SNB_ERR_INVALID_ARGUMENT, "matmul: product is null");
+    if (precision != SNB_PRECISION_F32 && precision != SNB_PRECISION_TF32)
+        return fail(SNB_ERR_INVALID_ARGUMENT,
+                    "matmul: precision must be SNB_PRECISION_F32 or SNB_PRECISION_TF32 for f32 operands");
+    GemmRequest r{};
+    r.p = *product;
+    r.count = count;
+    r.a_type = r.b_type = r.c_type = SNB_TYPE_F32;
+    r.precision = precision;
+    r.A = left;
+    r.B = right;
+    r.C = output;
+    r.aux_type = SNB_TYPE_F32;
+    return run(static_cast<cudaStream_t>(stream), r, left_len, right_len, output_len);
+}
+
+int snb_matmul_bf16(void* stream, const snb_product* product, uint64_t count, const uint16_t* left,
+                    uint64_t left_len, const uint16_t* right, uint64_t right_len, float* output, uint64_t output_len) {
+    t_last_path = SNB_PATH_NONE;
+    if (product == nullptr) return fail(SNB_ERR_INVALID_ARGUMENT, "matmul: product is null");
+    GemmRequest r{};
+    r.p = *product;
+    r.count = count;
+    r.a_type = r.b_type = SNB_TYPE_BF16;
+    r.c_type = SNB_TYPE_F32;
+    r.precision = SNB_PRECISION_BF16;
+    r.A = left;
+    r.B = right;
+    r.C = output;
+    r.aux_type = SNB_TYPE_F32;
+    return run(static_cast<cudaStream_t>(stream), r, left_len, right_len, output_len);
+}
+
+int snb_gemm(void* stream, const snb_gemm_args* a) {
+    t_last_path = SNB_PATH_NONE;
+    if (a == nullptr) return fail(SNB_ERR_INVALID_ARGUMENT, "gemm: args is null");
+    const bool types_ok = (a->left_type == SNB_TYPE_F32 || a->left_type == SNB_TYPE_BF16) &&
+                          a->right_type == a->left_type &&
+                          (a->output_type == SNB_TYPE_F32 || a->output_type == SNB_TYPE_BF16) &&
+                          (a->aux_type == SNB_TYPE_F32 || a->aux_type == SNB_TYPE_BF16);
+    if (!types_ok) return fail(SNB_ERR_INVALID_ARGUMENT, "gemm: unknown or mismatched element types");
+    const bool prec_ok = a->left_type == SNB_TYPE_BF16
+                             ? a->precision == SNB_PRECISION_BF16
+                             : (a->precision == SNB_PRECISION_F32 || a->precision == SNB_PRECISION_TF32);
+    if (!prec_ok) return fail(SNB_ERR_INVALID_ARGUMENT, "gemm: precision does not match the operand type");
+    if (a->activation < SNB_ACTIVATION_NONE || a->activation > SNB_ACTIVATION_GELU_GRAD)
+        return fail(SNB_ERR_INVALID_ARGUMENT, "gemm: unknown activation");
+    GemmRequest r{};
+    r.p = a->product;
+    r.count = a->count;
+    r.a_type = a->left_type;
+    r.b_type = a->right_type;
+    r.c_type = a->output_type;
+    r.precision = a->precision;
+    r.A = a->left;
+    r.B = a->right;
+    r.C = a->output;
+    r.bias = a->bias;
+    r.activation = a->activation;
+    r.aux_type = a->aux_type;
+    r.pre = a->pre_activation;
+    r.gelu_input = a->gelu_input;
+    r.residual = a->residual;
+    return run(static_cast<cudaStream_t>(stream), r, a->left_len, a->right_len, a->output_len);
+}
+
+int snb_causal_softmax(void* stream, float* scores, uint64_t scores_len, uint64_t rows, uint64_t queries,
+                       uint64_t keys, float scale, uint64_t query_offset) {
+    if (queries == 0 || rows % queries != 0)
+        return fail(SNB_ERR_INVALID_ARGUMENT, "causal_softmax: rows must be a multiple of queries");
+    if (scores_len < rows * keys) return fail(SNB_ERR_OUTPUT_TOO_SMALL, "causal_softmax: scores too small");
+    if (rows > 0 && keys > 0 && scores == nullptr) return fail(SNB_ERR_INVALID_ARGUMENT, "causal_softmax: null scores");
+    if (keys == 0) return SNB_OK;
+    std::string err;
+    int rc = snb::causal_softmax(static_cast<cudaStream_t>(stream), scores, rows, queries, keys, scale, query_offset, &err);
+    return rc == SNB_OK ? rc : fail(rc, err);
+}
+
+int snb_softmax_backward(void* stream, const float* probabilities, float* grad, uint64_t rows, uint64_t cols) {
+    if (rows > 0 && cols > 0 && (probabilities == nullptr || grad == nullptr))
+        return fail(SNB_ERR_INVALID_ARGUMENT, "softmax_backward: null pointer");
+    if (cols == 0) return SNB_OK;
+    std::string err;
+    int rc = snb::softmax_backward(static_cast<cudaStream_t>(stream), probabilities, grad, rows, cols, &err);
+    return rc == SNB_OK ? rc : fail(rc, err);
+}
+
+int snb_device_status(void) {
+    unsigned int status = 0;
+    std::string err;
+    int rc = read_and_clear_device_status(&status, &err);
+    if (rc != SNB_OK) return fail(rc, err);
+    if (status != 0) return fail(SNB_ERR_DEVICE_TIMEOUT, "a tensor-core kernel's bounded wait timed out");
+    return SNB_OK;
+}
+
+}  // extern "C"

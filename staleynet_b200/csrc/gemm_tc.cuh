@@ -1,0 +1,384 @@
+// gemm_tc.cuh — the tensor-core GEMM for sm_100a: C_b = scale * A_b * B_b (+ epilogue) for every matrix of a
+// batch, computing the same product as the reference's `matmul_*` kernels (crates/staleynet-cuda/src/kernels/
+// matmul.rs:216-448) with tcgen05 tensor cores.
+//
+// Structure (one persistent CTA of 256 threads per SM, work units strided over the grid):
+//   warp 0     TMA producer: one elected thread streams 128-byte-wide K slices of A and B into a STAGES-deep
+//              shared-memory ring (128B swizzle), completion tracked by `full` mbarriers.
+//   warp 1     MMA issuer: one elected thread issues tcgen05.mma (M=128, N=BN, K=32 bytes per instruction) into
+//              one of two TMEM accumulators and frees ring slots with tcgen05.commit on `empty` mbarriers.
+//   warp 2     allocates / frees TMEM (2*BN columns).
+//   warps 4-7  epilogue: each warp owns 32 TMEM lanes (= 32 output rows); it loads 32 columns at a time
+//              (tcgen05.ld 32x32b.x32), applies scale / bias / GELU / residual, writes a swizzled 32x128-byte box to
+//              shared memory and stores it with a TMA store, or a TMA reduce-add when accumulating into C. The
+//              second accumulator lets the epilogue of one tile overlap the main loop of the next.
+//
+// Operand layouts: each operand is either K-major (K contiguous) or MN-major (M or N contiguous); both are loaded
+// by TMA in their stored order and described to the tensor core by the major bits of the instruction descriptor,
+// so the four storage combinations of the reference (`Storage::{RowMajor,Transposed}`, ops/matmul.rs:16-33) run
+// without any transposition pass.
+//
+// Split-K: a work unit may cover only part of K; partial sums then always reach C through TMA reduce-add, which
+// adds element-wise in L2 (C must be pre-zeroed by the host for an overwrite).
+#pragma once
+
+#include <cuda.h>
+#include <cuda_bf16.h>
+#include <cstdint>
+
+#include "sm100_ptx.cuh"
+
+namespace snb {
+
+constexpr int TC_BM = 128;
+constexpr int TC_THREADS = 256;
+constexpr int TC_EPI_WARP0 = 4;
+constexpr int TC_EPI_BOX_BYTES = 32 * 128;  // one staged output box: 32 rows x 128 bytes
+
+struct TcParams {
+    int32_t M, N, K;          // rows, cols, inner of each product
+    int32_t count;            // matrices in the batch
+    int32_t a_mn_major;       // 1: A stored with M contiguous; 0: K contiguous
+    int32_t b_mn_major;       // 1: B stored with N contiguous; 0: K contiguous
+    int32_t a_batched;        // 0: one A shared by every matrix (batch stride 0)
+    int32_t b_batched;
+    int32_t m_tiles, n_tiles; // output tiles per matrix
+    int32_t k_blocks;         // 128-byte K slices per product
+    int32_t splits;           // K splits per tile (>= 1)
+    int32_t k_blocks_per_split;
+    int32_t num_units;        // count * m_tiles * n_tiles * splits
+    float scale;
+    int32_t reduce;           // 1: C += result via TMA reduce-add (accumulate or split-K); 0: TMA store
+    int32_t activation;       // SNB_ACTIVATION_*
+    int32_t aux_bf16;         // element type of gelu_input (pre_activation always has the output's type)
+    int32_t has_pre;          // pre-activation store through the second output map
+    const float* bias;        // [N] or nullptr
+    const void* residual;     // laid out like C (type of C) or nullptr
+    const void* gelu_input;   // laid out like C (aux type) or nullptr
+    int64_t out_batch_stride; // elements between output matrices (for residual / gelu_input addressing)
+};
+
+template <int BN>
+struct TcConfig {
+    static constexpr int STAGE_A = TC_BM * 128;
+    static constexpr int STAGE_B = BN * 128;
+    static constexpr int STAGE = STAGE_A + STAGE_B;
+    static constexpr int STAGES = BN == 256 ? 4 : (BN == 128 ? 6 : 8);
+    static constexpr int EPI_BYTES = 4 * 2 * TC_EPI_BOX_BYTES;
+    static constexpr int TMEM_COLS = 2 * BN;
+    static constexpr int BARRIER_BYTES = 256;
+    static constexpr int SMEM_BYTES = 1024 + STAGES * STAGE + EPI_BYTES + BARRIER_BYTES;
+    static_assert(SMEM_BYTES <= 232448, "shared memory budget of one sm_100 CTA");
+    static_assert(TMEM_COLS == 128 || TMEM_COLS == 256 || TMEM_COLS == 512, "TMEM allocation is a power of two");
+};
+
+struct TcUnit {
+    int32_t batch, m0, n0, kb_begin, kb_end, split;
+};
+
+__device__ __forceinline__ TcUnit tc_decode_unit(const TcParams& p, int32_t unit, int BN) {
+    TcUnit u;
+    const int32_t tile = unit / p.splits;
+    u.split = unit - tile * p.splits;
+    const int32_t nt = tile % p.n_tiles;
+    const int32_t rest = tile / p.n_tiles;
+    const int32_t mt = rest % p.m_tiles;
+    u.batch = rest / p.m_tiles;
+    u.m0 = mt * TC_BM;
+    u.n0 = nt * BN;
+    u.kb_begin = u.split * p.k_blocks_per_split;
+    u.kb_end = min(p.k_blocks, u.kb_begin + p.k_blocks_per_split);
+    return u;
+}
+
+__device__ __forceinline__ float gelu_tanh(float x) {
+    // 0.5 x (1 + tanh(sqrt(2/pi) (x + 0.044715 x^3))): the reference's tanh approximation (kernels/elementwise.rs:14-17)
+    const float inner = 0.7978846f * (x + 0.044715f * x * x * x);
+    return 0.5f * x * (1.0f + tanhf(inner));
+}
+
+__device__ __forceinline__ float gelu_tanh_derivative(float x) {
+    // kernels/elementwise.rs:20-24
+    const float t = tanhf(0.7978846f * (x + 0.044715f * x * x * x));
+    return 0.5f * (1.0f + t) + 0.5f * x * (1.0f - t * t) * 0.7978846f * (1.0f + 3.0f * 0.044715f * x * x);
+}
+
+__device__ __forceinline__ float load_elem(const void* base, int64_t index, int is_bf16) {
+    if (is_bf16) {
+        const uint16_t bits = __ldg(reinterpret_cast<const unsigned short*>(base) + index);
+        return __uint_as_float(static_cast<uint32_t>(bits) << 16);
+    }
+    return __ldg(reinterpret_cast<const float*>(base) + index);
+}
+
+__device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
+    __nv_bfloat162 v = __floats2bfloat162_rn(lo, hi);
+    return *reinterpret_cast<uint32_t*>(&v);
+}
+
+// Packs one lane's chunk (32 f32 values, or 64 values as bf16 pairs) into the 32 words of a 128-byte box row.
+template <bool OUT_BF16, int CHUNK>
+__device__ __forceinline__ void pack_chunk(const uint32_t (&x)[CHUNK], uint32_t (&w)[32]) {
+    if constexpr (OUT_BF16) {
+#pragma unroll
+        for (int j = 0; j < 32; ++j) w[j] = pack_bf16x2(__uint_as_float(x[2 * j]), __uint_as_float(x[2 * j + 1]));
+    } else {
+#pragma unroll
+        for (int j = 0; j < 32; ++j) w[j] = x[j];
+    }
+}
+
+// Writes 32 rows x 128 bytes (this lane's row = `lane`) into a 128B-swizzled staging box: 16-byte chunk j of row r
+// goes to chunk position j ^ (r % 8), the layout a SWIZZLE_128B tensor map expects.
+__device__ __forceinline__ void stage_row(uint8_t* box, int lane, const uint32_t (&w)[32]) {
+    uint8_t* row = box + lane * 128;
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+        uint4 v = make_uint4(w[4 * j], w[4 * j + 1], w[4 * j + 2], w[4 * j + 3]);
+        *reinterpret_cast<uint4*>(row + ((j ^ (lane & 7)) << 4)) = v;
+    }
+}
+
+template <typename E, int BN, bool OUT_BF16>
+__global__ void __launch_bounds__(TC_THREADS, 1)
+    tc_gemm_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constant__ CUtensorMap tm_b,
+                   const __grid_constant__ CUtensorMap tm_c, const __grid_constant__ CUtensorMap tm_pre,
+                   const TcParams p) {
+    using Cfg = TcConfig<BN>;
+    constexpr int ESIZE = sizeof(E);
+    constexpr int BK = 128 / ESIZE;      // K elements per ring slot (one 128-byte swizzle row)
+    constexpr int UMMA_K = 32 / ESIZE;   // K elements per tcgen05.mma (32 bytes)
+    constexpr int MN_BOX = 128 / ESIZE;  // M/N elements per 128-byte row of an MN-major box
+    constexpr bool IS_BF16 = ESIZE == 2;
+    constexpr uint32_t FORMAT = IS_BF16 ? 1u : 2u;  // instruction-descriptor A/B format: bf16 = 1, tf32 = 2
+    constexpr int CHUNK = OUT_BF16 ? 64 : 32;       // output columns per staged 128-byte box row
+
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    uint8_t* ring = smem;
+    uint8_t* epi = smem + Cfg::STAGES * Cfg::STAGE;
+    uint64_t* bars = reinterpret_cast<uint64_t*>(epi + Cfg::EPI_BYTES);
+    uint64_t* full = bars;
+    uint64_t* empty = bars + Cfg::STAGES;
+    uint64_t* acc_full = bars + 2 * Cfg::STAGES;
+    uint64_t* acc_empty = acc_full + 2;
+    uint64_t* drain = acc_empty + 2;
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
+
+    const int warp = threadIdx.x >> 5;
+    const int lane = threadIdx.x & 31;
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < Cfg::STAGES; ++s) {
+            mbar_init(smem_addr(&full[s]), 1);
+            mbar_init(smem_addr(&empty[s]), 1);
+        }
+        for (int a = 0; a < 2; ++a) {
+            mbar_init(smem_addr(&acc_full[a]), 1);
+            mbar_init(smem_addr(&acc_empty[a]), 4);  // one arrival per epilogue warp
+        }
+        mbar_init(smem_addr(drain), 1);
+        fence_mbarrier_init();
+        fence_proxy_async_shared();
+    }
+    if (warp == 0 && lane == 0) {
+        tma_prefetch_descriptor(&tm_a);
+        tma_prefetch_descriptor(&tm_b);
+        tma_prefetch_descriptor(&tm_c);
+    }
+    if (warp == 2) {
+        tmem_alloc(smem_addr(tmem_slot), Cfg::TMEM_COLS);
+        tmem_relinquish_alloc_permit();
+    }
+    tcgen05_fence_before_sync();
+    __syncthreads();
+    tcgen05_fence_after_sync();
+    const uint32_t tmem_base = *tmem_slot;
+
+    if (warp == 0) {
+        // ------------------------------------------------------------------ TMA producer
+        if (elect_one()) {
+            int stage = 0;
+            uint32_t phase = 0;
+            bool ok = true;
+            for (int32_t unit = blockIdx.x; unit < p.num_units && ok; unit += gridDim.x) {
+                const TcUnit u = tc_decode_unit(p, unit, BN);
+                const int32_t ba = p.a_batched ? u.batch : 0;
+                const int32_t bb = p.b_batched ? u.batch : 0;
+                for (int32_t kb = u.kb_begin; kb < u.kb_end; ++kb) {
+                    const uint32_t fb = smem_addr(&full[stage]);
+                    if (!mbar_wait(smem_addr(&empty[stage]), phase ^ 1u)) { ok = false; break; }
+                    mbar_arrive_expect_tx(fb, Cfg::STAGE);
+                    const uint32_t sa = smem_addr(ring + stage * Cfg::STAGE);
+                    const uint32_t sb = sa + Cfg::STAGE_A;
+                    const int32_t k0 = kb * BK;
+                    if (!p.a_mn_major) {
+                        tma_load_3d(sa, &tm_a, fb, k0, u.m0, ba);
+                    } else {
+#pragma unroll
+                        for (int j = 0; j < TC_BM / MN_BOX; ++j)
+                            tma_load_3d(sa + j * (BK * 128), &tm_a, fb, u.m0 + j * MN_BOX, k0, ba);
+                    }
+                    if (!p.b_mn_major) {
+                        tma_load_3d(sb, &tm_b, fb, k0, u.n0, bb);
+                    } else {
+#pragma unroll
+                        for (int j = 0; j < BN / MN_BOX; ++j)
+                            tma_load_3d(sb + j * (BK * 128), &tm_b, fb, u.n0 + j * MN_BOX, k0, bb);
+                    }
+                    if (++stage == Cfg::STAGES) { stage = 0; phase ^= 1u; }
+                }
+            }
+        }
+        __syncwarp();
+    } else if (warp == 1) {
+        // ------------------------------------------------------------------ MMA issuer
+        if (elect_one()) {
+            const uint32_t idesc = make_instr_desc(FORMAT, p.a_mn_major, p.b_mn_major, TC_BM, BN);
+            // Byte offsets of the canonical 128B-swizzled layouts: K-major rows are 128 bytes apart and groups of
+            // 8 rows 1024 bytes apart (SBO); MN-major slices have 128-byte K rows, 8-row groups 1024 bytes apart
+            // (SBO) and successive 128-byte MN chunks one box (BK rows) apart (LBO).
+            const uint32_t a_lbo = p.a_mn_major ? BK * 128 : 16;
+            const uint32_t b_lbo = p.b_mn_major ? BK * 128 : 16;
+            const uint32_t a_kstep = p.a_mn_major ? UMMA_K * 128 : 32;
+            const uint32_t b_kstep = p.b_mn_major ? UMMA_K * 128 : 32;
+            int stage = 0;
+            uint32_t phase = 0;
+            int iter = 0;
+            bool ok = true;
+            bool issued = false;
+            for (int32_t unit = blockIdx.x; unit < p.num_units && ok; unit += gridDim.x, ++iter) {
+                const TcUnit u = tc_decode_unit(p, unit, BN);
+                const int acc = iter & 1;
+                const uint32_t acc_phase = (iter >> 1) & 1;
+                if (!mbar_wait(smem_addr(&acc_empty[acc]), acc_phase ^ 1u)) { ok = false; break; }
+                tcgen05_fence_after_sync();
+                const uint32_t d_tmem = tmem_base + acc * BN;
+                for (int32_t kb = u.kb_begin; kb < u.kb_end; ++kb) {
+                    if (!mbar_wait(smem_addr(&full[stage]), phase)) { ok = false; break; }
+                    tcgen05_fence_after_sync();
+                    const uint32_t sa = smem_addr(ring + stage * Cfg::STAGE);
+                    const uint32_t sb = sa + Cfg::STAGE_A;
+#pragma unroll
+                    for (int k = 0; k < BK / UMMA_K; ++k) {
+                        const uint64_t ad = make_smem_desc(sa + k * a_kstep, a_lbo, 1024);
+                        const uint64_t bd = make_smem_desc(sb + k * b_kstep, b_lbo, 1024);
+                        const uint32_t accumulate = (kb > u.kb_begin || k > 0) ? 1u : 0u;
+                        if (IS_BF16) umma_bf16(d_tmem, ad, bd, idesc, accumulate);
+                        else umma_tf32(d_tmem, ad, bd, idesc, accumulate);
+                    }
+                    issued = true;
+                    umma_commit(smem_addr(&empty[stage]));
+                    if (++stage == Cfg::STAGES) { stage = 0; phase ^= 1u; }
+                }
+                if (!ok) break;
+                umma_commit(smem_addr(&acc_full[acc]));
+            }
+            if (!ok && issued) {
+                // Let every MMA already issued finish before TMEM is released.
+                umma_commit(smem_addr(drain));
+                mbar_wait(smem_addr(drain), 0);
+            }
+        }
+        __syncwarp();
+    } else if (warp >= TC_EPI_WARP0) {
+        // ------------------------------------------------------------------ epilogue
+        const int q = warp - TC_EPI_WARP0;  // TMEM lane quadrant = warp % 4
+        uint8_t* boxes = epi + q * 2 * TC_EPI_BOX_BYTES;
+        int ebuf = 0;
+        int iter = 0;
+        for (int32_t unit = blockIdx.x; unit < p.num_units; unit += gridDim.x, ++iter) {
+            const TcUnit u = tc_decode_unit(p, unit, BN);
+            const int acc = iter & 1;
+            const uint32_t acc_phase = (iter >> 1) & 1;
+            if (!mbar_wait(smem_addr(&acc_full[acc]), acc_phase)) break;
+            tcgen05_fence_after_sync();
+            const int32_t row0 = u.m0 + q * 32;
+            const int32_t row = row0 + lane;
+            const bool first_split = u.split == 0;
+            const int64_t out_base =
+                static_cast<int64_t>(u.batch) * p.out_batch_stride + static_cast<int64_t>(row) * p.N;
+            const uint32_t t_lane = tmem_base + (static_cast<uint32_t>(q * 32) << 16) + acc * BN;
+
+            for (int c = 0; c < BN && row0 < p.M && u.n0 + c < p.N; c += CHUNK) {
+                uint32_t x[CHUNK];
+                tmem_load_32x32b_x32(t_lane + c, *reinterpret_cast<uint32_t(*)[32]>(&x[0]));
+                if constexpr (CHUNK == 64)
+                    tmem_load_32x32b_x32(t_lane + c + 32, *reinterpret_cast<uint32_t(*)[32]>(&x[32]));
+                tmem_load_wait();
+
+                const int32_t col0 = u.n0 + c;
+                const bool row_live = row < p.M;
+                // x = scale * acc + bias
+#pragma unroll
+                for (int i = 0; i < CHUNK; ++i) {
+                    float f = p.scale * __uint_as_float(x[i]);
+                    if (p.bias != nullptr && first_split && col0 + i < p.N) f += __ldg(p.bias + col0 + i);
+                    x[i] = __float_as_uint(f);
+                }
+                // Optional pre-activation output (the GELU forward keeps x for the backward pass); same type as C.
+                if (p.has_pre) {
+                    uint32_t w[32];
+                    pack_chunk<OUT_BF16, CHUNK>(x, w);
+                    uint8_t* box = boxes + ebuf * TC_EPI_BOX_BYTES;
+                    if (lane == 0) bulk_wait_group_read<1>();
+                    __syncwarp();
+                    stage_row(box, lane, w);
+                    fence_proxy_async_shared();
+                    __syncwarp();
+                    if (lane == 0) {
+                        tma_store_3d(&tm_pre, smem_addr(box), col0, row0, u.batch);
+                        bulk_commit_group();
+                    }
+                    ebuf ^= 1;
+                }
+                if (p.activation == 1) {
+#pragma unroll
+                    for (int i = 0; i < CHUNK; ++i) x[i] = __float_as_uint(gelu_tanh(__uint_as_float(x[i])));
+                } else if (p.activation == 2) {
+#pragma unroll
+                    for (int i = 0; i < CHUNK; ++i) {
+                        const bool live = row_live && col0 + i < p.N;
+                        const float g = live ? load_elem(p.gelu_input, out_base + col0 + i, p.aux_bf16) : 0.0f;
+                        x[i] = __float_as_uint(__uint_as_float(x[i]) * gelu_tanh_derivative(g));
+                    }
+                }
+                if (p.residual != nullptr && first_split) {
+#pragma unroll
+                    for (int i = 0; i < CHUNK; ++i) {
+                        const bool live = row_live && col0 + i < p.N;
+                        if (live) x[i] = __float_as_uint(__uint_as_float(x[i]) + load_elem(p.residual, out_base + col0 + i, OUT_BF16));
+                    }
+                }
+                uint32_t w[32];
+                pack_chunk<OUT_BF16, CHUNK>(x, w);
+                uint8_t* box = boxes + ebuf * TC_EPI_BOX_BYTES;
+                if (lane == 0) bulk_wait_group_read<1>();
+                __syncwarp();
+                stage_row(box, lane, w);
+                fence_proxy_async_shared();
+                __syncwarp();
+                if (lane == 0) {
+                    if (p.reduce) tma_reduce_add_3d(&tm_c, smem_addr(box), col0, row0, u.batch);
+                    else tma_store_3d(&tm_c, smem_addr(box), col0, row0, u.batch);
+                    bulk_commit_group();
+                }
+                ebuf ^= 1;
+            }
+            tcgen05_fence_before_sync();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(smem_addr(&acc_empty[acc]));
+        }
+        if (lane == 0) bulk_wait_group<0>();
+        __syncwarp();
+    }
+
+    tcgen05_fence_before_sync();
+    __syncthreads();
+    if (warp == 2) {
+        tcgen05_fence_after_sync();
+        tmem_dealloc(tmem_base, Cfg::TMEM_COLS);
+    }
+}
+
+}  // namespace snb

@@ -1,0 +1,55 @@
+// internal.h — declarations shared by the library's translation units (not part of the C ABI).
+#pragma once
+
+#include <cuda_runtime.h>
+#include <cstdint>
+#include <string>
+
+#include "../../include/snb_matmul.h"
+
+namespace snb {
+
+// One product with its epilogue, after argument validation; element types are SNB_TYPE_*.
+struct GemmRequest {
+    snb_product p;
+    uint64_t count;
+    int a_type, b_type, c_type;
+    int precision;
+    const void* A;
+    const void* B;
+    void* C;
+    const float* bias;
+    int activation;
+    int aux_type;
+    void* pre;
+    const void* gelu_input;
+    const void* residual;
+};
+
+struct DeviceInfo {
+    int device;
+    int sm_count;
+    int major, minor;
+};
+
+// Properties of the current device (cached per device).
+int current_device_info(DeviceInfo* info, std::string* err);
+
+// Runs the product on the tcgen05 kernel if its layout allows TMA (unit strides, 16-byte alignment);
+// *launched says whether it did. Returns SNB_OK or an error code (with *err set).
+int tc_gemm_try(cudaStream_t stream, const GemmRequest& r, bool* launched, std::string* err);
+
+// Runs the product on the strided SIMT kernel (any layout).
+int simt_gemm(cudaStream_t stream, const GemmRequest& r, std::string* err);
+
+int causal_softmax(cudaStream_t stream, float* scores, uint64_t rows, uint64_t queries, uint64_t keys, float scale,
+                   uint64_t query_offset, std::string* err);
+int softmax_backward(cudaStream_t stream, const float* probabilities, float* grad, uint64_t rows, uint64_t cols,
+                     std::string* err);
+
+// Reads and clears the tensor-core kernels' device status word on the current device (synchronizes first).
+int read_and_clear_device_status(unsigned int* status, std::string* err);
+
+std::string cuda_message(const char* what, cudaError_t e);
+
+}  // namespace snb

@@ -1,0 +1,311 @@
+// tc_gemm.cu — host side of the tcgen05 GEMM: eligibility (TMA needs a unit stride and 16-byte aligned strides),
+// tensor-map encoding, tile-width and split-K choice, and the launch.
+#include <cuda.h>
+#include <cuda_runtime.h>
+
+#include <algorithm>
+#include <mutex>
+
+#include "gemm_tc.cuh"
+#include "internal.h"
+
+namespace snb {
+
+namespace {
+
+using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                   const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                   CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+EncodeTiledFn encode_fn() {
+    static EncodeTiledFn fn = nullptr;
+    static std::once_flag once;
+    std::call_once(once, [] {
+        void* p = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn = reinterpret_cast<EncodeTiledFn>(p);
+    });
+    return fn;
+}
+
+// How one operand is read: `mn_major` = the M (or N) index is contiguous; `ld` = elements between consecutive
+// rows of the other index; `batched` = distinct matrix per batch entry.
+struct OperandLayout {
+    bool ok;
+    bool mn_major;
+    uint64_t ld;
+    bool batched;
+};
+
+// Decides the layout of an operand with logical extents (mn, k): element (i, kk) at
+// b*batch + i*mn_stride + kk*k_stride.
+OperandLayout classify(uint64_t mn, uint64_t k, uint64_t mn_stride, uint64_t k_stride, uint64_t batch_stride,
+                       uint64_t count, int esize, const void* base) {
+    OperandLayout L{false, false, 0, false};
+    if (reinterpret_cast<uintptr_t>(base) % 16 != 0) return L;
+    // The contiguous dimension must have more than one element; with a single row the other stride is never
+    // used for addressing, so it is replaced by the row length.
+    if (k > 1 && k_stride == 1) {
+        L.mn_major = false;
+        L.ld = (mn == 1) ? k : mn_stride;
+        if (L.ld < k) return L;
+    } else if (mn > 1 && mn_stride == 1) {
+        L.mn_major = true;
+        L.ld = (k == 1) ? mn : k_stride;
+        if (L.ld < mn) return L;
+    } else {
+        return L;  // no unit stride (or a 1x1 matrix): the SIMT kernel handles it
+    }
+    const uint64_t outer = L.mn_major ? k : mn;
+    if (outer == 1) L.ld = ((L.ld * esize + 15) / 16) * 16 / esize;  // pad the unused stride to 16 bytes
+    if ((L.ld * esize) % 16 != 0) return L;
+    L.batched = count > 1 && batch_stride != 0;
+    if (L.batched) {
+        if ((batch_stride * esize) % 16 != 0) return L;
+        if (batch_stride < L.ld * outer) return L;
+    }
+    L.ok = true;
+    return L;
+}
+
+bool encode_3d(CUtensorMap* map, CUtensorMapDataType dt, int esize, const void* base, uint64_t d0, uint64_t d1,
+               uint64_t d2, uint64_t stride1_elems, uint64_t stride2_elems, uint32_t box0, uint32_t box1,
+               std::string* err) {
+    EncodeTiledFn fn = encode_fn();
+    if (!fn) {
+        *err = "cuTensorMapEncodeTiled is not available from the CUDA driver";
+        return false;
+    }
+    cuuint64_t dims[3] = {d0, d1, d2};
+    cuuint64_t strides[2] = {stride1_elems * esize, stride2_elems * esize};
+    cuuint32_t box[3] = {box0, box1, 1};
+    cuuint32_t estr[3] = {1, 1, 1};
+    CUresult r = fn(map, dt, 3, const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                    CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) {
+        *err = "cuTensorMapEncodeTiled failed with CUresult " + std::to_string(static_cast<int>(r));
+        return false;
+    }
+    return true;
+}
+
+template <typename E, int BN, bool OUT_BF16>
+int launch(cudaStream_t stream, const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& tc,
+           const CUtensorMap& tp, const TcParams& p, int grid, std::string* err) {
+    constexpr int smem = TcConfig<BN>::SMEM_BYTES;
+    static int configured_device = -1;
+    static std::mutex mu;
+    int dev = 0;
+    cudaGetDevice(&dev);
+    {
+        std::lock_guard<std::mutex> lock(mu);
+        // cudaFuncSetAttribute is per device; redo it when the current device changes.
+        if (configured_device != dev) {
+            cudaError_t e = cudaFuncSetAttribute(tc_gemm_kernel<E, BN, OUT_BF16>,
+                                                 cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+            if (e != cudaSuccess) {
+                *err = cuda_message("cudaFuncSetAttribute(tc_gemm_kernel)", e);
+                return SNB_ERR_CUDA;
+            }
+            configured_device = dev;
+        }
+    }
+    tc_gemm_kernel<E, BN, OUT_BF16><<<grid, TC_THREADS, smem, stream>>>(ta, tb, tc, tp, p);
+    cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess) {
+        *err = cuda_message("tc_gemm_kernel launch", e);
+        return SNB_ERR_CUDA;
+    }
+    return SNB_OK;
+}
+
+template <typename E, bool OUT_BF16>
+int launch_bn(int bn, cudaStream_t s, const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& tc,
+              const CUtensorMap& tp, const TcParams& p, int grid, std::string* err) {
+    switch (bn) {
+        case 64: return launch<E, 64, OUT_BF16>(s, ta, tb, tc, tp, p, grid, err);
+        case 128: return launch<E, 128, OUT_BF16>(s, ta, tb, tc, tp, p, grid, err);
+        default: return launch<E, 256, OUT_BF16>(s, ta, tb, tc, tp, p, grid, err);
+    }
+}
+
+// K splits for a problem of `tiles` output tiles and `kb` K slices on `sms` SMs: minimises
+// ceil(tiles*s/sms) * ceil(kb/s), keeping at least 4 K slices per split.
+int choose_splits(int64_t tiles, int64_t kb, int sms) {
+    if (tiles >= sms || kb < 8) return 1;
+    int best = 1;
+    int64_t best_cost = ((tiles + sms - 1) / sms) * kb;
+    for (int s = 2; s <= 32; ++s) {
+        const int64_t per = (kb + s - 1) / s;
+        if (per < 4) break;
+        const int64_t cost = ((tiles * s + sms - 1) / sms) * per;
+        if (cost < best_cost) {
+            best_cost = cost;
+            best = s;
+        }
+    }
+    return best;
+}
+
+}  // namespace
+
+int tc_gemm_try(cudaStream_t stream, const GemmRequest& r, bool* launched, std::string* err) {
+    *launched = false;
+    const snb_product& p = r.p;
+    if (p.inner == 0 || p.rows == 0 || p.cols == 0) return SNB_OK;
+    if (r.precision != SNB_PRECISION_TF32 && r.precision != SNB_PRECISION_BF16) return SNB_OK;
+    const bool bf16_in = r.a_type == SNB_TYPE_BF16;
+    if (bf16_in != (r.precision == SNB_PRECISION_BF16)) return SNB_OK;
+    const bool out_bf16 = r.c_type == SNB_TYPE_BF16;
+    if (!bf16_in && out_bf16) return SNB_OK;  // f32 operands run with an f32 output only
+    // 32-bit tile coordinates.
+    const uint64_t lim = (1ull << 31) - 256;
+    if (p.rows > lim || p.cols > lim || p.inner > lim || r.count > lim) return SNB_OK;
+
+    DeviceInfo dev;
+    int rc = current_device_info(&dev, err);
+    if (rc != SNB_OK) return rc;
+    if (dev.major != 10) return SNB_OK;  // the tcgen05 kernels are built for sm_100a only
+
+    const int esize = bf16_in ? 2 : 4;
+    const OperandLayout la = classify(p.rows, p.inner, p.left.row_stride, p.left.col_stride, p.left.batch_stride,
+                                      r.count, esize, r.A);
+    const OperandLayout lb = classify(p.cols, p.inner, p.right.col_stride, p.right.row_stride, p.right.batch_stride,
+                                      r.count, esize, r.B);
+    if (!la.ok || !lb.ok) return SNB_OK;
+
+    // Output (and every tensor laid out like it): row-major [rows, cols] with rows `cols` apart.
+    const int csize = out_bf16 ? 2 : 4;
+    if ((p.cols * csize) % 16 != 0) return SNB_OK;
+    if (reinterpret_cast<uintptr_t>(r.C) % 16 != 0) return SNB_OK;
+    if (r.pre && reinterpret_cast<uintptr_t>(r.pre) % 16 != 0) return SNB_OK;
+    if (r.pre && r.aux_type != r.c_type) return SNB_OK;
+    const bool c_batched = r.count > 1;
+    if (c_batched && ((p.output_batch_stride * csize) % 16 != 0 || p.output_batch_stride < p.rows * p.cols))
+        return SNB_OK;
+
+    const int bn = p.cols <= 64 ? 64 : (p.cols <= 128 ? 128 : 256);
+    const int bk = 128 / esize;
+    const int64_t m_tiles = (p.rows + TC_BM - 1) / TC_BM;
+    const int64_t n_tiles = (p.cols + bn - 1) / bn;
+    const int64_t k_blocks = (p.inner + bk - 1) / bk;
+    const int64_t tiles = static_cast<int64_t>(r.count) * m_tiles * n_tiles;
+    if (tiles > (1ll << 30)) return SNB_OK;
+    const bool plain_epilogue = !out_bf16 && r.activation == SNB_ACTIVATION_NONE && r.pre == nullptr;
+    const int splits = plain_epilogue ? choose_splits(tiles, k_blocks, dev.sm_count) : 1;
+    const int64_t kb_per_split = (k_blocks + splits - 1) / splits;
+    const int64_t splits_used = (k_blocks + kb_per_split - 1) / kb_per_split;  // every split has >= 1 slice
+
+    CUtensorMap ta, tb, tc, tp;
+    const CUtensorMapDataType in_dt = bf16_in ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_TFLOAT32;
+    const uint32_t mn_box = 128 / esize;
+    // A: (mn = rows, k = inner)
+    if (la.mn_major) {
+        if (!encode_3d(&ta, in_dt, esize, r.A, p.rows, p.inner, la.batched ? r.count : 1, la.ld,
+                       la.batched ? p.left.batch_stride : la.ld * p.inner, mn_box, bk, err))
+            return SNB_OK;
+    } else {
+        if (!encode_3d(&ta, in_dt, esize, r.A, p.inner, p.rows, la.batched ? r.count : 1, la.ld,
+                       la.batched ? p.left.batch_stride : la.ld * p.rows, bk, TC_BM, err))
+            return SNB_OK;
+    }
+    // B: (mn = cols, k = inner)
+    if (lb.mn_major) {
+        if (!encode_3d(&tb, in_dt, esize, r.B, p.cols, p.inner, lb.batched ? r.count : 1, lb.ld,
+                       lb.batched ? p.right.batch_stride : lb.ld * p.inner, mn_box, bk, err))
+            return SNB_OK;
+    } else {
+        if (!encode_3d(&tb, in_dt, esize, r.B, p.inner, p.cols, lb.batched ? r.count : 1, lb.ld,
+                       lb.batched ? p.right.batch_stride : lb.ld * p.cols, bk, static_cast<uint32_t>(bn), err))
+            return SNB_OK;
+    }
+    const CUtensorMapDataType out_dt = out_bf16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT32;
+    const uint32_t chunk = out_bf16 ? 64 : 32;
+    const uint64_t c_bstride = c_batched ? p.output_batch_stride : p.rows * p.cols;
+    if (!encode_3d(&tc, out_dt, csize, r.C, p.cols, p.rows, c_batched ? r.count : 1, p.cols, c_bstride, chunk, 32,
+                   err))
+        return SNB_OK;
+    if (r.pre) {
+        if (!encode_3d(&tp, out_dt, csize, r.pre, p.cols, p.rows, c_batched ? r.count : 1, p.cols, c_bstride, chunk,
+                       32, err))
+            return SNB_OK;
+    } else {
+        tp = tc;
+    }
+
+    // An overwrite computed in several K splits reaches C by reduce-add, so C starts at zero.
+    const bool reduce = p.accumulate != 0 || splits_used > 1;
+    if (p.accumulate == 0 && splits_used > 1) {
+        cudaError_t e;
+        if (!c_batched || p.output_batch_stride == p.rows * p.cols) {
+            e = cudaMemsetAsync(r.C, 0, r.count * p.rows * p.cols * csize, stream);
+        } else {
+            e = cudaMemset2DAsync(r.C, p.output_batch_stride * csize, 0, p.rows * p.cols * csize, r.count, stream);
+        }
+        if (e != cudaSuccess) {
+            *err = cuda_message("zeroing the split-K output", e);
+            return SNB_ERR_CUDA;
+        }
+    }
+
+    TcParams kp{};
+    kp.M = static_cast<int32_t>(p.rows);
+    kp.N = static_cast<int32_t>(p.cols);
+    kp.K = static_cast<int32_t>(p.inner);
+    kp.count = static_cast<int32_t>(r.count);
+    kp.a_mn_major = la.mn_major;
+    kp.b_mn_major = lb.mn_major;
+    kp.a_batched = la.batched;
+    kp.b_batched = lb.batched;
+    kp.m_tiles = static_cast<int32_t>(m_tiles);
+    kp.n_tiles = static_cast<int32_t>(n_tiles);
+    kp.k_blocks = static_cast<int32_t>(k_blocks);
+    kp.splits = static_cast<int32_t>(splits_used);
+    kp.k_blocks_per_split = static_cast<int32_t>(kb_per_split);
+    const int64_t units = tiles * splits_used;
+    if (units > (1ll << 31) - 1) return SNB_OK;
+    kp.num_units = static_cast<int32_t>(units);
+    kp.scale = p.scale;
+    kp.reduce = reduce;
+    kp.activation = r.activation;
+    kp.aux_bf16 = r.aux_type == SNB_TYPE_BF16;
+    kp.has_pre = r.pre != nullptr;
+    kp.bias = r.bias;
+    kp.residual = r.residual;
+    kp.gelu_input = r.gelu_input;
+    kp.out_batch_stride = static_cast<int64_t>(c_batched ? p.output_batch_stride : 0);
+
+    const int grid = static_cast<int>(std::min<int64_t>(units, dev.sm_count));
+    if (bf16_in) {
+        rc = out_bf16 ? launch_bn<__nv_bfloat16, true>(bn, stream, ta, tb, tc, tp, kp, grid, err)
+                      : launch_bn<__nv_bfloat16, false>(bn, stream, ta, tb, tc, tp, kp, grid, err);
+    } else {
+        rc = launch_bn<float, false>(bn, stream, ta, tb, tc, tp, kp, grid, err);
+    }
+    if (rc == SNB_OK) *launched = true;
+    return rc;
+}
+
+int read_and_clear_device_status(unsigned int* status, std::string* err) {
+    cudaError_t e = cudaDeviceSynchronize();
+    if (e != cudaSuccess) {
+        *err = cuda_message("cudaDeviceSynchronize", e);
+        return SNB_ERR_CUDA;
+    }
+    e = cudaMemcpyFromSymbol(status, g_device_status, sizeof(unsigned int));
+    if (e != cudaSuccess) {
+        *err = cuda_message("reading the device status", e);
+        return SNB_ERR_CUDA;
+    }
+    const unsigned int zero = 0;
+    e = cudaMemcpyToSymbol(g_device_status, &zero, sizeof(unsigned int));
+    if (e != cudaSuccess) {
+        *err = cuda_message("clearing the device status", e);
+        return SNB_ERR_CUDA;
+    }
+    return SNB_OK;
+}
+
+}  // namespace snb

@@ -1,0 +1,251 @@
+"""Host-side mirror of the reference's GEMM operator API (crates/staleynet-cuda/src/ops/matmul.rs, ops/mod.rs,
+device.rs), bound to the sm_100a library through the C ABI.
+
+Names, fields and error behaviour follow the reference so callers and tests read like the reference's own:
+`Storage`, `BatchStrides`, `MatmulSpec` with its builders, `WriteMode`, `MatmulKernel` with `tolerance()`, and
+`Gpu.matmul(spec, left, right, output)`. Tensors are torch CUDA tensors (torch is the device-memory plumbing here);
+every product runs in libsnb_b200.so.
+"""
+from __future__ import annotations
+
+import ctypes
+import enum
+from dataclasses import dataclass, replace
+
+from . import _ffi
+
+
+class WriteMode(enum.Enum):
+    """Overwrite or accumulate into the output (ops/mod.rs:27-45)."""
+
+    OVERWRITE = 0
+    ACCUMULATE = 1
+
+    def flag(self) -> int:
+        return self.value
+
+
+class Storage(enum.Enum):
+    """How an operand is laid out relative to the logical matrix op(X) (ops/matmul.rs:14-33)."""
+
+    ROW_MAJOR = 0
+    TRANSPOSED = 1
+
+    def operand(self, rows: int, cols: int, batch_stride: int) -> _ffi.Operand:
+        if self is Storage.ROW_MAJOR:
+            return _ffi.Operand(row_stride=cols, col_stride=1, batch_stride=batch_stride)
+        return _ffi.Operand(row_stride=1, col_stride=rows, batch_stride=batch_stride)
+
+
+@dataclass(frozen=True)
+class BatchStrides:
+    """Element offsets between consecutive matrices of a batch (ops/matmul.rs:35-54)."""
+
+    count: int
+    left: int
+    right: int
+    output: int
+
+
+BatchStrides.SINGLE = BatchStrides(count=1, left=0, right=0, output=0)
+
+
+@dataclass(frozen=True)
+class MatmulSpec:
+    """Full description of one (batched) GEMM (ops/matmul.rs:56-142)."""
+
+    rows: int
+    cols: int
+    inner: int
+    left: Storage = Storage.ROW_MAJOR
+    right: Storage = Storage.ROW_MAJOR
+    batch: BatchStrides = BatchStrides.SINGLE
+    scale: float = 1.0
+    write: WriteMode = WriteMode.OVERWRITE
+
+    @staticmethod
+    def new(rows: int, cols: int, inner: int) -> "MatmulSpec":
+        return MatmulSpec(rows, cols, inner)
+
+    def left_transposed(self) -> "MatmulSpec":
+        return replace(self, left=Storage.TRANSPOSED)
+
+    def right_transposed(self) -> "MatmulSpec":
+        return replace(self, right=Storage.TRANSPOSED)
+
+    def accumulate(self) -> "MatmulSpec":
+        return replace(self, write=WriteMode.ACCUMULATE)
+
+    def scaled(self, scale: float) -> "MatmulSpec":
+        return replace(self, scale=scale)
+
+    def batched(self, strides: BatchStrides) -> "MatmulSpec":
+        return replace(self, batch=strides)
+
+    def product(self) -> _ffi.Product:
+        """The kernel-level description (`MatmulSpec::product`, ops/matmul.rs:124-136)."""
+        return _ffi.Product(
+            rows=self.rows,
+            cols=self.cols,
+            inner=self.inner,
+            left=self.left.operand(self.rows, self.inner, self.batch.left),
+            right=self.right.operand(self.inner, self.cols, self.batch.right),
+            output_batch_stride=self.batch.output,
+            scale=self.scale,
+            accumulate=self.write.flag(),
+        )
+
+    def required_len(self, stride: int, per_matrix: int) -> int:
+        """Elements an operand of `per_matrix` elements must hold (ops/matmul.rs:138-141)."""
+        return (self.batch.count - 1) * stride + per_matrix
+
+
+class MatmulKernel(enum.Enum):
+    """Arithmetic of `Gpu.matmul` (device.rs:38-67). The reference's four f32 kernels become two precisions of
+    one sm_100a implementation; BF16_TENSOR_CORE is new and needs bf16 operands."""
+
+    NAIVE = "naive"
+    TILED = "tiled"
+    BLOCKED = "blocked"
+    TENSOR_CORE = "tensor_core"
+    BF16_TENSOR_CORE = "bf16_tensor_core"
+
+    def precision(self) -> int:
+        if self is MatmulKernel.TENSOR_CORE:
+            return _ffi.PRECISION_TF32
+        if self is MatmulKernel.BF16_TENSOR_CORE:
+            return _ffi.PRECISION_BF16
+        return _ffi.PRECISION_F32
+
+    def tolerance(self) -> float:
+        """Largest max|delta|/max|expected| against an exact f32 product (device.rs:57-66); bf16 keeps 8
+        mantissa bits, so its bound is the 1e-2 stated for bf16 in the build's north star."""
+        if self is MatmulKernel.TENSOR_CORE:
+            return 2e-3
+        if self is MatmulKernel.BF16_TENSOR_CORE:
+            return 1e-2
+        return 1e-5
+
+
+class SnbError(RuntimeError):
+    """A failed library call: `code` is the SNB_ERR_* status, the message is snb_last_error()."""
+
+    def __init__(self, code: int, message: str):
+        super().__init__(f"{message} (status {code})")
+        self.code = code
+
+
+class OperandTooSmall(SnbError, AssertionError):
+    """The reference's `assert!` panics on undersized operands (ops/matmul.rs:147-149)."""
+
+
+def check(code: int) -> None:
+    if code == _ffi.OK:
+        return
+    msg = _ffi.last_error()
+    if code in (_ffi.ERR_LEFT_TOO_SMALL, _ffi.ERR_RIGHT_TOO_SMALL, _ffi.ERR_OUTPUT_TOO_SMALL):
+        raise OperandTooSmall(code, msg)
+    raise SnbError(code, msg)
+
+
+def _ptr(t) -> int:
+    return int(t.data_ptr()) if t is not None else 0
+
+
+def _require_cuda(*tensors) -> None:
+    for t in tensors:
+        if t is not None and not t.is_cuda:
+            raise SnbError(_ffi.ERR_INVALID_ARGUMENT, "tensors must live in CUDA device memory")
+
+
+class Gpu:
+    """One device and one stream, like the reference's `Gpu` (device.rs:129-208). `matmul_kernel` selects the
+    arithmetic (the reference's `--matmul` switch)."""
+
+    def __init__(self, device: int = 0, stream=None):
+        import torch
+
+        self.device = torch.device("cuda", device)
+        self.stream = stream if stream is not None else torch.cuda.current_stream(self.device)
+        self.matmul_kernel = MatmulKernel.BLOCKED
+        self.lib = _ffi.load()
+
+    def _stream_handle(self):
+        return ctypes.c_void_p(self.stream.cuda_stream)
+
+    def matmul(self, spec: MatmulSpec, left, right, output) -> None:
+        """`Gpu::matmul` (ops/matmul.rs:146-171): output[b] = scale*op(left[b])*op(right[b]) (+ output[b])."""
+        import torch
+
+        _require_cuda(left, right, output)
+        product = spec.product()
+        if self.matmul_kernel is MatmulKernel.BF16_TENSOR_CORE:
+            if left.dtype != torch.bfloat16 or right.dtype != torch.bfloat16 or output.dtype != torch.float32:
+                raise SnbError(_ffi.ERR_INVALID_ARGUMENT, "bf16 matmul takes bf16 operands and an f32 output")
+            code = self.lib.snb_matmul_bf16(self._stream_handle(), ctypes.byref(product), spec.batch.count,
+                                            _ptr(left), left.numel(), _ptr(right), right.numel(), _ptr(output),
+                                            output.numel())
+        else:
+            if left.dtype != torch.float32 or right.dtype != torch.float32 or output.dtype != torch.float32:
+                raise SnbError(_ffi.ERR_INVALID_ARGUMENT, "f32 matmul takes f32 tensors")
+            code = self.lib.snb_matmul(self._stream_handle(), ctypes.byref(product), spec.batch.count, _ptr(left),
+                                       left.numel(), _ptr(right), right.numel(), _ptr(output), output.numel(),
+                                       self.matmul_kernel.precision())
+        check(code)
+
+    def gemm(self, spec: MatmulSpec, left, right, output, *, bias=None, activation: int = _ffi.ACTIVATION_NONE,
+             pre_activation=None, gelu_input=None, residual=None) -> None:
+        """`Gpu.matmul` with the caller's elementwise follow-up fused into the epilogue (snb_gemm)."""
+        import torch
+
+        _require_cuda(left, right, output, bias, pre_activation, gelu_input, residual)
+        bf16 = left.dtype == torch.bfloat16
+        args = _ffi.GemmArgs()
+        args.product = spec.product()
+        args.count = spec.batch.count
+        args.left_type = args.right_type = _ffi.TYPE_BF16 if bf16 else _ffi.TYPE_F32
+        if right.dtype != left.dtype:
+            raise SnbError(_ffi.ERR_INVALID_ARGUMENT, "left and right must share a dtype")
+        args.output_type = _ffi.TYPE_BF16 if output.dtype == torch.bfloat16 else _ffi.TYPE_F32
+        args.precision = _ffi.PRECISION_BF16 if bf16 else self.matmul_kernel.precision()
+        if not bf16 and args.precision == _ffi.PRECISION_BF16:
+            args.precision = _ffi.PRECISION_TF32
+        args.left, args.left_len = _ptr(left), left.numel()
+        args.right, args.right_len = _ptr(right), right.numel()
+        args.output, args.output_len = _ptr(output), output.numel()
+        args.bias = _ptr(bias) if bias is not None else None
+        args.activation = activation
+        aux = pre_activation if pre_activation is not None else gelu_input
+        args.aux_type = _ffi.TYPE_BF16 if (aux is not None and aux.dtype == torch.bfloat16) else _ffi.TYPE_F32
+        args.pre_activation = _ptr(pre_activation) if pre_activation is not None else None
+        args.gelu_input = _ptr(gelu_input) if gelu_input is not None else None
+        args.residual = _ptr(residual) if residual is not None else None
+        check(self.lib.snb_gemm(self._stream_handle(), ctypes.byref(args)))
+
+    def causal_softmax(self, scores, queries: int, scale: float, query_offset: int) -> None:
+        """`Gpu::causal_softmax` (ops/attention.rs:57-81) on scores [rows, keys]."""
+        _require_cuda(scores)
+        rows, keys = scores.shape
+        if rows % queries != 0:
+            raise AssertionError("causal_softmax: rows must be a multiple of queries")
+        check(self.lib.snb_causal_softmax(self._stream_handle(), _ptr(scores), scores.numel(), rows, queries, keys,
+                                          scale, query_offset))
+
+    def softmax_backward(self, probabilities, grad) -> None:
+        """`Gpu::softmax_backward` (ops/attention.rs:83-100)."""
+        _require_cuda(probabilities, grad)
+        if tuple(probabilities.shape) != tuple(grad.shape):
+            raise AssertionError("softmax_backward: shape mismatch")
+        rows, cols = probabilities.shape
+        check(self.lib.snb_softmax_backward(self._stream_handle(), _ptr(probabilities), _ptr(grad), rows, cols))
+
+    def synchronize(self) -> None:
+        self.stream.synchronize()
+
+    def device_status(self) -> None:
+        """Raises if a tensor-core kernel's bounded wait gave up since the last check."""
+        check(self.lib.snb_device_status())
+
+
+def last_path() -> int:
+    return _ffi.last_path()

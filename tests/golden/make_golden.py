@@ -1,0 +1,145 @@
+"""Writes tests/golden/reference_kats.json: the known-answer vectors of the reference's own tests for the GEMM
+path and its neighbours, each with the file:line it comes from.
+
+    python tests/golden/make_golden.py [--reference /path/to/staleynet]
+
+The vectors are transcribed below; when the reference checkout is given (or found at the default path), every
+literal is checked to occur verbatim at the cited lines before the fixture is written, so the fixture cannot drift
+from the reference's tests. The GPU box never runs this script; tests read only the JSON.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import sys
+from pathlib import Path
+
+HERE = Path(__file__).resolve().parent
+DEFAULT_REFERENCE = Path("/root/reference")
+REF_FILE = "crates/staleynet-cuda/src/reference.rs"
+
+# (name, source lines, literal snippets that must appear in those lines, case data)
+MATMUL_KATS = [
+    {
+        "name": "matmul_overwrites_a_row_major_product",
+        "source": f"{REF_FILE}:177-187",
+        "snippets": ["MatmulSpec::new(2, 3, 2)", "[1.0, 2.0, 3.0, 4.0]", "[5.0, 6.0, 7.0, 8.0, 9.0, 10.0]",
+                     "[21.0, 24.0, 27.0, 47.0, 54.0, 61.0]"],
+        "rows": 2, "cols": 3, "inner": 2, "left_transposed": False, "right_transposed": False,
+        "batch": {"count": 1, "left": 0, "right": 0, "output": 0}, "scale": 1.0, "accumulate": False,
+        "left": [1.0, 2.0, 3.0, 4.0], "right": [5.0, 6.0, 7.0, 8.0, 9.0, 10.0], "initial": [0.0] * 6,
+        "expected": [21.0, 24.0, 27.0, 47.0, 54.0, 61.0],
+    },
+    {
+        "name": "matmul_scales_and_accumulates_into_the_existing_output",
+        "source": f"{REF_FILE}:189-199",
+        "snippets": ["MatmulSpec::new(2, 3, 2).scaled(0.5).accumulate()", "[1.0f32; 6]",
+                     "[11.5, 13.0, 14.5, 24.5, 28.0, 31.5]"],
+        "rows": 2, "cols": 3, "inner": 2, "left_transposed": False, "right_transposed": False,
+        "batch": {"count": 1, "left": 0, "right": 0, "output": 0}, "scale": 0.5, "accumulate": True,
+        "left": [1.0, 2.0, 3.0, 4.0], "right": [5.0, 6.0, 7.0, 8.0, 9.0, 10.0], "initial": [1.0] * 6,
+        "expected": [11.5, 13.0, 14.5, 24.5, 28.0, 31.5],
+    },
+    {
+        "name": "matmul_honours_transposed_storage",
+        "source": f"{REF_FILE}:201-211",
+        "snippets": ["MatmulSpec::new(2, 2, 2).left_transposed()", "[5.0, 6.0, 7.0, 8.0]",
+                     "[26.0, 30.0, 38.0, 44.0]"],
+        "rows": 2, "cols": 2, "inner": 2, "left_transposed": True, "right_transposed": False,
+        "batch": {"count": 1, "left": 0, "right": 0, "output": 0}, "scale": 1.0, "accumulate": False,
+        "left": [1.0, 2.0, 3.0, 4.0], "right": [5.0, 6.0, 7.0, 8.0], "initial": [0.0] * 4,
+        "expected": [26.0, 30.0, 38.0, 44.0],
+    },
+    {
+        "name": "matmul_broadcasts_batched_operands",
+        "source": f"{REF_FILE}:213-224",
+        "snippets": ["BatchStrides { count: 2, left: 4, right: 0, output: 4 }",
+                     "[1.0, 2.0, 3.0, 4.0, 5.0, 6.0, 7.0, 8.0]", "[1.0, 0.0, 0.0, 1.0]",
+                     "assert_eq!(output, left)"],
+        "rows": 2, "cols": 2, "inner": 2, "left_transposed": False, "right_transposed": False,
+        "batch": {"count": 2, "left": 4, "right": 0, "output": 4}, "scale": 1.0, "accumulate": False,
+        "left": [1.0, 2.0, 3.0, 4.0, 5.0, 6.0, 7.0, 8.0], "right": [1.0, 0.0, 0.0, 1.0], "initial": [0.0] * 8,
+        "expected": [1.0, 2.0, 3.0, 4.0, 5.0, 6.0, 7.0, 8.0],
+    },
+]
+
+SOFTMAX_KATS = [
+    {
+        "name": "causal_softmax_masks_future_keys",
+        "source": f"{REF_FILE}:267-280",
+        "snippets": ["[1.0, 100.0, 100.0, 1.0, 2.0, 100.0]", "causal_softmax(&mut scores, 2, 3, 1.0, 0)",
+                     "0.268_941_4", "0.731_058_6"],
+        "scores": [1.0, 100.0, 100.0, 1.0, 2.0, 100.0], "queries": 2, "keys": 3, "scale": 1.0, "query_offset": 0,
+        "expected": [1.0, 0.0, 0.0, 0.2689414, 0.7310586, 0.0], "tolerance": 1e-6,
+    },
+]
+
+SOFTMAX_BACKWARD_KATS = [
+    {
+        "name": "softmax_backward_projects_out_the_weighted_sum",
+        "source": f"{REF_FILE}:295-306",
+        "snippets": ["[0.25, 0.25, 0.5]", "[1.0, 2.0, 3.0]", "-0.3125", "-0.0625", "0.375"],
+        "probabilities": [0.25, 0.25, 0.5], "grad": [1.0, 2.0, 3.0], "cols": 3,
+        "expected": [-0.3125, -0.0625, 0.375], "tolerance": 1e-6,
+    },
+]
+
+GELU_KATS = [
+    {
+        "name": "gelu_matches_known_values_and_its_finite_difference_derivative",
+        "source": f"{REF_FILE}:226-239",
+        "snippets": ["close(gelu(0.0), 0.0, 1e-6)", "close(gelu(1.0), 0.841_191, 1e-4)",
+                     "close(gelu_derivative(0.0), 0.5, 1e-6)"],
+        "points": [[0.0, 0.0, 1e-6], [1.0, 0.841191, 1e-4]],
+        "derivative_points": [[0.0, 0.5, 1e-6]],
+    },
+]
+
+# SplitMix64 is the reference's generator (crates/staleynet-model/src/random.rs:4-46). Its published output for
+# state 0 (Vigna's splitmix64.c, the algorithm of Steele, Lea & Flood 2014) pins next_u64.
+SPLITMIX_KATS = {
+    "source": "crates/staleynet-model/src/random.rs:4-46",
+    "seed": 0,
+    "outputs": ["0xe220a8397b1dcdaf", "0x6e789e6aa1b965f4", "0x06c45d188009454f"],
+}
+
+
+def check_against_reference(reference: Path) -> None:
+    lines = (reference / REF_FILE).read_text().splitlines()
+    for case in MATMUL_KATS + SOFTMAX_KATS + SOFTMAX_BACKWARD_KATS + GELU_KATS:
+        span = case["source"].rsplit(":", 1)[1]
+        lo, hi = (int(x) for x in span.split("-"))
+        text = "\n".join(lines[lo - 1:hi])
+        for snippet in case["snippets"]:
+            if snippet not in text:
+                raise SystemExit(f"{case['name']}: {snippet!r} not found at {case['source']}")
+    random_src = (reference / "crates/staleynet-model/src/random.rs").read_text()
+    for constant in ("0x9E37_79B9_7F4A_7C15", "0xBF58_476D_1CE4_E5B9", "0x94D0_49BB_1331_11EB"):
+        if constant not in random_src:
+            raise SystemExit(f"SplitMix64 constant {constant} not found in random.rs")
+
+
+def main(argv=None) -> int:
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--reference", type=Path, default=DEFAULT_REFERENCE)
+    args = ap.parse_args(argv)
+    checked = False
+    if (args.reference / REF_FILE).exists():
+        check_against_reference(args.reference)
+        checked = True
+    out = {
+        "generated_by": "tests/golden/make_golden.py",
+        "checked_against_reference_source": checked,
+        "matmul": [{k: v for k, v in c.items() if k != "snippets"} for c in MATMUL_KATS],
+        "causal_softmax": [{k: v for k, v in c.items() if k != "snippets"} for c in SOFTMAX_KATS],
+        "softmax_backward": [{k: v for k, v in c.items() if k != "snippets"} for c in SOFTMAX_BACKWARD_KATS],
+        "gelu": [{k: v for k, v in c.items() if k != "snippets"} for c in GELU_KATS],
+        "splitmix64": SPLITMIX_KATS,
+    }
+    (HERE / "reference_kats.json").write_text(json.dumps(out, indent=1) + "\n")
+    print(f"wrote {HERE / 'reference_kats.json'} (checked against reference source: {checked})")
+    return 0
+
+
+if __name__ == "__main__":
+    sys.exit(main())
