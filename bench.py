@@ -1,0 +1,363 @@
+"""Benchmark: GEMM TFLOP/s of the fwd+dX+dW products of one training step of StaleyNET's width-768 decoder.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+    torchrun --nproc-per-node N bench.py --gpus N ...      (one rank per GPU, NCCL)
+
+Workload (config 5 at N=8): per GPU, one micro-batch of 32 x 2048 = 65,536 tokens through the
+12-block width-768 decoder's linear GEMMs (QKV 768->2304, output 768->768, FFN 768->3072->768) and the 16 x 1024
+codebook head, forward, dX and dW, bf16 operands with f32 accumulation and fused bias / GELU / residual epilogues
+(staleynet_b200/step.py). 38.35 TFLOP per GPU per step. N GPUs run N micro-batches (weak scaling, global batch
+N x 32 x 2048) and all-reduce the f32 weight gradients with NCCL, per block, overlapped with the backward pass.
+
+One JSON line (rank 0): `value` = whole-job TFLOP/s with inputs resident in HBM; `e2e` = the same step through
+the C ABI with the step's input activations copied from pinned host memory and a result read back every step;
+`roofline` = the tcgen05 GEMM kernel's FLOP rate from CUDA events around each launch in the timed region, against
+the measured bf16 peak; `cpu_baseline` = the CPU restatement of the reference's f32 GEMM loop on the host cores,
+timed on a sample of every GEMM's output rows and extrapolated by rows.
+`--impl reference` times that CPU path alone (the reference's own implementation cannot be built here).
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import tempfile
+import time
+from pathlib import Path
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+
+METRIC = "GEMM TFLOP/s (fwd+bwd) & % bf16 tensor peak at 1/2/4/8 B200 vs host-CPU ref"
+UNIT = "TFLOP/s"
+FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}
+
+
+def load_peaks():
+    path = ROOT / "MEASURED_PEAKS.json"
+    if path.exists():
+        data = json.loads(path.read_text())
+        return data, "measured"
+    return dict(FALLBACK_PEAKS), "fallback"
+
+
+def workload_config(shape, n_gpus: int) -> dict:
+    return {
+        "workload": "cfg3 12-block width-768 decoder: linear + 16x1024 codebook-head GEMMs, fwd+dX+dW, "
+                    "32x2048 tokens per GPU (cfg5 data-parallel step at N=8)",
+        "model": "staleynet width-768 12-block decoder (111.5M), linear/head GEMMs",
+        "blocks": shape.blocks,
+        "width": shape.width,
+        "ffn": shape.ffn,
+        "head": f"{shape.codebooks}x{shape.codebook_size}",
+        "tokens_per_gpu": shape.tokens,
+        "global_batch": 32 * n_gpus,
+        "seq_len": 2048,
+        "parallelism": f"dp{n_gpus}",
+        "operands": "bf16 in, f32 accumulate; dW f32 via reduce-add; activations bf16",
+        "l2": "inputs larger than L2: one step moves > 20 GB through HBM (126 MB L2 flushed by the step itself)",
+        "not_in_step": "attention score/softmax products, norms, bias-gradient column sums (not linear GEMMs)",
+    }
+
+
+# ------------------------------------------------------------------------------------------------ clocks
+class ClockSampler:
+    """nvidia-smi samples of SM clock and throttle reasons while the timed region runs."""
+
+    QUERY = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+             "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+             "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, device_index: int):
+        self.device_index = device_index
+        self.proc = None
+        self.file = None
+
+    def start(self):
+        try:
+            self.file = tempfile.NamedTemporaryFile("w+", suffix=".csv", delete=False)
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--id={self.device_index}", f"--query-gpu={self.QUERY}", "--format=csv,noheader",
+                 "-lms", "200"], stdout=self.file, stderr=subprocess.DEVNULL)
+        except (OSError, FileNotFoundError):
+            self.proc = None
+
+    def stop(self) -> dict:
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+        self.file.flush()
+        rows = [line.split(",") for line in Path(self.file.name).read_text().splitlines() if line.strip()]
+        os.unlink(self.file.name)
+        sm, smax, power, reasons = [], None, [], set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for r in rows:
+            try:
+                sm.append(float(r[1].split()[0]))
+                smax = float(r[2].split()[0])
+                power.append(float(r[3].split()[0]))
+            except (ValueError, IndexError):
+                continue
+            for name, flag in zip(names, r[5:9]):
+                if "Active" in flag and "Not" not in flag:
+                    reasons.add(name)
+        loaded = [v for v in sm if smax and v > 0.3 * smax] or sm
+        return {"sm_mhz": statistics.median(loaded) if loaded else None, "sm_max_mhz": smax,
+                "reasons": sorted(reasons), "samples": len(sm),
+                "power_w_max": max(power) if power else None}
+
+
+# ------------------------------------------------------------------------------------------------ CPU baseline
+def cpu_baseline(shape, budget_flops: float = 20e9, threads: int = 0) -> dict:
+    """Times the CPU oracle (the reference's f32 GEMM loop, reference.rs:18-38) on a sample of every GEMM of the
+    step and extrapolates by output elements (each output element costs the same `inner` multiply-adds).
+
+    The sample of a GEMM is its first rows x cols output block with cols = min(N, 256), sized to `budget_flops`
+    over the whole step; operands keep the step's true strides (zero pages are mapped lazily, so only the lines
+    the sample reads become resident). Each sample runs twice and the second run is timed."""
+    import numpy as np
+
+    from oracle import oracle as o
+    from staleynet_b200.step import linear_shapes, step_flops
+
+    s = shape
+    T, w, V = s.tokens, s.width, s.head_width
+    total = step_flops(s)
+    frac = min(1.0, budget_flops / total)
+    gemms = []  # (repeats per step, M, N, K, left transposed, right transposed)
+    for _, i, out in linear_shapes(s):
+        gemms.append((s.blocks, T, out, i, False, False))   # forward  Y = X W
+        gemms.append((s.blocks, T, i, out, False, True))    # dX = dY W^T
+        gemms.append((s.blocks, i, out, T, True, False))    # dW += X^T dY
+    gemms += [(1, T, V, w, False, False), (1, T, w, V, False, True), (1, w, V, T, True, False)]
+    seconds_full = 0.0
+    sampled_flops = 0.0
+    used_threads = 1
+    t_start = time.perf_counter()
+    for mult, M, N, K, lt, rt in gemms:
+        cols = min(N, 256)
+        rows = min(M, max(1, int(round(frac * M * N / cols))))
+        left = np.zeros(M * K, np.float32)
+        right = np.zeros(K * N, np.float32)
+        out = np.zeros(rows * cols, np.float32)
+        p = o.product(rows, cols, K, o.storage_strides(lt, M, K, 0), o.storage_strides(rt, K, N, 0), 0)
+        o.matmul_rows(p, 1, left, right, out, 0, rows, threads)
+        t0 = time.perf_counter()
+        used_threads = o.matmul_rows(p, 1, left, right, out, 0, rows, threads)
+        dt = time.perf_counter() - t0
+        seconds_full += mult * dt * (M * N) / (rows * cols)
+        sampled_flops += 2.0 * rows * cols * K
+        del left, right, out
+    wall = time.perf_counter() - t_start
+    return {"value": total / seconds_full / 1e12, "unit": UNIT, "cores": used_threads, "kind": "port",
+            "sample": f"first rows x min(N,256) output block of every GEMM of the step, {frac:.2e} of its "
+                      f"outputs ({sampled_flops / 1e9:.1f} GFLOP timed, {wall:.1f} s wall incl. an untimed "
+                      f"first pass), extrapolated by output elements; f32 operands at the step's strides",
+            "seconds_per_step_extrapolated": seconds_full}
+
+
+# ------------------------------------------------------------------------------------------------ main paths
+def run_reference(args, shape, rank: int, world: int) -> int:
+    if rank != 0:
+        return 0
+    from oracle import oracle as o
+
+    o.build()
+    for _ in range(args.warmup):
+        cpu_baseline(shape, budget_flops=args.cpu_sample_flops)
+    vals, secs = [], []
+    for _ in range(args.steps):
+        r = cpu_baseline(shape, budget_flops=args.cpu_sample_flops)
+        vals.append(r["value"])
+        secs.append(r["seconds_per_step_extrapolated"])
+    value = statistics.median(vals)
+    line = {
+        "impl": "reference", "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": args.gpus,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": statistics.median(secs) * 1e3,
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "config": workload_config(shape, args.gpus),
+        "cpu_baseline": {"value": value, "unit": UNIT, "cores": r["cores"], "kind": "port", "sample": r["sample"]},
+        "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+        "note": "CPU restatement of reference::matmul (crates/staleynet-cuda/src/reference.rs:18-38); the "
+                "reference's Rust CPU path cannot be built here (no Rust toolchain)",
+    }
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+def run_ours(args, shape, rank: int, world: int, local_rank: int) -> int:
+    import torch
+    import torch.distributed as dist
+
+    from staleynet_b200.step import TrainingStepGemms
+
+    torch.cuda.set_device(local_rank)
+    device = torch.device("cuda", local_rank)
+    stream = torch.cuda.current_stream(device)
+    comm = torch.cuda.Stream(device) if world > 1 else None
+    step = TrainingStepGemms(shape, device, seed=1234 + rank)
+    handle = stream.cuda_stream
+
+    def one_step(events=None):
+        works = []
+        step.zero_grads()
+
+        def on_block(b):
+            ev = torch.cuda.Event()
+            ev.record(stream)
+            with torch.cuda.stream(comm):
+                comm.wait_event(ev)
+                bufs = [step.block_grad_flat[b]]
+                if b == shape.blocks - 1:
+                    bufs.append(step.head_grad)
+                for t in bufs:
+                    works.append(dist.all_reduce(t, async_op=True))
+
+        step.run(handle, on_block_done=on_block if world > 1 else None, events=events)
+        for wk in works:
+            wk.wait()
+
+    # Warm-up (also configures every kernel variant and builds the NCCL communicator).
+    for _ in range(args.warmup):
+        one_step()
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+
+    # Timed region: device-resident inputs.
+    n_launch = step.launches_per_step()
+    ev_pairs = [[(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+                 for _ in range(n_launch)] for _ in range(args.steps)]
+    clocks = ClockSampler(local_rank)
+    clocks.start()
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    start.record(stream)
+    for k in range(args.steps):
+        one_step(events=ev_pairs[k])
+    end.record(stream)
+    torch.cuda.synchronize()
+    clock_info = clocks.stop()
+    if world > 1:
+        dist.barrier()
+    ms_total = start.elapsed_time(end)
+    kernel_ms = sum(a.elapsed_time(b) for pairs in ev_pairs for a, b in pairs)
+
+    # End-to-end: the step's input activations come from pinned host memory every step and one result value is
+    # read back; everything else as above.
+    host_x = torch.empty(step.x_in.numel(), dtype=step.x_in.dtype, pin_memory=True)
+    host_x.copy_(step.x_in.cpu())
+    host_out = torch.empty(1, dtype=torch.float32, pin_memory=True)
+    h2d = host_x.numel() * host_x.element_size()
+    d2h = host_out.numel() * host_out.element_size()
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    e_start, e_end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e_start.record(stream)
+    for _ in range(args.steps):
+        step.x_in.copy_(host_x, non_blocking=True)
+        one_step()
+        host_out.copy_(step.head_grad[:1], non_blocking=True)
+    e_end.record(stream)
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    e2e_ms_total = e_start.elapsed_time(e_end)
+
+    stats = torch.tensor([ms_total, e2e_ms_total, kernel_ms], device=device, dtype=torch.float64)
+    if world > 1:
+        dist.all_reduce(stats, op=dist.ReduceOp.MAX)
+    ms_total, e2e_ms_total, kernel_ms = stats.tolist()
+
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        cpu = cpu_baseline(shape, budget_flops=args.cpu_sample_flops)
+
+    if rank == 0:
+        peaks, source = load_peaks()
+        flops_step = step.plan_flops
+        ms_step = ms_total / args.steps
+        value = flops_step * world * args.steps / (ms_total / 1e3) / 1e12
+        e2e_value = flops_step * world * args.steps / (e2e_ms_total / 1e3) / 1e12
+        achieved = flops_step * args.steps / (kernel_ms / 1e3) / 1e12
+        peak_sus = float(peaks.get("bf16_tflops_sustained", FALLBACK_PEAKS["bf16_tflops_sustained"]))
+        peak_burst = float(peaks.get("bf16_tflops", FALLBACK_PEAKS["bf16_tflops"]))
+        line = {
+            "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": ms_step, "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "bf16", "data": "synthetic (seeded N(0,1) activations, N(0,1/sqrt(768)) "
+                                                           "weights, torch generator)",
+            "config": workload_config(shape, world),
+            "pct_bf16_peak_sustained": 100.0 * (value / world) / peak_sus,
+            "pct_bf16_peak_burst": 100.0 * (value / world) / peak_burst,
+            "roofline": {
+                "bound": "tensor", "achieved": achieved, "peak": peak_sus, "unit": "TFLOP/s",
+                "frac": achieved / peak_sus, "traffic": None,
+                "kernel": "snb::tc_gemm_kernel (all launches of one step on rank 0)",
+                "peak_source": f"{source} bf16_tflops_sustained (kernel timed inside a long step); "
+                               f"burst {peak_burst}",
+                "launches_per_step": n_launch,
+                "flops_per_step": flops_step,
+            },
+            "e2e": {"value": e2e_value, "unit": UNIT, "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
+                    "ms_per_step": e2e_ms_total / args.steps, "path": "snb_gemm C ABI via ctypes"},
+            "gpu_launches": n_launch * args.steps,
+            "clocks": clock_info,
+        }
+        if cpu is not None:
+            line["cpu_baseline"] = {k: cpu[k] for k in ("value", "unit", "cores", "kind", "sample")}
+        print(json.dumps(line), flush=True)
+    del step
+    return 0
+
+
+def main(argv=None) -> int:
+    ap = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=10)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--tokens", type=int, default=32 * 2048, help="tokens per GPU (default: BASELINE config 3)")
+    ap.add_argument("--cpu-sample-flops", type=float, default=20e9)
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args(argv)
+    if args.warmup < 3:
+        ap.error("--warmup must be at least 3")
+
+    from staleynet_b200.step import ModelShape
+
+    shape = ModelShape(tokens=args.tokens)
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local_rank = int(os.environ.get("LOCAL_RANK", "0"))
+    if args.impl == "reference":
+        return run_reference(args, shape, rank, world)
+
+    if world > 1:
+        import datetime
+
+        import torch
+        import torch.distributed as dist
+
+        torch.cuda.set_device(local_rank)
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                device_id=torch.device("cuda", local_rank))
+    try:
+        return run_ours(args, shape, rank, world, local_rank)
+    finally:
+        if world > 1:
+            import torch.distributed as dist
+
+            dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    sys.exit(main())

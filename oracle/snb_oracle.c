@@ -51,23 +51,34 @@ void snb_oracle_matmul(const snb_product* p, uint64_t count, const float* left, 
     snb_oracle_matmul_rows(p, count, left, right, output, 0, p->rows);
 }
 
-/* The same loop, output rows split over `threads` OpenMP threads (0 = all). Each output element is still the
- * reference's sequential f32 sum, so results are bit-identical to snb_oracle_matmul. Used as the all-cores CPU
- * baseline. Returns the thread count used. */
+/* The same loop over the output block [row_begin, row_end) x [0, cols), output elements split over `threads`
+ * OpenMP threads (0 = all). Each output element is still the reference's sequential f32 sum, so results are
+ * bit-identical to snb_oracle_matmul. Used as the all-cores CPU baseline. Returns the thread count used. */
 int snb_oracle_matmul_parallel(const snb_product* p, uint64_t count, const float* left, const float* right,
                                float* output, uint64_t row_begin, uint64_t row_end, int threads) {
     int used = 1;
+    const int64_t begin = (int64_t)row_begin, end = (int64_t)(row_end < p->rows ? row_end : p->rows);
+    const int64_t cols = (int64_t)p->cols;
 #ifdef _OPENMP
     if (threads <= 0) threads = omp_get_max_threads();
     used = threads;
-    int64_t begin = (int64_t)row_begin, end = (int64_t)(row_end < p->rows ? row_end : p->rows);
-#pragma omp parallel for num_threads(threads) schedule(static)
-    for (int64_t row = begin; row < end; ++row) {
-        snb_oracle_matmul_rows(p, count, left, right, output, (uint64_t)row, (uint64_t)row + 1);
+#pragma omp parallel for collapse(3) num_threads(threads) schedule(static)
+#endif
+    for (int64_t batch = 0; batch < (int64_t)count; ++batch) {
+        for (int64_t row = begin; row < end; ++row) {
+            for (int64_t col = 0; col < cols; ++col) {
+                float sum = 0.0f;
+                for (uint64_t step = 0; step < p->inner; ++step) {
+                    sum += operand_at(left, &p->left, (uint64_t)batch, (uint64_t)row, step) *
+                           operand_at(right, &p->right, (uint64_t)batch, step, (uint64_t)col);
+                }
+                float* slot = &output[batch * p->output_batch_stride + row * p->cols + col];
+                *slot = p->accumulate ? *slot + p->scale * sum : p->scale * sum;
+            }
+        }
     }
-#else
+#ifndef _OPENMP
     (void)threads;
-    snb_oracle_matmul_rows(p, count, left, right, output, row_begin, row_end);
 #endif
     return used;
 }

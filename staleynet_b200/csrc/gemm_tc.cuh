@@ -16,7 +16,8 @@
 // Operand layouts: each operand is either K-major (K contiguous) or MN-major (M or N contiguous); both are loaded
 // by TMA in their stored order and described to the tensor core by the major bits of the instruction descriptor,
 // so the four storage combinations of the reference (`Storage::{RowMajor,Transposed}`, ops/matmul.rs:16-33) run
-// without any transposition pass.
+// without any transposition pass. Every operand uses a 128-byte swizzle with 16-byte atoms except MN-major tf32
+// operands, which the tensor core reads only with 32-byte atoms (TMA's SWIZZLE_128B_ATOM_32B).
 //
 // Split-K: a work unit may cover only part of K; partial sums then always reach C through TMA reduce-add, which
 // adds element-wise in L2 (C must be pre-zeroed by the host for an overwrite).
@@ -235,11 +236,18 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
         // ------------------------------------------------------------------ MMA issuer
         if (elect_one()) {
             const uint32_t idesc = make_instr_desc(FORMAT, p.a_mn_major, p.b_mn_major, TC_BM, BN);
-            // Byte offsets of the canonical 128B-swizzled layouts: K-major rows are 128 bytes apart and groups of
-            // 8 rows 1024 bytes apart (SBO); MN-major slices have 128-byte K rows, 8-row groups 1024 bytes apart
-            // (SBO) and successive 128-byte MN chunks one box (BK rows) apart (LBO).
+            // Byte offsets of the canonical 128-byte-swizzled layouts: K-major rows are 128 bytes apart and groups
+            // of 8 rows 1024 bytes apart (SBO). MN-major slices have 128-byte K rows and successive 128-byte MN
+            // chunks one box (BK rows) apart (LBO); their K rows group by 8 (16-byte swizzle atoms, bf16, SBO 1024)
+            // or by 4 (32-byte atoms, tf32, SBO 512).
+            constexpr uint32_t MN_LAYOUT = IS_BF16 ? SNB_LAYOUT_SWIZZLE_128B : SNB_LAYOUT_SWIZZLE_128B_BASE32B;
+            constexpr uint32_t MN_SBO = IS_BF16 ? 1024 : 512;
             const uint32_t a_lbo = p.a_mn_major ? BK * 128 : 16;
             const uint32_t b_lbo = p.b_mn_major ? BK * 128 : 16;
+            const uint32_t a_sbo = p.a_mn_major ? MN_SBO : 1024;
+            const uint32_t b_sbo = p.b_mn_major ? MN_SBO : 1024;
+            const uint32_t a_layout = p.a_mn_major ? MN_LAYOUT : SNB_LAYOUT_SWIZZLE_128B;
+            const uint32_t b_layout = p.b_mn_major ? MN_LAYOUT : SNB_LAYOUT_SWIZZLE_128B;
             const uint32_t a_kstep = p.a_mn_major ? UMMA_K * 128 : 32;
             const uint32_t b_kstep = p.b_mn_major ? UMMA_K * 128 : 32;
             int stage = 0;
@@ -261,8 +269,8 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
                     const uint32_t sb = sa + Cfg::STAGE_A;
 #pragma unroll
                     for (int k = 0; k < BK / UMMA_K; ++k) {
-                        const uint64_t ad = make_smem_desc(sa + k * a_kstep, a_lbo, 1024);
-                        const uint64_t bd = make_smem_desc(sb + k * b_kstep, b_lbo, 1024);
+                        const uint64_t ad = make_smem_desc(sa + k * a_kstep, a_lbo, a_sbo, a_layout);
+                        const uint64_t bd = make_smem_desc(sb + k * b_kstep, b_lbo, b_sbo, b_layout);
                         const uint32_t accumulate = (kb > u.kb_begin || k > 0) ? 1u : 0u;
                         if (IS_BF16) umma_bf16(d_tmem, ad, bd, idesc, accumulate);
                         else umma_tf32(d_tmem, ad, bd, idesc, accumulate);

@@ -202,16 +202,20 @@ __device__ __forceinline__ void tmem_load_wait() { asm volatile("tcgen05.wait::l
 // ------------------------------------------------------------------------------------------------ descriptors
 // Shared-memory matrix descriptor (tcgen05 "matrix descriptor"): start address, leading/stride byte offsets (all
 // in 16-byte units), version 1 (bits 46-47), base offset 0, and the layout (swizzle) type in bits 61-63.
-// SWIZZLE_128B is encoded as 2.
-constexpr uint64_t SNB_LAYOUT_SWIZZLE_128B = 2;
+// SWIZZLE_128B (16-byte chunks XORed with the 128-byte row index mod 8) is encoded as 2; SWIZZLE_128B_BASE32B
+// (32-byte chunks XORed with the row index mod 4), the only layout the tensor core accepts for MN-major 32-bit
+// (tf32) operands, as 1.
+constexpr uint32_t SNB_LAYOUT_SWIZZLE_128B = 2;
+constexpr uint32_t SNB_LAYOUT_SWIZZLE_128B_BASE32B = 1;
 
-__device__ __forceinline__ uint64_t make_smem_desc(uint32_t saddr, uint32_t lbo_bytes, uint32_t sbo_bytes) {
+__device__ __forceinline__ uint64_t make_smem_desc(uint32_t saddr, uint32_t lbo_bytes, uint32_t sbo_bytes,
+                                                   uint32_t layout) {
     uint64_t d = 0;
     d |= static_cast<uint64_t>((saddr >> 4) & 0x3FFFu);
     d |= static_cast<uint64_t>((lbo_bytes >> 4) & 0x3FFFu) << 16;
     d |= static_cast<uint64_t>((sbo_bytes >> 4) & 0x3FFFu) << 32;
     d |= static_cast<uint64_t>(1) << 46;
-    d |= SNB_LAYOUT_SWIZZLE_128B << 61;
+    d |= static_cast<uint64_t>(layout & 7u) << 61;
     return d;
 }
 

@@ -72,7 +72,7 @@ OperandLayout classify(uint64_t mn, uint64_t k, uint64_t mn_stride, uint64_t k_s
 
 bool encode_3d(CUtensorMap* map, CUtensorMapDataType dt, int esize, const void* base, uint64_t d0, uint64_t d1,
                uint64_t d2, uint64_t stride1_elems, uint64_t stride2_elems, uint32_t box0, uint32_t box1,
-               std::string* err) {
+               std::string* err, CUtensorMapSwizzle swizzle = CU_TENSOR_MAP_SWIZZLE_128B) {
     EncodeTiledFn fn = encode_fn();
     if (!fn) {
         *err = "cuTensorMapEncodeTiled is not available from the CUDA driver";
@@ -83,7 +83,7 @@ bool encode_3d(CUtensorMap* map, CUtensorMapDataType dt, int esize, const void* 
     cuuint32_t box[3] = {box0, box1, 1};
     cuuint32_t estr[3] = {1, 1, 1};
     CUresult r = fn(map, dt, 3, const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
-                    CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+                    swizzle, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
     if (r != CUDA_SUCCESS) {
         *err = "cuTensorMapEncodeTiled failed with CUresult " + std::to_string(static_cast<int>(r));
         return false;
@@ -201,10 +201,13 @@ int tc_gemm_try(cudaStream_t stream, const GemmRequest& r, bool* launched, std::
     CUtensorMap ta, tb, tc, tp;
     const CUtensorMapDataType in_dt = bf16_in ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_TFLOAT32;
     const uint32_t mn_box = 128 / esize;
+    // MN-major tf32 slices use 32-byte swizzle atoms (the only MN-major layout the tensor core reads for 32-bit
+    // operands); everything else 16-byte atoms.
+    const CUtensorMapSwizzle mn_swizzle = bf16_in ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B;
     // A: (mn = rows, k = inner)
     if (la.mn_major) {
         if (!encode_3d(&ta, in_dt, esize, r.A, p.rows, p.inner, la.batched ? r.count : 1, la.ld,
-                       la.batched ? p.left.batch_stride : la.ld * p.inner, mn_box, bk, err))
+                       la.batched ? p.left.batch_stride : la.ld * p.inner, mn_box, bk, err, mn_swizzle))
             return SNB_OK;
     } else {
         if (!encode_3d(&ta, in_dt, esize, r.A, p.inner, p.rows, la.batched ? r.count : 1, la.ld,
@@ -214,7 +217,7 @@ int tc_gemm_try(cudaStream_t stream, const GemmRequest& r, bool* launched, std::
     // B: (mn = cols, k = inner)
     if (lb.mn_major) {
         if (!encode_3d(&tb, in_dt, esize, r.B, p.cols, p.inner, lb.batched ? r.count : 1, lb.ld,
-                       lb.batched ? p.right.batch_stride : lb.ld * p.inner, mn_box, bk, err))
+                       lb.batched ? p.right.batch_stride : lb.ld * p.inner, mn_box, bk, err, mn_swizzle))
             return SNB_OK;
     } else {
         if (!encode_3d(&tb, in_dt, esize, r.B, p.inner, p.cols, lb.batched ? r.count : 1, lb.ld,

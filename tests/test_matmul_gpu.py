@@ -97,7 +97,7 @@ def test_matmul_matches_reference_for_every_storage_and_kernel(gpu, rows, cols, 
 @pytest.mark.parametrize("lt,rt", [(False, False), (True, False), (False, True), (True, True)])
 def test_bf16_tensor_core_is_exact_up_to_summation_order(gpu, lt, rt):
     """Against the oracle on the same bf16-rounded inputs the only difference left is the f32 summation order."""
-    rows, cols, inner, batch = 257, 264, 136, 2
+    rows, cols, inner, batch = 264, 264, 136, 2  # every stride a multiple of 16 bytes in every storage
     spec = variants(rows, cols, inner, batch)[(1 if lt else 0) + (2 if rt else 0)]
     left, _ = o.round_bf16(o.lcg_values(batch * rows * inner, 4))
     right, _ = o.round_bf16(o.lcg_values(batch * inner * cols, 5))
