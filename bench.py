@@ -249,6 +249,19 @@ def run_ours(args, shape, rank: int, world: int, local_rank: int) -> int:
         dist.barrier()
     ms_total = start.elapsed_time(end)
     kernel_ms = sum(a.elapsed_time(b) for pairs in ev_pairs for a, b in pairs)
+    if args.breakdown and rank == 0:
+        table = {}
+        for pairs in ev_pairs:
+            for (name, flops, _), (a, b) in zip(step.plan, pairs):
+                row = table.setdefault(name, {"launches": 0, "ms": 0.0, "flops": 0.0})
+                row["launches"] += 1
+                row["ms"] += a.elapsed_time(b)
+                row["flops"] += flops
+        for row in table.values():
+            row["tflops"] = row["flops"] / (row["ms"] / 1e3) / 1e12
+            row["ms_per_step"] = row["ms"] / args.steps
+            row["share"] = row["ms"] / kernel_ms
+        Path(args.breakdown).write_text(json.dumps(table, indent=1) + "\n")
 
     # End-to-end: the step's input activations come from pinned host memory every step and one result value is
     # read back; everything else as above.
@@ -328,6 +341,7 @@ def main(argv=None) -> int:
     ap.add_argument("--tokens", type=int, default=32 * 2048, help="tokens per GPU (default: BASELINE config 3)")
     ap.add_argument("--cpu-sample-flops", type=float, default=20e9)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--breakdown", default=None, help="write per-GEMM kernel times of the timed region here (JSON)")
     args = ap.parse_args(argv)
     if args.warmup < 3:
         ap.error("--warmup must be at least 3")

@@ -46,6 +46,7 @@ struct TcParams {
     int32_t m_tiles, n_tiles; // output tiles per matrix
     int32_t k_blocks;         // 128-byte K slices per product
     int32_t splits;           // K splits per tile (>= 1)
+    int32_t m_fastest;        // unit order: 1 = M tile index fastest, 0 = N tile index fastest
     int32_t k_blocks_per_split;
     int32_t num_units;        // count * m_tiles * n_tiles * splits
     float scale;
@@ -77,14 +78,26 @@ struct TcUnit {
     int32_t batch, m0, n0, kb_begin, kb_end, split;
 };
 
+// Work-unit order: K split outermost (the tiles of one split run side by side, so concurrent CTAs share operand
+// slices in L2 and the splits of one tile never reduce into C at the same time), then the batch, then output tiles
+// with the M or the N tile index fastest, whichever keeps the larger operand streaming through DRAM once.
 __device__ __forceinline__ TcUnit tc_decode_unit(const TcParams& p, int32_t unit, int BN) {
     TcUnit u;
-    const int32_t tile = unit / p.splits;
-    u.split = unit - tile * p.splits;
-    const int32_t nt = tile % p.n_tiles;
-    const int32_t rest = tile / p.n_tiles;
-    const int32_t mt = rest % p.m_tiles;
-    u.batch = rest / p.m_tiles;
+    const int32_t tiles = p.count * p.m_tiles * p.n_tiles;
+    u.split = unit / tiles;
+    const int32_t tile = unit - u.split * tiles;
+    int32_t mt, nt, rest;
+    if (p.m_fastest) {
+        mt = tile % p.m_tiles;
+        rest = tile / p.m_tiles;
+        nt = rest % p.n_tiles;
+        u.batch = rest / p.n_tiles;
+    } else {
+        nt = tile % p.n_tiles;
+        rest = tile / p.n_tiles;
+        mt = rest % p.m_tiles;
+        u.batch = rest / p.m_tiles;
+    }
     u.m0 = mt * TC_BM;
     u.n0 = nt * BN;
     u.kb_begin = u.split * p.k_blocks_per_split;
@@ -92,40 +105,109 @@ __device__ __forceinline__ TcUnit tc_decode_unit(const TcParams& p, int32_t unit
     return u;
 }
 
-__device__ __forceinline__ float gelu_tanh(float x) {
-    // 0.5 x (1 + tanh(sqrt(2/pi) (x + 0.044715 x^3))): the reference's tanh approximation (kernels/elementwise.rs:14-17)
-    const float inner = 0.7978846f * (x + 0.044715f * x * x * x);
-    return 0.5f * x * (1.0f + tanhf(inner));
-}
-
-__device__ __forceinline__ float gelu_tanh_derivative(float x) {
-    // kernels/elementwise.rs:20-24
-    const float t = tanhf(0.7978846f * (x + 0.044715f * x * x * x));
-    return 0.5f * (1.0f + t) + 0.5f * x * (1.0f - t * t) * 0.7978846f * (1.0f + 3.0f * 0.044715f * x * x);
-}
-
-__device__ __forceinline__ float load_elem(const void* base, int64_t index, int is_bf16) {
-    if (is_bf16) {
-        const uint16_t bits = __ldg(reinterpret_cast<const unsigned short*>(base) + index);
-        return __uint_as_float(static_cast<uint32_t>(bits) << 16);
-    }
-    return __ldg(reinterpret_cast<const float*>(base) + index);
-}
-
 __device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
     __nv_bfloat162 v = __floats2bfloat162_rn(lo, hi);
     return *reinterpret_cast<uint32_t*>(&v);
 }
 
-// Packs one lane's chunk (32 f32 values, or 64 values as bf16 pairs) into the 32 words of a 128-byte box row.
-template <bool OUT_BF16, int CHUNK>
-__device__ __forceinline__ void pack_chunk(const uint32_t (&x)[CHUNK], uint32_t (&w)[32]) {
-    if constexpr (OUT_BF16) {
+// Loads 32 consecutive elements (f32: 8 x 16 bytes; bf16: 4 x 16 bytes) of one row starting at element `index`,
+// zero where `valid` (columns left in the row) runs out or the row is dead. The host guarantees 16-byte alignment
+// of every row start and that the row length is a multiple of 16 bytes.
+__device__ __forceinline__ void load_row_32(const void* base, int64_t index, int is_bf16, int valid, bool live,
+                                            uint4 (&r)[8]) {
+    if (is_bf16) {
+        const uint4* src = reinterpret_cast<const uint4*>(reinterpret_cast<const uint16_t*>(base) + index);
 #pragma unroll
-        for (int j = 0; j < 32; ++j) w[j] = pack_bf16x2(__uint_as_float(x[2 * j]), __uint_as_float(x[2 * j + 1]));
+        for (int j = 0; j < 4; ++j) r[j] = (live && 8 * j < valid) ? __ldg(src + j) : make_uint4(0, 0, 0, 0);
+    } else {
+        const uint4* src = reinterpret_cast<const uint4*>(reinterpret_cast<const float*>(base) + index);
+#pragma unroll
+        for (int j = 0; j < 8; ++j) r[j] = (live && 4 * j < valid) ? __ldg(src + j) : make_uint4(0, 0, 0, 0);
+    }
+}
+
+// tanh for the GELU epilogues. Outputs rounded to bf16 use the hardware's tanh.approx.f32 (one MUFU instruction,
+// relative error about 2^-11, below the 2^-9 rounding of bf16), which keeps a GELU epilogue off the critical path;
+// f32 outputs use the accurate tanhf.
+template <bool FAST>
+__device__ __forceinline__ float tanh_epilogue(float x) {
+    if constexpr (FAST) {
+        float y;
+        asm("tanh.approx.f32 %0, %1;" : "=f"(y) : "f"(x));
+        return y;
+    } else {
+        return tanhf(x);
+    }
+}
+
+// GELU, tanh approximation (the reference's gelu_forward, crates/staleynet-cuda/src/kernels/elementwise.rs:14-17)
+// and its derivative (kernels/elementwise.rs:20-24), on pairs of values with Blackwell's packed f32x2 arithmetic:
+//   t = tanh(c (x + a x^3)),  gelu = 0.5 x (1 + t),  gelu' = 0.5 (1 + t) + 0.5 x (1 - t^2) (c + 3 a c x^2)
+// with c = sqrt(2/pi) and a = 0.044715.
+constexpr float GELU_C = 0.7978846f;
+constexpr float GELU_A = 0.044715f;
+
+__device__ __forceinline__ float2 f2(float v) { return make_float2(v, v); }
+
+template <bool FAST>
+__device__ __forceinline__ float2 gelu_tanh_arg(float2 x, float2& x2) {
+    x2 = __fmul2_rn(x, x);
+    const float2 x3 = __fmul2_rn(x2, x);
+    const float2 inner = __ffma2_rn(f2(GELU_A), x3, x);
+    const float2 arg = __fmul2_rn(f2(GELU_C), inner);
+    return make_float2(tanh_epilogue<FAST>(arg.x), tanh_epilogue<FAST>(arg.y));
+}
+
+template <bool FAST>
+__device__ __forceinline__ float2 gelu2(float2 x) {
+    float2 x2;
+    const float2 t = gelu_tanh_arg<FAST>(x, x2);
+    const float2 hx = __fmul2_rn(f2(0.5f), x);
+    return __ffma2_rn(hx, t, hx);
+}
+
+template <bool FAST>
+__device__ __forceinline__ float2 gelu2_derivative(float2 x) {
+    float2 x2;
+    const float2 t = gelu_tanh_arg<FAST>(x, x2);
+    const float2 half_1pt = __ffma2_rn(f2(0.5f), t, f2(0.5f));
+    const float2 one_m_t2 = __ffma2_rn(make_float2(-t.x, -t.y), t, f2(1.0f));
+    const float2 poly = __ffma2_rn(f2(3.0f * GELU_A * GELU_C), x2, f2(GELU_C));
+    const float2 q = __fmul2_rn(__fmul2_rn(f2(0.5f), x), one_m_t2);
+    return __ffma2_rn(q, poly, half_1pt);
+}
+
+// Unpacks 32 auxiliary values loaded by load_row_32 into 16 pairs.
+__device__ __forceinline__ void unpack_row_32x2(const uint4 (&r)[8], int is_bf16, float2 (&v)[16]) {
+    if (is_bf16) {
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+            const uint32_t u[4] = {r[j].x, r[j].y, r[j].z, r[j].w};
+#pragma unroll
+            for (int k = 0; k < 4; ++k) v[4 * j + k] = make_float2(__uint_as_float(u[k] << 16), __uint_as_float(u[k] & 0xffff0000u));
+        }
     } else {
 #pragma unroll
-        for (int j = 0; j < 32; ++j) w[j] = x[j];
+        for (int j = 0; j < 8; ++j) {
+            v[2 * j] = make_float2(__uint_as_float(r[j].x), __uint_as_float(r[j].y));
+            v[2 * j + 1] = make_float2(__uint_as_float(r[j].z), __uint_as_float(r[j].w));
+        }
+    }
+}
+
+// Packs 16 pairs into this lane's box row: f32 fills words [0, 32); bf16 fills words [16h, 16h + 16) of a
+// 64-column chunk.
+template <bool OUT_BF16>
+__device__ __forceinline__ void pack_pairs(const float2 (&v)[16], uint32_t (&w)[32], int h) {
+    if constexpr (OUT_BF16) {
+#pragma unroll
+        for (int j = 0; j < 16; ++j) w[16 * h + j] = pack_bf16x2(v[j].x, v[j].y);
+    } else {
+#pragma unroll
+        for (int j = 0; j < 16; ++j) {
+            w[2 * j] = __float_as_uint(v[j].x);
+            w[2 * j + 1] = __float_as_uint(v[j].y);
+        }
     }
 }
 
@@ -144,6 +226,7 @@ template <typename E, int BN, bool OUT_BF16>
 __global__ void __launch_bounds__(TC_THREADS, 1)
     tc_gemm_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constant__ CUtensorMap tm_b,
                    const __grid_constant__ CUtensorMap tm_c, const __grid_constant__ CUtensorMap tm_pre,
+                   const __grid_constant__ CUtensorMap tm_res, const __grid_constant__ CUtensorMap tm_gin,
                    const TcParams p) {
     using Cfg = TcConfig<BN>;
     constexpr int ESIZE = sizeof(E);
@@ -206,6 +289,11 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
                 const TcUnit u = tc_decode_unit(p, unit, BN);
                 const int32_t ba = p.a_batched ? u.batch : 0;
                 const int32_t bb = p.b_batched ? u.batch : 0;
+                // Bring this tile's epilogue inputs into L2 now; the epilogue reads them one main loop later.
+                if (u.split == 0) {
+                    if (p.residual != nullptr) tma_prefetch_l2_3d(&tm_res, u.n0, u.m0, u.batch);
+                    if (p.activation == 2) tma_prefetch_l2_3d(&tm_gin, u.n0, u.m0, u.batch);
+                }
                 for (int32_t kb = u.kb_begin; kb < u.kb_end; ++kb) {
                     const uint32_t fb = smem_addr(&full[stage]);
                     if (!mbar_wait(smem_addr(&empty[stage]), phase ^ 1u)) { ok = false; break; }
@@ -309,29 +397,66 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
             const uint32_t t_lane = tmem_base + (static_cast<uint32_t>(q * 32) << 16) + acc * BN;
 
             for (int c = 0; c < BN && row0 < p.M && u.n0 + c < p.N; c += CHUNK) {
-                uint32_t x[CHUNK];
-                tmem_load_32x32b_x32(t_lane + c, *reinterpret_cast<uint32_t(*)[32]>(&x[0]));
-                if constexpr (CHUNK == 64)
-                    tmem_load_32x32b_x32(t_lane + c + 32, *reinterpret_cast<uint32_t(*)[32]>(&x[32]));
-                tmem_load_wait();
-
                 const int32_t col0 = u.n0 + c;
                 const bool row_live = row < p.M;
-                // x = scale * acc + bias
+                uint32_t w[32];   // this lane's 128-byte row of the output box
+                uint32_t wp[32];  // ... and of the pre-activation box
+                // The chunk is processed 32 columns at a time (one tcgen05.ld); a bf16 chunk has two such halves.
 #pragma unroll
-                for (int i = 0; i < CHUNK; ++i) {
-                    float f = p.scale * __uint_as_float(x[i]);
-                    if (p.bias != nullptr && first_split && col0 + i < p.N) f += __ldg(p.bias + col0 + i);
-                    x[i] = __float_as_uint(f);
+                for (int h = 0; h < CHUNK / 32; ++h) {
+                    const int32_t colh = col0 + 32 * h;
+                    uint32_t x[32];
+                    tmem_load_32x32b_x32(t_lane + c + 32 * h, x);
+                    // Issue the auxiliary loads before waiting for TMEM so their latency overlaps.
+                    const int valid = p.N - colh;  // columns of this half inside the matrix (a multiple of 4 or 8)
+                    const bool aux_live = row_live && first_split;
+                    uint4 rres[8];
+                    uint4 rgin[8];
+                    if (p.residual != nullptr) load_row_32(p.residual, out_base + colh, OUT_BF16, valid, aux_live, rres);
+                    if (p.activation == 2) load_row_32(p.gelu_input, out_base + colh, p.aux_bf16, valid, row_live, rgin);
+                    tmem_load_wait();
+
+                    float2 v[16];
+#pragma unroll
+                    for (int j = 0; j < 16; ++j) v[j] = make_float2(__uint_as_float(x[2 * j]), __uint_as_float(x[2 * j + 1]));
+                    if (p.scale != 1.0f) {
+#pragma unroll
+                        for (int j = 0; j < 16; ++j) v[j] = __fmul2_rn(f2(p.scale), v[j]);
+                    }
+                    if (p.bias != nullptr && first_split) {
+                        const float4* b4 = reinterpret_cast<const float4*>(p.bias + colh);
+#pragma unroll
+                        for (int j = 0; j < 8; ++j) {
+                            const float4 b = (4 * j < valid) ? __ldg(b4 + j) : make_float4(0.f, 0.f, 0.f, 0.f);
+                            v[2 * j] = __fadd2_rn(v[2 * j], make_float2(b.x, b.y));
+                            v[2 * j + 1] = __fadd2_rn(v[2 * j + 1], make_float2(b.z, b.w));
+                        }
+                    }
+                    if (p.has_pre) pack_pairs<OUT_BF16>(v, wp, h);
+                    if (p.activation == 1) {
+#pragma unroll
+                        for (int j = 0; j < 16; ++j) v[j] = gelu2<OUT_BF16>(v[j]);
+                    } else if (p.activation == 2) {
+                        float2 gi[16];
+                        unpack_row_32x2(rgin, p.aux_bf16, gi);
+#pragma unroll
+                        for (int j = 0; j < 16; ++j) v[j] = __fmul2_rn(v[j], gelu2_derivative<OUT_BF16>(gi[j]));
+                    }
+                    if (p.residual != nullptr && first_split) {
+                        float2 r[16];
+                        unpack_row_32x2(rres, OUT_BF16, r);
+#pragma unroll
+                        for (int j = 0; j < 16; ++j) v[j] = __fadd2_rn(v[j], r[j]);
+                    }
+                    pack_pairs<OUT_BF16>(v, w, h);
                 }
+
                 // Optional pre-activation output (the GELU forward keeps x for the backward pass); same type as C.
                 if (p.has_pre) {
-                    uint32_t w[32];
-                    pack_chunk<OUT_BF16, CHUNK>(x, w);
                     uint8_t* box = boxes + ebuf * TC_EPI_BOX_BYTES;
                     if (lane == 0) bulk_wait_group_read<1>();
                     __syncwarp();
-                    stage_row(box, lane, w);
+                    stage_row(box, lane, wp);
                     fence_proxy_async_shared();
                     __syncwarp();
                     if (lane == 0) {
@@ -340,26 +465,6 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
                     }
                     ebuf ^= 1;
                 }
-                if (p.activation == 1) {
-#pragma unroll
-                    for (int i = 0; i < CHUNK; ++i) x[i] = __float_as_uint(gelu_tanh(__uint_as_float(x[i])));
-                } else if (p.activation == 2) {
-#pragma unroll
-                    for (int i = 0; i < CHUNK; ++i) {
-                        const bool live = row_live && col0 + i < p.N;
-                        const float g = live ? load_elem(p.gelu_input, out_base + col0 + i, p.aux_bf16) : 0.0f;
-                        x[i] = __float_as_uint(__uint_as_float(x[i]) * gelu_tanh_derivative(g));
-                    }
-                }
-                if (p.residual != nullptr && first_split) {
-#pragma unroll
-                    for (int i = 0; i < CHUNK; ++i) {
-                        const bool live = row_live && col0 + i < p.N;
-                        if (live) x[i] = __float_as_uint(__uint_as_float(x[i]) + load_elem(p.residual, out_base + col0 + i, OUT_BF16));
-                    }
-                }
-                uint32_t w[32];
-                pack_chunk<OUT_BF16, CHUNK>(x, w);
                 uint8_t* box = boxes + ebuf * TC_EPI_BOX_BYTES;
                 if (lane == 0) bulk_wait_group_read<1>();
                 __syncwarp();

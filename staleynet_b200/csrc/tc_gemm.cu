@@ -93,7 +93,8 @@ bool encode_3d(CUtensorMap* map, CUtensorMapDataType dt, int esize, const void* 
 
 template <typename E, int BN, bool OUT_BF16>
 int launch(cudaStream_t stream, const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& tc,
-           const CUtensorMap& tp, const TcParams& p, int grid, std::string* err) {
+           const CUtensorMap& tp, const CUtensorMap& tr, const CUtensorMap& tg, const TcParams& p, int grid,
+           std::string* err) {
     constexpr int smem = TcConfig<BN>::SMEM_BYTES;
     static int configured_device = -1;
     static std::mutex mu;
@@ -112,7 +113,7 @@ int launch(cudaStream_t stream, const CUtensorMap& ta, const CUtensorMap& tb, co
             configured_device = dev;
         }
     }
-    tc_gemm_kernel<E, BN, OUT_BF16><<<grid, TC_THREADS, smem, stream>>>(ta, tb, tc, tp, p);
+    tc_gemm_kernel<E, BN, OUT_BF16><<<grid, TC_THREADS, smem, stream>>>(ta, tb, tc, tp, tr, tg, p);
     cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess) {
         *err = cuda_message("tc_gemm_kernel launch", e);
@@ -122,19 +123,18 @@ int launch(cudaStream_t stream, const CUtensorMap& ta, const CUtensorMap& tb, co
 }
 
 template <typename E, bool OUT_BF16>
-int launch_bn(int bn, cudaStream_t s, const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& tc,
-              const CUtensorMap& tp, const TcParams& p, int grid, std::string* err) {
+int launch_bn(int bn, cudaStream_t s, const CUtensorMap* maps, const TcParams& p, int grid, std::string* err) {
     switch (bn) {
-        case 64: return launch<E, 64, OUT_BF16>(s, ta, tb, tc, tp, p, grid, err);
-        case 128: return launch<E, 128, OUT_BF16>(s, ta, tb, tc, tp, p, grid, err);
-        default: return launch<E, 256, OUT_BF16>(s, ta, tb, tc, tp, p, grid, err);
+        case 64: return launch<E, 64, OUT_BF16>(s, maps[0], maps[1], maps[2], maps[3], maps[4], maps[5], p, grid, err);
+        case 128: return launch<E, 128, OUT_BF16>(s, maps[0], maps[1], maps[2], maps[3], maps[4], maps[5], p, grid, err);
+        default: return launch<E, 256, OUT_BF16>(s, maps[0], maps[1], maps[2], maps[3], maps[4], maps[5], p, grid, err);
     }
 }
 
-// K splits for a problem of `tiles` output tiles and `kb` K slices on `sms` SMs: minimises
-// ceil(tiles*s/sms) * ceil(kb/s), keeping at least 4 K slices per split.
+// K splits for a problem of `tiles` output tiles and `kb` K slices on `sms` SMs: minimises the critical path
+// ceil(tiles*s/sms) * ceil(kb/s) (waves times slices per unit), keeping at least 4 K slices per split.
 int choose_splits(int64_t tiles, int64_t kb, int sms) {
-    if (tiles >= sms || kb < 8) return 1;
+    if (kb < 8) return 1;
     int best = 1;
     int64_t best_cost = ((tiles + sms - 1) / sms) * kb;
     for (int s = 2; s <= 32; ++s) {
@@ -182,6 +182,14 @@ int tc_gemm_try(cudaStream_t stream, const GemmRequest& r, bool* launched, std::
     if (reinterpret_cast<uintptr_t>(r.C) % 16 != 0) return SNB_OK;
     if (r.pre && reinterpret_cast<uintptr_t>(r.pre) % 16 != 0) return SNB_OK;
     if (r.pre && r.aux_type != r.c_type) return SNB_OK;
+    // The epilogue reads bias, residual and GELU input with 16-byte vector loads: every row start must be
+    // 16-byte aligned.
+    const int aux_size = r.aux_type == SNB_TYPE_BF16 ? 2 : 4;
+    if (r.bias && reinterpret_cast<uintptr_t>(r.bias) % 16 != 0) return SNB_OK;
+    if (r.residual && reinterpret_cast<uintptr_t>(r.residual) % 16 != 0) return SNB_OK;
+    if (r.gelu_input && (reinterpret_cast<uintptr_t>(r.gelu_input) % 16 != 0 || (p.cols * aux_size) % 16 != 0 ||
+                         (r.count > 1 && (p.output_batch_stride * aux_size) % 16 != 0)))
+        return SNB_OK;
     const bool c_batched = r.count > 1;
     if (c_batched && ((p.output_batch_stride * csize) % 16 != 0 || p.output_batch_stride < p.rows * p.cols))
         return SNB_OK;
@@ -198,7 +206,8 @@ int tc_gemm_try(cudaStream_t stream, const GemmRequest& r, bool* launched, std::
     const int64_t kb_per_split = (k_blocks + splits - 1) / splits;
     const int64_t splits_used = (k_blocks + kb_per_split - 1) / kb_per_split;  // every split has >= 1 slice
 
-    CUtensorMap ta, tb, tc, tp;
+    CUtensorMap maps[6];
+    CUtensorMap &ta = maps[0], &tb = maps[1], &tc = maps[2], &tp = maps[3], &tr = maps[4], &tg = maps[5];
     const CUtensorMapDataType in_dt = bf16_in ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_TFLOAT32;
     const uint32_t mn_box = 128 / esize;
     // MN-major tf32 slices use 32-byte swizzle atoms (the only MN-major layout the tensor core reads for 32-bit
@@ -237,6 +246,21 @@ int tc_gemm_try(cudaStream_t stream, const GemmRequest& r, bool* launched, std::
     } else {
         tp = tc;
     }
+    // Residual and GELU-input maps serve only the L2 prefetch of each tile (box: the whole tile, no swizzle).
+    const uint32_t pf_cols = static_cast<uint32_t>(std::min(bn, 256));
+    tr = tc;
+    tg = tc;
+    if (r.residual &&
+        !encode_3d(&tr, out_dt, csize, r.residual, p.cols, p.rows, c_batched ? r.count : 1, p.cols, c_bstride,
+                   pf_cols, TC_BM, err, CU_TENSOR_MAP_SWIZZLE_NONE))
+        return SNB_OK;
+    if (r.activation == SNB_ACTIVATION_GELU_GRAD) {
+        const CUtensorMapDataType gdt =
+            r.aux_type == SNB_TYPE_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT32;
+        if (!encode_3d(&tg, gdt, aux_size, r.gelu_input, p.cols, p.rows, c_batched ? r.count : 1, p.cols, c_bstride,
+                       pf_cols, TC_BM, err, CU_TENSOR_MAP_SWIZZLE_NONE))
+            return SNB_OK;
+    }
 
     // An overwrite computed in several K splits reaches C by reduce-add, so C starts at zero.
     const bool reduce = p.accumulate != 0 || splits_used > 1;
@@ -266,6 +290,11 @@ int tc_gemm_try(cudaStream_t stream, const GemmRequest& r, bool* launched, std::
     kp.n_tiles = static_cast<int32_t>(n_tiles);
     kp.k_blocks = static_cast<int32_t>(k_blocks);
     kp.splits = static_cast<int32_t>(splits_used);
+    // Stream the larger operand once: with the N tile index fastest a wave shares A's rows and re-reads all of B
+    // per wave (right when B is small, e.g. weights); with M fastest it is the other way round.
+    const double a_bytes = static_cast<double>(p.rows) * p.inner;
+    const double b_bytes = static_cast<double>(p.cols) * p.inner;
+    kp.m_fastest = b_bytes > a_bytes ? 1 : 0;
     kp.k_blocks_per_split = static_cast<int32_t>(kb_per_split);
     const int64_t units = tiles * splits_used;
     if (units > (1ll << 31) - 1) return SNB_OK;
@@ -282,10 +311,10 @@ int tc_gemm_try(cudaStream_t stream, const GemmRequest& r, bool* launched, std::
 
     const int grid = static_cast<int>(std::min<int64_t>(units, dev.sm_count));
     if (bf16_in) {
-        rc = out_bf16 ? launch_bn<__nv_bfloat16, true>(bn, stream, ta, tb, tc, tp, kp, grid, err)
-                      : launch_bn<__nv_bfloat16, false>(bn, stream, ta, tb, tc, tp, kp, grid, err);
+        rc = out_bf16 ? launch_bn<__nv_bfloat16, true>(bn, stream, maps, kp, grid, err)
+                      : launch_bn<__nv_bfloat16, false>(bn, stream, maps, kp, grid, err);
     } else {
-        rc = launch_bn<float, false>(bn, stream, ta, tb, tc, tp, kp, grid, err);
+        rc = launch_bn<float, false>(bn, stream, maps, kp, grid, err);
     }
     if (rc == SNB_OK) *launched = true;
     return rc;
