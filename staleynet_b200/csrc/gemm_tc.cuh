@@ -2,16 +2,19 @@
 // batch, computing the same product as the reference's `matmul_*` kernels (crates/staleynet-cuda/src/kernels/
 // matmul.rs:216-448) with tcgen05 tensor cores.
 //
-// Structure (one persistent CTA of 256 threads per SM, work units strided over the grid):
+// Structure (one persistent CTA of 320 threads per SM, work units strided over the grid):
 //   warp 0     TMA producer: one elected thread streams 128-byte-wide K slices of A and B into a STAGES-deep
-//              shared-memory ring (128B swizzle), completion tracked by `full` mbarriers.
-//   warp 1     MMA issuer: one elected thread issues tcgen05.mma (M=128, N=BN, K=32 bytes per instruction) into
-//              one of two TMEM accumulators and frees ring slots with tcgen05.commit on `empty` mbarriers.
-//   warp 2     allocates / frees TMEM (2*BN columns).
-//   warps 4-7  epilogue: each warp owns 32 TMEM lanes (= 32 output rows); it loads 32 columns at a time
-//              (tcgen05.ld 32x32b.x32), applies scale / bias / GELU / residual, writes a swizzled 32x128-byte box to
-//              shared memory and stores it with a TMA store, or a TMA reduce-add when accumulating into C. The
-//              second accumulator lets the epilogue of one tile overlap the main loop of the next.
+//              shared-memory ring (128B swizzle), completion tracked by `full` mbarriers; it also prefetches each
+//              tile's epilogue inputs (residual, GELU input) into L2.
+//   warp 1     allocates / frees TMEM (2*BN columns); one elected thread issues tcgen05.mma (M=128, N=BN,
+//              K=32 bytes per instruction) into one of two TMEM accumulators and frees ring slots with
+//              tcgen05.commit on `empty` mbarriers.
+//   warps 2-9  epilogue: a warp may read the 32 TMEM lanes of its quadrant (warp % 4) = 32 output rows; the two
+//              warps of a quadrant take alternate 128-byte column chunks. Per chunk a warp loads 32 columns at a
+//              time (tcgen05.ld 32x32b.x32), applies scale / bias / GELU / residual, writes a swizzled 32x128-byte
+//              box to shared memory and stores it with a TMA store, or a TMA reduce-add when accumulating into C.
+//              The second accumulator lets the epilogue of one tile overlap the main loop of the next; eight
+//              warps (two per scheduler) hide the latency of TMEM and global loads.
 //
 // Operand layouts: each operand is either K-major (K contiguous) or MN-major (M or N contiguous); both are loaded
 // by TMA in their stored order and described to the tensor core by the major bits of the instruction descriptor,
@@ -32,8 +35,9 @@
 namespace snb {
 
 constexpr int TC_BM = 128;
-constexpr int TC_THREADS = 256;
-constexpr int TC_EPI_WARP0 = 4;
+constexpr int TC_EPI_WARP0 = 2;   // warps 2..9 drain the accumulator
+constexpr int TC_EPI_WARPS = 8;   // two per TMEM lane quadrant, splitting the tile's columns
+constexpr int TC_THREADS = 32 * (TC_EPI_WARP0 + TC_EPI_WARPS);
 constexpr int TC_EPI_BOX_BYTES = 32 * 128;  // one staged output box: 32 rows x 128 bytes
 
 struct TcParams {
@@ -66,7 +70,7 @@ struct TcConfig {
     static constexpr int STAGE_B = BN * 128;
     static constexpr int STAGE = STAGE_A + STAGE_B;
     static constexpr int STAGES = BN == 256 ? 4 : (BN == 128 ? 6 : 8);
-    static constexpr int EPI_BYTES = 4 * 2 * TC_EPI_BOX_BYTES;
+    static constexpr int EPI_BYTES = TC_EPI_WARPS * TC_EPI_BOX_BYTES;  // one staging box per epilogue warp
     static constexpr int TMEM_COLS = 2 * BN;
     static constexpr int BARRIER_BYTES = 256;
     static constexpr int SMEM_BYTES = 1024 + STAGES * STAGE + EPI_BYTES + BARRIER_BYTES;
@@ -195,30 +199,79 @@ __device__ __forceinline__ void unpack_row_32x2(const uint4 (&r)[8], int is_bf16
     }
 }
 
-// Packs 16 pairs into this lane's box row: f32 fills words [0, 32); bf16 fills words [16h, 16h + 16) of a
-// 64-column chunk.
+// Writes 32 values (one tcgen05.ld of a lane) into this lane's row of the 128B-swizzled staging box: f32 fills
+// 16-byte chunks [0, 8) (a 32-column box), bf16 fills chunks [4h, 4h + 4) of a 64-column box. Chunk j of row r
+// sits at position j ^ (r % 8), the layout a SWIZZLE_128B tensor map expects.
 template <bool OUT_BF16>
-__device__ __forceinline__ void pack_pairs(const float2 (&v)[16], uint32_t (&w)[32], int h) {
+__device__ __forceinline__ void stage_half(uint8_t* box, int lane, int h, const float2 (&v)[16]) {
+    uint8_t* row = box + lane * 128;
     if constexpr (OUT_BF16) {
 #pragma unroll
-        for (int j = 0; j < 16; ++j) w[16 * h + j] = pack_bf16x2(v[j].x, v[j].y);
+        for (int j = 0; j < 4; ++j) {
+            const uint4 q4 = make_uint4(pack_bf16x2(v[4 * j].x, v[4 * j].y), pack_bf16x2(v[4 * j + 1].x, v[4 * j + 1].y),
+                                        pack_bf16x2(v[4 * j + 2].x, v[4 * j + 2].y),
+                                        pack_bf16x2(v[4 * j + 3].x, v[4 * j + 3].y));
+            *reinterpret_cast<uint4*>(row + (((4 * h + j) ^ (lane & 7)) << 4)) = q4;
+        }
     } else {
 #pragma unroll
-        for (int j = 0; j < 16; ++j) {
-            w[2 * j] = __float_as_uint(v[j].x);
-            w[2 * j + 1] = __float_as_uint(v[j].y);
+        for (int j = 0; j < 8; ++j) {
+            const uint4 q4 = make_uint4(__float_as_uint(v[2 * j].x), __float_as_uint(v[2 * j].y),
+                                        __float_as_uint(v[2 * j + 1].x), __float_as_uint(v[2 * j + 1].y));
+            *reinterpret_cast<uint4*>(row + ((j ^ (lane & 7)) << 4)) = q4;
         }
     }
 }
 
-// Writes 32 rows x 128 bytes (this lane's row = `lane`) into a 128B-swizzled staging box: 16-byte chunk j of row r
-// goes to chunk position j ^ (r % 8), the layout a SWIZZLE_128B tensor map expects.
-__device__ __forceinline__ void stage_row(uint8_t* box, int lane, const uint32_t (&w)[32]) {
-    uint8_t* row = box + lane * 128;
+// The epilogue function for 32 columns [col, col + 32) of one output row, starting from the TMEM accumulator:
+//   x = scale * acc + bias;  pre_only: return x;  y = activation(x) (+ residual).
+// The first auxiliary input (GELU input, else residual) is requested before waiting for TMEM so the two latencies
+// overlap; only when both are present is the residual read afterwards.
+template <bool OUT_BF16>
+__device__ __forceinline__ void epilogue_half(const TcParams& p, uint32_t taddr, int32_t col, int32_t row,
+                                              int64_t out_base, bool first_split, bool pre_only, float2 (&v)[16]) {
+    uint32_t x[32];
+    tmem_load_32x32b_x32(taddr, x);
+    const int valid = p.N - col;  // columns of this piece inside the matrix (a multiple of 4 or 8)
+    const bool row_live = row < p.M;
+    const bool want_gin = !pre_only && p.activation == 2;
+    const bool want_res = !pre_only && p.residual != nullptr && first_split;
+    uint4 raux[8];
+    if (want_gin) load_row_32(p.gelu_input, out_base + col, p.aux_bf16, valid, row_live, raux);
+    else if (want_res) load_row_32(p.residual, out_base + col, OUT_BF16, valid, row_live, raux);
+    tmem_load_wait();
+
 #pragma unroll
-    for (int j = 0; j < 8; ++j) {
-        uint4 v = make_uint4(w[4 * j], w[4 * j + 1], w[4 * j + 2], w[4 * j + 3]);
-        *reinterpret_cast<uint4*>(row + ((j ^ (lane & 7)) << 4)) = v;
+    for (int j = 0; j < 16; ++j) v[j] = make_float2(__uint_as_float(x[2 * j]), __uint_as_float(x[2 * j + 1]));
+    if (p.scale != 1.0f) {
+#pragma unroll
+        for (int j = 0; j < 16; ++j) v[j] = __fmul2_rn(f2(p.scale), v[j]);
+    }
+    if (p.bias != nullptr && first_split) {
+        const float4* b4 = reinterpret_cast<const float4*>(p.bias + col);
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+            const float4 b = (4 * j < valid) ? __ldg(b4 + j) : make_float4(0.f, 0.f, 0.f, 0.f);
+            v[2 * j] = __fadd2_rn(v[2 * j], make_float2(b.x, b.y));
+            v[2 * j + 1] = __fadd2_rn(v[2 * j + 1], make_float2(b.z, b.w));
+        }
+    }
+    if (pre_only) return;
+    if (p.activation == 1) {
+#pragma unroll
+        for (int j = 0; j < 16; ++j) v[j] = gelu2<OUT_BF16>(v[j]);
+    } else if (p.activation == 2) {
+        float2 gi[16];
+        unpack_row_32x2(raux, p.aux_bf16, gi);
+#pragma unroll
+        for (int j = 0; j < 16; ++j) v[j] = __fmul2_rn(v[j], gelu2_derivative<OUT_BF16>(gi[j]));
+        if (want_res) load_row_32(p.residual, out_base + col, OUT_BF16, valid, row_live, raux);
+    }
+    if (want_res) {
+        float2 r[16];
+        unpack_row_32x2(raux, OUT_BF16, r);
+#pragma unroll
+        for (int j = 0; j < 16; ++j) v[j] = __fadd2_rn(v[j], r[j]);
     }
 }
 
@@ -259,7 +312,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
         }
         for (int a = 0; a < 2; ++a) {
             mbar_init(smem_addr(&acc_full[a]), 1);
-            mbar_init(smem_addr(&acc_empty[a]), 4);  // one arrival per epilogue warp
+            mbar_init(smem_addr(&acc_empty[a]), TC_EPI_WARPS);  // one arrival per epilogue warp
         }
         mbar_init(smem_addr(drain), 1);
         fence_mbarrier_init();
@@ -270,7 +323,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
         tma_prefetch_descriptor(&tm_b);
         tma_prefetch_descriptor(&tm_c);
     }
-    if (warp == 2) {
+    if (warp == 1) {
         tmem_alloc(smem_addr(tmem_slot), Cfg::TMEM_COLS);
         tmem_relinquish_alloc_permit();
     }
@@ -379,9 +432,11 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
         __syncwarp();
     } else if (warp >= TC_EPI_WARP0) {
         // ------------------------------------------------------------------ epilogue
-        const int q = warp - TC_EPI_WARP0;  // TMEM lane quadrant = warp % 4
-        uint8_t* boxes = epi + q * 2 * TC_EPI_BOX_BYTES;
-        int ebuf = 0;
+        // A warp may read only the TMEM lanes of its quadrant (warp % 4): 32 output rows. The two warps of a
+        // quadrant take alternate chunks of the tile's columns.
+        const int q = warp & 3;
+        const int group = (warp - TC_EPI_WARP0) >> 2;
+        uint8_t* box = epi + (warp - TC_EPI_WARP0) * TC_EPI_BOX_BYTES;
         int iter = 0;
         for (int32_t unit = blockIdx.x; unit < p.num_units; unit += gridDim.x, ++iter) {
             const TcUnit u = tc_decode_unit(p, unit, BN);
@@ -396,87 +451,29 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
                 static_cast<int64_t>(u.batch) * p.out_batch_stride + static_cast<int64_t>(row) * p.N;
             const uint32_t t_lane = tmem_base + (static_cast<uint32_t>(q * 32) << 16) + acc * BN;
 
-            for (int c = 0; c < BN && row0 < p.M && u.n0 + c < p.N; c += CHUNK) {
+            for (int c = group * CHUNK; c < BN && row0 < p.M && u.n0 + c < p.N; c += 2 * CHUNK) {
                 const int32_t col0 = u.n0 + c;
-                const bool row_live = row < p.M;
-                uint32_t w[32];   // this lane's 128-byte row of the output box
-                uint32_t wp[32];  // ... and of the pre-activation box
-                // The chunk is processed 32 columns at a time (one tcgen05.ld); a bf16 chunk has two such halves.
-#pragma unroll
-                for (int h = 0; h < CHUNK / 32; ++h) {
-                    const int32_t colh = col0 + 32 * h;
-                    uint32_t x[32];
-                    tmem_load_32x32b_x32(t_lane + c + 32 * h, x);
-                    // Issue the auxiliary loads before waiting for TMEM so their latency overlaps.
-                    const int valid = p.N - colh;  // columns of this half inside the matrix (a multiple of 4 or 8)
-                    const bool aux_live = row_live && first_split;
-                    uint4 rres[8];
-                    uint4 rgin[8];
-                    if (p.residual != nullptr) load_row_32(p.residual, out_base + colh, OUT_BF16, valid, aux_live, rres);
-                    if (p.activation == 2) load_row_32(p.gelu_input, out_base + colh, p.aux_bf16, valid, row_live, rgin);
-                    tmem_load_wait();
-
-                    float2 v[16];
-#pragma unroll
-                    for (int j = 0; j < 16; ++j) v[j] = make_float2(__uint_as_float(x[2 * j]), __uint_as_float(x[2 * j + 1]));
-                    if (p.scale != 1.0f) {
-#pragma unroll
-                        for (int j = 0; j < 16; ++j) v[j] = __fmul2_rn(f2(p.scale), v[j]);
-                    }
-                    if (p.bias != nullptr && first_split) {
-                        const float4* b4 = reinterpret_cast<const float4*>(p.bias + colh);
-#pragma unroll
-                        for (int j = 0; j < 8; ++j) {
-                            const float4 b = (4 * j < valid) ? __ldg(b4 + j) : make_float4(0.f, 0.f, 0.f, 0.f);
-                            v[2 * j] = __fadd2_rn(v[2 * j], make_float2(b.x, b.y));
-                            v[2 * j + 1] = __fadd2_rn(v[2 * j + 1], make_float2(b.z, b.w));
-                        }
-                    }
-                    if (p.has_pre) pack_pairs<OUT_BF16>(v, wp, h);
-                    if (p.activation == 1) {
-#pragma unroll
-                        for (int j = 0; j < 16; ++j) v[j] = gelu2<OUT_BF16>(v[j]);
-                    } else if (p.activation == 2) {
-                        float2 gi[16];
-                        unpack_row_32x2(rgin, p.aux_bf16, gi);
-#pragma unroll
-                        for (int j = 0; j < 16; ++j) v[j] = __fmul2_rn(v[j], gelu2_derivative<OUT_BF16>(gi[j]));
-                    }
-                    if (p.residual != nullptr && first_split) {
-                        float2 r[16];
-                        unpack_row_32x2(rres, OUT_BF16, r);
-#pragma unroll
-                        for (int j = 0; j < 16; ++j) v[j] = __fadd2_rn(v[j], r[j]);
-                    }
-                    pack_pairs<OUT_BF16>(v, w, h);
-                }
-
-                // Optional pre-activation output (the GELU forward keeps x for the backward pass); same type as C.
-                if (p.has_pre) {
-                    uint8_t* box = boxes + ebuf * TC_EPI_BOX_BYTES;
-                    if (lane == 0) bulk_wait_group_read<1>();
+                // Pass 0 writes the pre-activation box (GELU forward with pre_activation), pass 1 the output box;
+                // pass 0 re-reads nothing but TMEM, so no row of values is held across passes.
+                for (int pass = p.has_pre ? 0 : 1; pass < 2; ++pass) {
+                    if (lane == 0) bulk_wait_group_read<0>();  // the box's previous TMA store has read it
                     __syncwarp();
-                    stage_row(box, lane, wp);
+#pragma unroll
+                    for (int h = 0; h < CHUNK / 32; ++h) {
+                        float2 v[16];
+                        epilogue_half<OUT_BF16>(p, t_lane + c + 32 * h, col0 + 32 * h, row, out_base, first_split,
+                                                pass == 0, v);
+                        stage_half<OUT_BF16>(box, lane, h, v);
+                    }
                     fence_proxy_async_shared();
                     __syncwarp();
                     if (lane == 0) {
-                        tma_store_3d(&tm_pre, smem_addr(box), col0, row0, u.batch);
+                        if (pass == 0) tma_store_3d(&tm_pre, smem_addr(box), col0, row0, u.batch);
+                        else if (p.reduce) tma_reduce_add_3d(&tm_c, smem_addr(box), col0, row0, u.batch);
+                        else tma_store_3d(&tm_c, smem_addr(box), col0, row0, u.batch);
                         bulk_commit_group();
                     }
-                    ebuf ^= 1;
                 }
-                uint8_t* box = boxes + ebuf * TC_EPI_BOX_BYTES;
-                if (lane == 0) bulk_wait_group_read<1>();
-                __syncwarp();
-                stage_row(box, lane, w);
-                fence_proxy_async_shared();
-                __syncwarp();
-                if (lane == 0) {
-                    if (p.reduce) tma_reduce_add_3d(&tm_c, smem_addr(box), col0, row0, u.batch);
-                    else tma_store_3d(&tm_c, smem_addr(box), col0, row0, u.batch);
-                    bulk_commit_group();
-                }
-                ebuf ^= 1;
             }
             tcgen05_fence_before_sync();
             __syncwarp();
@@ -488,7 +485,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
 
     tcgen05_fence_before_sync();
     __syncthreads();
-    if (warp == 2) {
+    if (warp == 1) {
         tcgen05_fence_after_sync();
         tmem_dealloc(tmem_base, Cfg::TMEM_COLS);
     }

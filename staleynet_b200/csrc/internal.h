@@ -5,7 +5,7 @@
 #include <cstdint>
 #include <string>
 
-#include "../../include/snb_matmul.h"
+#include "snb_matmul.h"
 
 namespace snb {
 
