@@ -44,6 +44,17 @@ def load_peaks():
     return dict(FALLBACK_PEAKS), "fallback"
 
 
+def load_traffic(shape) -> dict:
+    """Per-launch DRAM traffic of the step's GEMM launches, summarised from an ncu capture of this workload
+    (profiles/tc_gemm_cfg3_step_launches.json); empty when the workload differs or no capture is committed."""
+    path = ROOT / "profiles" / "tc_gemm_cfg3_step_launches.json"
+    from staleynet_b200.step import ModelShape
+
+    if shape != ModelShape() or not path.exists():
+        return {}
+    return json.loads(path.read_text())
+
+
 def workload_config(shape, n_gpus: int) -> dict:
     return {
         "workload": "cfg3 12-block width-768 decoder: linear + 16x1024 codebook-head GEMMs, fwd+dX+dW, "
@@ -196,33 +207,29 @@ def run_ours(args, shape, rank: int, world: int, local_rank: int) -> int:
     import torch
     import torch.distributed as dist
 
+    from staleynet_b200.data_parallel import OverlappedAllReduce
     from staleynet_b200.step import TrainingStepGemms
 
     torch.cuda.set_device(local_rank)
     device = torch.device("cuda", local_rank)
     stream = torch.cuda.current_stream(device)
-    comm = torch.cuda.Stream(device) if world > 1 else None
     step = TrainingStepGemms(shape, device, seed=1234 + rank)
     handle = stream.cuda_stream
 
+    reducer = OverlappedAllReduce(compute_stream=stream) if world > 1 else None
+
     def one_step(events=None):
-        works = []
         step.zero_grads()
 
         def on_block(b):
-            ev = torch.cuda.Event()
-            ev.record(stream)
-            with torch.cuda.stream(comm):
-                comm.wait_event(ev)
-                bufs = [step.block_grad_flat[b]]
-                if b == shape.blocks - 1:
-                    bufs.append(step.head_grad)
-                for t in bufs:
-                    works.append(dist.all_reduce(t, async_op=True))
+            # The head's gradient is complete before block L-1's; both go out once block L-1's backward is queued.
+            if b == shape.blocks - 1:
+                reducer.submit(step.head_grad)
+            reducer.submit(step.block_grad_flat[b])
 
         step.run(handle, on_block_done=on_block if world > 1 else None, events=events)
-        for wk in works:
-            wk.wait()
+        if reducer is not None:
+            reducer.wait()
 
     # Warm-up (also configures every kernel variant and builds the NCCL communicator).
     for _ in range(args.warmup):
@@ -296,6 +303,7 @@ def run_ours(args, shape, rank: int, world: int, local_rank: int) -> int:
 
     if rank == 0:
         peaks, source = load_peaks()
+        traffic = load_traffic(shape)
         flops_step = step.plan_flops
         ms_step = ms_total / args.steps
         value = flops_step * world * args.steps / (ms_total / 1e3) / 1e12
@@ -313,7 +321,12 @@ def run_ours(args, shape, rank: int, world: int, local_rank: int) -> int:
             "pct_bf16_peak_burst": 100.0 * (value / world) / peak_burst,
             "roofline": {
                 "bound": "tensor", "achieved": achieved, "peak": peak_sus, "unit": "TFLOP/s",
-                "frac": achieved / peak_sus, "traffic": None,
+                "frac": achieved / peak_sus, "traffic": traffic.get("traffic_bytes_per_launch"),
+                "traffic_source": traffic.get("source"),
+                "algorithmic_bytes_per_launch": traffic.get("algorithmic_bytes_per_launch"),
+                "achieved_hbm_gbs": (traffic["algorithmic_bytes_per_launch"] * n_launch * args.steps /
+                                     (kernel_ms / 1e3) / 1e9) if "algorithmic_bytes_per_launch" in traffic else None,
+                "hbm_peak_gbs": float(peaks.get("hbm_gbs", FALLBACK_PEAKS["hbm_gbs"])),
                 "kernel": "snb::tc_gemm_kernel (all launches of one step on rank 0)",
                 "peak_source": f"{source} bf16_tflops_sustained (kernel timed inside a long step); "
                                f"burst {peak_burst}",

@@ -24,6 +24,7 @@ import ctypes
 from dataclasses import dataclass
 
 from . import _ffi
+from .data_parallel import GradientBuckets
 from .matmul import MatmulSpec, check
 
 
@@ -86,18 +87,13 @@ class TrainingStepGemms:
         # Weight gradients of one block are views of one flat f32 buffer, so the data-parallel step all-reduces a
         # block with one collective.
         sizes = [i * o for _, i, o in linear_shapes(s)]
-        self.block_grad_flat = []
-        for _ in range(s.blocks):
-            flat = torch.zeros(sum(sizes), device=device, dtype=f32)
-            self.block_grad_flat.append(flat)
-            views, off = {}, 0
-            for (name, _, _), n in zip(linear_shapes(s), sizes):
-                views[name] = flat[off:off + n]
-                off += n
-            self.weight_grads.append(views)
+        self.grads = GradientBuckets([sizes] * s.blocks, w * V, device, f32)
+        self.block_grad_flat = self.grads.flat
+        for b in range(s.blocks):
+            self.weight_grads.append({name: view for (name, _, _), view in zip(linear_shapes(s), self.grads.views[b])})
         self.head_w = normal(w * V, wstd)
         self.head_b = torch.zeros(V, device=device, dtype=f32)
-        self.head_grad = torch.zeros(w * V, device=device, dtype=f32)
+        self.head_grad = self.grads.head
 
         # Activations kept per block, as a training step keeps them for the backward pass.
         self.x_in = normal(T * w, 1.0)  # the step's input activations (uploaded per step in the end-to-end run)
@@ -231,6 +227,4 @@ class TrainingStepGemms:
                 on_block_done(ends[i + 1 - nfwd])
 
     def zero_grads(self) -> None:
-        for flat in self.block_grad_flat:
-            flat.zero_()
-        self.head_grad.zero_()
+        self.grads.zero_()
