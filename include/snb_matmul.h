@@ -169,6 +169,13 @@ SNB_API int snb_last_path(void);
  * read completed, else SNB_ERR_DEVICE_TIMEOUT. Synchronizes the device. */
 SNB_API int snb_device_status(void);
 
+/* Failure-detection self-test: launches a one-thread kernel that waits on an mbarrier nothing completes, through
+ * the bounded wait every tensor-core pipeline wait uses. The wait gives up after limit_ns (at most 1 s), records a
+ * timeout in the device status word and the kernel returns normally; a following snb_device_status() reports
+ * SNB_ERR_DEVICE_TIMEOUT and the context stays usable. No reference counterpart (the reference's kernels have no
+ * bounded waits). */
+SNB_API int snb_selftest_bounded_wait(void* stream, uint64_t limit_ns);
+
 /* Version of this ABI (major*100 + minor). */
 SNB_API int snb_abi_version(void);
 

@@ -47,6 +47,7 @@ EXPORTED_SYMBOLS = (
     "snb_last_error",
     "snb_last_path",
     "snb_device_status",
+    "snb_selftest_bounded_wait",
     "snb_abi_version",
 )
 
@@ -127,6 +128,8 @@ def load() -> ctypes.CDLL:
         lib.snb_last_path.restype = c_int
         lib.snb_device_status.argtypes = []
         lib.snb_device_status.restype = c_int
+        lib.snb_selftest_bounded_wait.argtypes = [c_void_p, c_uint64]
+        lib.snb_selftest_bounded_wait.restype = c_int
         lib.snb_abi_version.argtypes = []
         lib.snb_abi_version.restype = c_int
         _lib = lib

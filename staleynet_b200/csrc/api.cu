@@ -204,6 +204,14 @@ int snb_softmax_backward(void* stream, const float* probabilities, float* grad, 
     return rc == SNB_OK ? rc : fail(rc, err);
 }
 
+int snb_selftest_bounded_wait(void* stream, uint64_t limit_ns) {
+    if (limit_ns == 0 || limit_ns > 1000000000ull)
+        return fail(SNB_ERR_INVALID_ARGUMENT, "selftest: limit_ns must lie in (0, 1 s]");
+    std::string err;
+    int rc = bounded_wait_probe(static_cast<cudaStream_t>(stream), limit_ns, &err);
+    return rc == SNB_OK ? rc : fail(rc, err);
+}
+
 int snb_device_status(void) {
     unsigned int status = 0;
     std::string err;

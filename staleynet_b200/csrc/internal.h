@@ -47,6 +47,9 @@ int causal_softmax(cudaStream_t stream, float* scores, uint64_t rows, uint64_t q
 int softmax_backward(cudaStream_t stream, const float* probabilities, float* grad, uint64_t rows, uint64_t cols,
                      std::string* err);
 
+// Launches a one-thread kernel whose mbarrier wait nothing completes; it gives up after limit_ns.
+int bounded_wait_probe(cudaStream_t stream, uint64_t limit_ns, std::string* err);
+
 // Reads and clears the tensor-core kernels' device status word on the current device (synchronizes first).
 int read_and_clear_device_status(unsigned int* status, std::string* err);
 

@@ -71,13 +71,13 @@ __device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
 }
 
 // Waits until the phase with the given parity has completed. Returns false (and flags the device status) if it
-// did not complete within SNB_WAIT_LIMIT_NS.
-__device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity) {
+// did not complete within `limit_ns` of global time (default SNB_WAIT_LIMIT_NS).
+__device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, uint64_t limit_ns = SNB_WAIT_LIMIT_NS) {
     if (mbar_try_wait(bar, parity)) return true;
     const uint64_t start = global_timer_ns();
     while (true) {
         if (mbar_try_wait(bar, parity)) return true;
-        if (global_timer_ns() - start > SNB_WAIT_LIMIT_NS) {
+        if (global_timer_ns() - start > limit_ns) {
             atomicOr(&g_device_status, SNB_DEVICE_TIMEOUT);
             return false;
         }

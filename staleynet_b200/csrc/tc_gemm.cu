@@ -320,6 +320,30 @@ int tc_gemm_try(cudaStream_t stream, const GemmRequest& r, bool* launched, std::
     return rc;
 }
 
+namespace {
+
+// Waits on an mbarrier that nothing ever completes, through the same bounded wait the GEMM pipeline uses: the wait
+// must give up after `limit_ns`, flag the device status and let the kernel return normally.
+__global__ void bounded_wait_probe_kernel(uint64_t limit_ns) {
+    __shared__ uint64_t bar;
+    if (threadIdx.x != 0) return;
+    mbar_init(smem_addr(&bar), 1);
+    fence_mbarrier_init();
+    mbar_wait(smem_addr(&bar), 0, limit_ns);
+}
+
+}  // namespace
+
+int bounded_wait_probe(cudaStream_t stream, uint64_t limit_ns, std::string* err) {
+    bounded_wait_probe_kernel<<<1, 32, 0, stream>>>(limit_ns);
+    cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess) {
+        *err = cuda_message("bounded_wait_probe_kernel launch", e);
+        return SNB_ERR_CUDA;
+    }
+    return SNB_OK;
+}
+
 int read_and_clear_device_status(unsigned int* status, std::string* err) {
     cudaError_t e = cudaDeviceSynchronize();
     if (e != cudaSuccess) {

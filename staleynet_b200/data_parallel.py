@@ -117,3 +117,33 @@ class OverlappedAllReduce:
         for w in self.works:
             w.wait()
         self.works = []
+
+
+class PeerLost(RuntimeError):
+    """A peer rank did not reach the next step within the heartbeat timeout."""
+
+
+class StepHeartbeat:
+    """Host-side liveness check between steps. Before issuing any collective of step k a rank posts
+    `ready/<rank>/<k>` to a key-value store and waits, bounded, for every peer's post; a rank that has left (between
+    steps, with none of its kernels or collectives in flight) is detected here, on the host, before the survivors
+    launch work that would wait on it."""
+
+    def __init__(self, store, rank: int, world: int, timeout_s: float = 10.0):
+        self.store = store
+        self.rank = rank
+        self.world = world
+        self.timeout_s = timeout_s
+
+    def ready(self, step: int) -> None:
+        import datetime
+
+        self.store.set(f"snb/ready/{self.rank}/{step}", "1")
+        keys = [f"snb/ready/{r}/{step}" for r in range(self.world) if r != self.rank]
+        if not keys:
+            return
+        try:
+            self.store.wait(keys, datetime.timedelta(seconds=self.timeout_s))
+        except Exception as e:  # the store raises its own timeout error type
+            missing = [k for k in keys if not self.store.check([k])]
+            raise PeerLost(f"step {step}: no heartbeat from {missing} within {self.timeout_s} s") from e

@@ -68,19 +68,23 @@ def gradient_parity(rank, world, port, result_queue):
         dist.destroy_process_group()
 
 
-def dead_peer(rank, world, port, result_queue):
-    """Rank 1 leaves between steps without joining the next collective; rank 0's all-reduce must end with an error
-    once the process-group timeout passes, not wait forever."""
-    import torch
+def heartbeat_detects_a_departed_rank(rank, world, port, result_queue):
+    """Step 0 completes on both ranks; rank 1 leaves; rank 0 learns of it from the store before launching step 1."""
+    import datetime
+
     import torch.distributed as dist
 
-    _init(rank, world, port, timeout_s=3)
+    from staleynet_b200.data_parallel import PeerLost, StepHeartbeat
+
+    store = dist.TCPStore("127.0.0.1", port, world, is_master=(rank == 0), timeout=datetime.timedelta(seconds=30))
+    hb = StepHeartbeat(store, rank, world, timeout_s=2.0)
+    hb.ready(0)
     if rank == 1:
         os._exit(0)
-    t = torch.ones(8)
     try:
-        dist.all_reduce(t)
+        hb.ready(1)
         result_queue.put(("no error", None))
-    except Exception as e:  # noqa: BLE001
-        result_queue.put(("error", type(e).__name__))
-    os._exit(0)
+    except PeerLost as e:
+        result_queue.put(("peer lost", str(e)))
+    result_queue.close()
+    result_queue.join_thread()  # deliver the result before this process ends

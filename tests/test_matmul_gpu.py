@@ -295,3 +295,23 @@ def test_undersized_operands_raise_like_the_reference(gpu):
     with pytest.raises(OperandTooSmall, match="left operand too small"):
         gpu.matmul(MatmulSpec.new(4, 5, 6), a, b, c)
     gpu.device_status()
+
+
+def test_bounded_wait_gives_up_and_the_context_stays_usable(gpu):
+    """Failure detection on the device: a wait that nothing completes returns after its limit with an error status
+    the host reads, instead of hanging; the next product still runs correctly."""
+    import ctypes
+
+    lib = _ffi.load()
+    handle = ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)
+    gpu.device_status()  # start clean
+    assert lib.snb_selftest_bounded_wait(handle, 20_000_000) == _ffi.OK
+    assert lib.snb_device_status() == _ffi.ERR_DEVICE_TIMEOUT
+    assert lib.snb_device_status() == _ffi.OK  # reading clears it
+    spec = MatmulSpec.new(128, 256, 64)
+    left, right = o.lcg_values(128 * 64, 1), o.lcg_values(64 * 256, 2)
+    zero = np.zeros(128 * 256, np.float32)
+    actual, path = run_on_gpu(gpu, MatmulKernel.TENSOR_CORE, spec, left, right, zero)
+    assert path == _ffi.PATH_TENSOR_CORE
+    assert o.relative_error(expected_product(spec, left, right, zero), actual) < MatmulKernel.TENSOR_CORE.tolerance()
+    gpu.device_status()
