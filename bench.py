@@ -345,6 +345,106 @@ def run_ours(args, shape, rank: int, world: int, local_rank: int) -> int:
     return 0
 
 
+def attention_cpu_baseline(s, budget_flops: float = 10e9, threads: int = 0) -> dict:
+    """The oracle's reference loop on a sample of rows of each of the six attention products (dense, as the
+    reference's CPU matmul computes them), extrapolated by rows; softmax passes are not timed (elementwise)."""
+    import numpy as np
+
+    from oracle import oracle as o
+
+    S, d, n = s.time, s.head_dim, s.count
+    total_dense = 6 * 2.0 * S * S * d * n
+    frac = min(1.0, budget_flops / total_dense)
+    products = [(S, S, d, False, True), (S, d, S, False, False), (S, S, d, False, True), (S, d, S, True, False),
+                (S, d, S, False, False), (S, d, S, True, False)]
+    seconds = 0.0
+    used = 1
+    for M, N, K, lt, rt in products:
+        rows = max(1, int(round(frac * M)))
+        left = np.zeros(M * K, np.float32)
+        right = np.zeros(K * N, np.float32)
+        out = np.zeros(rows * N, np.float32)
+        p = o.product(rows, N, K, o.storage_strides(lt, M, K, 0), o.storage_strides(rt, K, N, 0), 0)
+        o.matmul_rows(p, 1, left, right, out, 0, rows, threads)
+        t0 = time.perf_counter()
+        used = o.matmul_rows(p, 1, left, right, out, 0, rows, threads)
+        seconds += (time.perf_counter() - t0) * (M / rows) * n
+    causal_flops = 6 * 2.0 * s.head_dim * sum(min(q + 1, S) for q in range(S)) * n
+    return {"value": causal_flops / seconds / 1e12, "unit": UNIT, "cores": used, "kind": "port",
+            "sample": f"{frac:.1e} of the rows of each of the six products of one head (dense f32 loop), "
+                      f"extrapolated by rows and heads; softmax passes not included"}
+
+
+def run_attention(args, rank: int, world: int, local_rank: int) -> int:
+    """the six batched causal attention products with the fp32 causal softmax (and its
+    backward) between them; one forward + backward per step."""
+    import torch
+
+    from staleynet_b200.attention import AttentionProducts, AttentionShape
+
+    torch.cuda.set_device(local_rank)
+    device = torch.device("cuda", local_rank)
+    stream = torch.cuda.current_stream(device)
+    shape = AttentionShape()
+    att = AttentionProducts(shape, device, seed=rank)
+    h = stream.cuda_stream
+    for _ in range(args.warmup):
+        att.forward(h)
+        att.backward(h)
+    torch.cuda.synchronize()
+    clocks = ClockSampler(local_rank)
+    clocks.start()
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    start.record(stream)
+    for _ in range(args.steps):
+        att.forward(h)
+        att.backward(h)
+    end.record(stream)
+    torch.cuda.synchronize()
+    clock_info = clocks.stop()
+    ms = start.elapsed_time(end)
+    host = [torch.empty(t.numel(), dtype=t.dtype, pin_memory=True) for t in (att.q, att.k, att.v, att.d_out)]
+    for hb, t in zip(host, (att.q, att.k, att.v, att.d_out)):
+        hb.copy_(t.cpu())
+    host_out = torch.empty(1, dtype=torch.float32, pin_memory=True)
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(args.steps):
+        for hb, t in zip(host, (att.q, att.k, att.v, att.d_out)):
+            t.copy_(hb, non_blocking=True)
+        att.forward(h)
+        att.backward(h)
+        host_out.copy_(att.dq[:1], non_blocking=True)
+    e1.record(stream)
+    torch.cuda.synchronize()
+    e2e_ms = e0.elapsed_time(e1)
+    if rank != 0:
+        return 0
+    peaks, source = load_peaks()
+    hbm = float(peaks.get("hbm_gbs", FALLBACK_PEAKS["hbm_gbs"]))
+    sec = ms / 1e3 / args.steps
+    achieved_gbs = att.bytes / sec / 1e9
+    line = {
+        "metric": METRIC, "value": att.flops / sec / 1e12, "unit": UNIT, "n_gpus": 1, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": ms / args.steps, "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "bf16", "data": "synthetic (seeded N(0,1) bf16 Q/K/V/dO)",
+        "config": {"workload": "cfg4 batched causal attention products fwd+bwd (QK^T, P.V, dO.V^T, P^T.dO, dS.K, "
+                               "dS^T.Q) with fp32 causal softmax and its backward between them",
+                   "batch": shape.batch, "heads": shape.heads, "head_dim": shape.head_dim, "seq_len": shape.time,
+                   "flops": "causal (visible query-key pairs) count", "l2": "inputs larger than L2 (scores 3.6 GB)"},
+        "roofline": {"bound": "hbm", "achieved": achieved_gbs, "peak": hbm, "unit": "GB/s", "frac": achieved_gbs / hbm,
+                     "traffic": None, "algorithmic_bytes_per_step": att.bytes, "peak_source": f"{source} hbm_gbs"},
+        "e2e": {"value": att.flops / (e2e_ms / 1e3 / args.steps) / 1e12, "unit": UNIT,
+                "h2d_bytes_per_step": sum(x.numel() * x.element_size() for x in host), "d2h_bytes_per_step": 4},
+        "gpu_launches": att.launches() * args.steps, "clocks": clock_info,
+    }
+    if not args.no_cpu_baseline:
+        line["cpu_baseline"] = attention_cpu_baseline(shape)
+    print(json.dumps(line), flush=True)
+    return 0
+
+
 def main(argv=None) -> int:
     ap = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
     ap.add_argument("--gpus", type=int, default=1)
@@ -355,6 +455,8 @@ def main(argv=None) -> int:
     ap.add_argument("--cpu-sample-flops", type=float, default=20e9)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--breakdown", default=None, help="write per-GEMM kernel times of the timed region here (JSON)")
+    ap.add_argument("--workload", choices=["step", "attention"], default="step",
+                    help="step: the cfg3 training-step GEMMs (default); attention: the cfg4 attention products")
     args = ap.parse_args(argv)
     if args.warmup < 3:
         ap.error("--warmup must be at least 3")
@@ -378,6 +480,8 @@ def main(argv=None) -> int:
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
                                 device_id=torch.device("cuda", local_rank))
     try:
+        if args.workload == "attention":
+            return run_attention(args, rank, world, local_rank)
         return run_ours(args, shape, rank, world, local_rank)
     finally:
         if world > 1:

@@ -83,6 +83,23 @@ enum {
     SNB_ACTIVATION_GELU_GRAD = 2 /* out = x * gelu'(gelu_input) (`gelu_backward`, kernels/elementwise.rs:153) */
 };
 
+/* Causal structure of a batched attention product, so the kernel can skip work the causal softmax makes void.
+ * Query q of each matrix sees keys 0..=q+offset (`causal_softmax`, kernels/attention.rs:153-180); masked scores
+ * are never read by the softmax and masked probabilities are 0.
+ *   SKIP_MASKED_OUTPUT  output is a [queries, keys] score matrix (Q*K^T, dO*V^T): tiles whose every element is
+ *                       masked are not computed and keep their previous contents.
+ *   LEFT_MASKED         left operand is a [queries, keys] probability-like matrix, zero after key q+offset
+ *                       (P*V, dS*K): the sum over keys stops there.
+ *   LEFT_T_MASKED       left operand is such a matrix transposed, [keys, queries] (P^T*dO, dS^T*Q): the sum
+ *                       over queries starts at key-offset.
+ * The SIMT kernel ignores the hint (it computes every element, which the hint's contract allows). */
+enum {
+    SNB_CAUSAL_NONE = 0,
+    SNB_CAUSAL_SKIP_MASKED_OUTPUT = 1,
+    SNB_CAUSAL_LEFT_MASKED = 2,
+    SNB_CAUSAL_LEFT_T_MASKED = 3
+};
+
 /* Status codes. */
 enum {
     SNB_OK = 0,
@@ -145,6 +162,9 @@ typedef struct snb_gemm_args {
     void* pre_activation;       /* GELU: receives x, laid out like the output; or NULL */
     const void* gelu_input;     /* GELU_GRAD: the forward pre-activation, laid out like the output */
     const void* residual;       /* laid out like the output, same type as the output; or NULL */
+    int32_t causal;             /* SNB_CAUSAL_*: structure of a batched attention product (work it may skip) */
+    int32_t reserved;
+    int64_t causal_offset;      /* query q sees keys 0..=q+causal_offset (the softmax's query_offset) */
 } snb_gemm_args;
 
 SNB_API int snb_gemm(void* stream, const snb_gemm_args* args);
@@ -158,6 +178,19 @@ SNB_API int snb_causal_softmax(void* stream, float* scores, uint64_t scores_len,
 /* In place on grad [rows, cols]: grad = p * (grad - sum(grad * p)) per row. Replaces `Gpu::softmax_backward`
  * (ops/attention.rs:84-100; kernel kernels/attention.rs:190-207). */
 SNB_API int snb_softmax_backward(void* stream, const float* probabilities, float* grad, uint64_t rows, uint64_t cols);
+
+/* snb_causal_softmax that also writes the probabilities as bf16 into probabilities_bf16 ([rows, keys], may be
+ * NULL), the operand of bf16 tensor-core P*V and P^T*dO products. No reference counterpart (the reference keeps
+ * f32 only). */
+SNB_API int snb_causal_softmax_bf16(void* stream, float* scores, uint64_t scores_len, uint64_t rows, uint64_t queries,
+                                    uint64_t keys, float scale, uint64_t query_offset, uint16_t* probabilities_bf16);
+
+/* softmax_backward for causal probabilities: row r (query q = r % queries) reads only its visible keys
+ * 0..=q+query_offset, where p can be non-zero, and writes grad = p * (grad - sum) there and 0 after; masked grad
+ * entries are never read (a SKIP_MASKED_OUTPUT dO*V^T leaves them unwritten). Equal to snb_softmax_backward
+ * wherever the latter's inputs are finite. Optionally also writes grad as bf16 (grad_bf16, may be NULL). */
+SNB_API int snb_causal_softmax_backward(void* stream, const float* probabilities, float* grad, uint64_t rows,
+                                        uint64_t queries, uint64_t cols, uint64_t query_offset, uint16_t* grad_bf16);
 
 /* Message of the last failed call on the calling thread ("" if none). Valid until the next call. */
 SNB_API const char* snb_last_error(void);

@@ -24,6 +24,11 @@ ACTIVATION_NONE = 0
 ACTIVATION_GELU = 1
 ACTIVATION_GELU_GRAD = 2
 
+CAUSAL_NONE = 0
+CAUSAL_SKIP_MASKED_OUTPUT = 1
+CAUSAL_LEFT_MASKED = 2
+CAUSAL_LEFT_T_MASKED = 3
+
 OK = 0
 ERR_LEFT_TOO_SMALL = 1
 ERR_RIGHT_TOO_SMALL = 2
@@ -44,6 +49,8 @@ EXPORTED_SYMBOLS = (
     "snb_gemm",
     "snb_causal_softmax",
     "snb_softmax_backward",
+    "snb_causal_softmax_bf16",
+    "snb_causal_softmax_backward",
     "snb_last_error",
     "snb_last_path",
     "snb_device_status",
@@ -89,6 +96,9 @@ class GemmArgs(ctypes.Structure):
         ("pre_activation", c_void_p),
         ("gelu_input", c_void_p),
         ("residual", c_void_p),
+        ("causal", c_int32),
+        ("reserved", c_int32),
+        ("causal_offset", ctypes.c_int64),
     ]
 
 
@@ -122,6 +132,12 @@ def load() -> ctypes.CDLL:
         lib.snb_causal_softmax.restype = c_int
         lib.snb_softmax_backward.argtypes = [c_void_p, c_void_p, c_void_p, c_uint64, c_uint64]
         lib.snb_softmax_backward.restype = c_int
+        lib.snb_causal_softmax_bf16.argtypes = [c_void_p, c_void_p, c_uint64, c_uint64, c_uint64, c_uint64,
+                                                c_float, c_uint64, c_void_p]
+        lib.snb_causal_softmax_bf16.restype = c_int
+        lib.snb_causal_softmax_backward.argtypes = [c_void_p, c_void_p, c_void_p, c_uint64, c_uint64, c_uint64,
+                                                    c_uint64, c_void_p]
+        lib.snb_causal_softmax_backward.restype = c_int
         lib.snb_last_error.argtypes = []
         lib.snb_last_error.restype = c_char_p
         lib.snb_last_path.argtypes = []

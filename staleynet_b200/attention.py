@@ -1,0 +1,157 @@
+"""The batched attention products of `CausalSelfAttention` (crates/staleynet-model/src/layers/attention.rs:188-267)
+through the C ABI, on head-major tensors [batch*heads, time, head_dim], with the fp32 causal softmax between them:
+
+  forward   scores = Q·Kᵀ                     MatmulSpec(S, S, d).right_transposed()   (attention.rs:206-209)
+            P      = causal_softmax(scores)                                            (attention.rs:210)
+            ctx    = P·V                      MatmulSpec(S, d, S)                      (attention.rs:212-213)
+  backward  dP     = dO·Vᵀ                                                              (attention.rs:239-242)
+            dV     = Pᵀ·dO                    .left_transposed()                        (attention.rs:244-247)
+            dS     = softmax_backward(P, dP)                                            (attention.rs:249)
+            dQ     = s·dS·K                   .scaled(s)                                (attention.rs:251-254)
+            dK     = s·dSᵀ·Q                  .left_transposed().scaled(s)              (attention.rs:256-260)
+
+Q, K, V, dO are bf16; scores, P, dP and dS are f32 as in the reference, and the softmax kernels also write bf16
+copies of P and dS so that every product runs on bf16 tensor cores. Each product carries its causal hint
+(SNB_CAUSAL_*): masked score tiles are not computed, and products over P or dS stop or start their sum where the
+causal mask makes the operand zero. ctx, dQ, dK and dV are f32.
+"""
+from __future__ import annotations
+
+import ctypes
+from dataclasses import dataclass
+
+from . import _ffi
+from .matmul import BatchStrides, MatmulSpec, check
+
+
+@dataclass(frozen=True)
+class AttentionShape:
+    """batch 8, 12 heads of 64, sequence 3072."""
+
+    batch: int = 8
+    heads: int = 12
+    time: int = 3072
+    head_dim: int = 64
+    query_offset: int = 0
+
+    @property
+    def count(self) -> int:
+        return self.batch * self.heads
+
+
+def causal_pairs(s: AttentionShape) -> int:
+    """Visible (query, key) pairs of one matrix: sum over q of min(q + offset + 1, time)."""
+    S, o = s.time, s.query_offset
+    return sum(min(q + o + 1, S) for q in range(S))
+
+
+def product_flops(s: AttentionShape, causal: bool = True) -> float:
+    """FLOPs of the six products: 2*d per visible (causal) or every (dense) query-key pair, per product."""
+    pairs = causal_pairs(s) if causal else s.time * s.time
+    return 6 * 2.0 * s.head_dim * pairs * s.count
+
+
+def algorithmic_bytes(s: AttentionShape) -> float:
+    """Bytes the forward + backward must move at the types above: every operand read once, every output written
+    once; score-shaped f32 tensors are written in full by the softmax kernels (masked entries become 0, the
+    reference's contract) and read over their visible part only."""
+    S, d, n = s.time, s.head_dim, s.count
+    vis = causal_pairs(s)
+    head = S * d
+    fwd = (2 * head * 2 + vis * 4           # Q, K read; visible scores written
+           + vis * 4 + S * S * (4 + 2)      # softmax: visible read, full f32 + bf16 written
+           + vis * 2 + head * 2 + head * 4)  # P.V: bf16 P visible, V, ctx f32
+    bwd = (2 * head * 2 + vis * 4           # dO, V read; visible dP written
+           + vis * 2 + head * 2 + head * 4  # dV = P^T dO
+           + 2 * vis * 4 + S * S * (4 + 2)  # softmax backward: P, dP visible read; dS f32 + bf16 written
+           + 2 * (vis * 2 + head * 2 + head * 4))  # dQ, dK
+    return float(n) * (fwd + bwd)
+
+
+class AttentionProducts:
+    """Device tensors and pre-built C-ABI arguments for the six products of one attention layer call."""
+
+    def __init__(self, shape: AttentionShape, device, seed: int = 0):
+        import torch
+
+        s = shape
+        self.shape = s
+        self.lib = _ffi.load()
+        n, S, d = s.count, s.time, s.head_dim
+        gen = torch.Generator(device=device)
+        gen.manual_seed(seed)
+
+        def normal(numel):
+            return torch.randn(numel, generator=gen, device=device, dtype=torch.float32).to(torch.bfloat16)
+
+        bf16, f32 = torch.bfloat16, torch.float32
+        self.q, self.k, self.v, self.d_out = (normal(n * S * d) for _ in range(4))
+        self.scores = torch.empty(n * S * S, device=device, dtype=f32)      # scores, then P (in place)
+        self.p16 = torch.empty(n * S * S, device=device, dtype=bf16)
+        self.ctx = torch.empty(n * S * d, device=device, dtype=f32)
+        self.d_scores = torch.empty(n * S * S, device=device, dtype=f32)    # dP, then dS (in place)
+        self.ds16 = torch.empty(n * S * S, device=device, dtype=bf16)
+        self.dq = torch.empty(n * S * d, device=device, dtype=f32)
+        self.dk = torch.empty(n * S * d, device=device, dtype=f32)
+        self.dv = torch.empty(n * S * d, device=device, dtype=f32)
+        self.scale = 1.0 / (d ** 0.5)
+
+        head, score = S * d, S * S
+        per_head = lambda left, right, out: BatchStrides(count=n, left=left, right=right, output=out)  # noqa: E731
+        C = _ffi
+        self.args = {
+            "scores": self._args(MatmulSpec.new(S, S, d).right_transposed().batched(per_head(head, head, score)),
+                                 self.q, self.k, self.scores, C.CAUSAL_SKIP_MASKED_OUTPUT),
+            "ctx": self._args(MatmulSpec.new(S, d, S).batched(per_head(score, head, head)),
+                              self.p16, self.v, self.ctx, C.CAUSAL_LEFT_MASKED),
+            "dP": self._args(MatmulSpec.new(S, S, d).right_transposed().batched(per_head(head, head, score)),
+                             self.d_out, self.v, self.d_scores, C.CAUSAL_SKIP_MASKED_OUTPUT),
+            "dV": self._args(MatmulSpec.new(S, d, S).left_transposed().batched(per_head(score, head, head)),
+                             self.p16, self.d_out, self.dv, C.CAUSAL_LEFT_T_MASKED),
+            "dQ": self._args(MatmulSpec.new(S, d, S).scaled(self.scale).batched(per_head(score, head, head)),
+                             self.ds16, self.k, self.dq, C.CAUSAL_LEFT_MASKED),
+            "dK": self._args(MatmulSpec.new(S, d, S).left_transposed().scaled(self.scale)
+                             .batched(per_head(score, head, head)), self.ds16, self.q, self.dk, C.CAUSAL_LEFT_T_MASKED),
+        }
+        self.flops = product_flops(s)
+        self.bytes = algorithmic_bytes(s)
+
+    def _args(self, spec: MatmulSpec, left, right, out, causal: int) -> _ffi.GemmArgs:
+        a = _ffi.GemmArgs()
+        a.product = spec.product()
+        a.count = spec.batch.count
+        a.left_type = a.right_type = _ffi.TYPE_BF16
+        a.output_type = _ffi.TYPE_F32
+        a.precision = _ffi.PRECISION_BF16
+        a.aux_type = _ffi.TYPE_F32
+        a.left, a.left_len = left.data_ptr(), left.numel()
+        a.right, a.right_len = right.data_ptr(), right.numel()
+        a.output, a.output_len = out.data_ptr(), out.numel()
+        a.causal = causal
+        a.causal_offset = self.shape.query_offset
+        return a
+
+    def _gemm(self, h, name) -> None:
+        check(self.lib.snb_gemm(h, ctypes.byref(self.args[name])))
+
+    def forward(self, stream_handle: int) -> None:
+        s = self.shape
+        h = ctypes.c_void_p(stream_handle)
+        self._gemm(h, "scores")
+        check(self.lib.snb_causal_softmax_bf16(h, self.scores.data_ptr(), self.scores.numel(), s.count * s.time,
+                                               s.time, s.time, self.scale, s.query_offset, self.p16.data_ptr()))
+        self._gemm(h, "ctx")
+
+    def backward(self, stream_handle: int) -> None:
+        s = self.shape
+        h = ctypes.c_void_p(stream_handle)
+        self._gemm(h, "dP")
+        self._gemm(h, "dV")
+        check(self.lib.snb_causal_softmax_backward(h, self.scores.data_ptr(), self.d_scores.data_ptr(),
+                                                   s.count * s.time, s.time, s.time, s.query_offset,
+                                                   self.ds16.data_ptr()))
+        self._gemm(h, "dQ")
+        self._gemm(h, "dK")
+
+    def launches(self) -> int:
+        return 8

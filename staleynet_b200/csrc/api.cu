@@ -164,6 +164,8 @@ int snb_gemm(void* stream, const snb_gemm_args* a) {
     if (!prec_ok) return fail(SNB_ERR_INVALID_ARGUMENT, "gemm: precision does not match the operand type");
     if (a->activation < SNB_ACTIVATION_NONE || a->activation > SNB_ACTIVATION_GELU_GRAD)
         return fail(SNB_ERR_INVALID_ARGUMENT, "gemm: unknown activation");
+    if (a->causal < SNB_CAUSAL_NONE || a->causal > SNB_CAUSAL_LEFT_T_MASKED || a->causal_offset < 0)
+        return fail(SNB_ERR_INVALID_ARGUMENT, "gemm: unknown causal mode or negative offset");
     GemmRequest r{};
     r.p = a->product;
     r.count = a->count;
@@ -180,18 +182,39 @@ int snb_gemm(void* stream, const snb_gemm_args* a) {
     r.pre = a->pre_activation;
     r.gelu_input = a->gelu_input;
     r.residual = a->residual;
+    r.causal = a->causal;
+    r.causal_offset = a->causal_offset;
     return run(static_cast<cudaStream_t>(stream), r, a->left_len, a->right_len, a->output_len);
 }
 
-int snb_causal_softmax(void* stream, float* scores, uint64_t scores_len, uint64_t rows, uint64_t queries,
-                       uint64_t keys, float scale, uint64_t query_offset) {
+int snb_causal_softmax_bf16(void* stream, float* scores, uint64_t scores_len, uint64_t rows, uint64_t queries,
+                            uint64_t keys, float scale, uint64_t query_offset, uint16_t* probabilities_bf16) {
     if (queries == 0 || rows % queries != 0)
         return fail(SNB_ERR_INVALID_ARGUMENT, "causal_softmax: rows must be a multiple of queries");
     if (scores_len < rows * keys) return fail(SNB_ERR_OUTPUT_TOO_SMALL, "causal_softmax: scores too small");
     if (rows > 0 && keys > 0 && scores == nullptr) return fail(SNB_ERR_INVALID_ARGUMENT, "causal_softmax: null scores");
     if (keys == 0) return SNB_OK;
     std::string err;
-    int rc = snb::causal_softmax(static_cast<cudaStream_t>(stream), scores, rows, queries, keys, scale, query_offset, &err);
+    int rc = snb::causal_softmax(static_cast<cudaStream_t>(stream), scores, rows, queries, keys, scale, query_offset,
+                                 probabilities_bf16, &err);
+    return rc == SNB_OK ? rc : fail(rc, err);
+}
+
+int snb_causal_softmax(void* stream, float* scores, uint64_t scores_len, uint64_t rows, uint64_t queries,
+                       uint64_t keys, float scale, uint64_t query_offset) {
+    return snb_causal_softmax_bf16(stream, scores, scores_len, rows, queries, keys, scale, query_offset, nullptr);
+}
+
+int snb_causal_softmax_backward(void* stream, const float* probabilities, float* grad, uint64_t rows,
+                                uint64_t queries, uint64_t cols, uint64_t query_offset, uint16_t* grad_bf16) {
+    if (queries == 0 || rows % queries != 0)
+        return fail(SNB_ERR_INVALID_ARGUMENT, "causal_softmax_backward: rows must be a multiple of queries");
+    if (rows > 0 && cols > 0 && (probabilities == nullptr || grad == nullptr))
+        return fail(SNB_ERR_INVALID_ARGUMENT, "causal_softmax_backward: null pointer");
+    if (cols == 0) return SNB_OK;
+    std::string err;
+    int rc = snb::causal_softmax_backward(static_cast<cudaStream_t>(stream), probabilities, grad, rows, queries, cols,
+                                          query_offset, grad_bf16, &err);
     return rc == SNB_OK ? rc : fail(rc, err);
 }
 

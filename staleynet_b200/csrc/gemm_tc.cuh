@@ -62,6 +62,8 @@ struct TcParams {
     const void* residual;     // laid out like C (type of C) or nullptr
     const void* gelu_input;   // laid out like C (aux type) or nullptr
     int64_t out_batch_stride; // elements between output matrices (for residual / gelu_input addressing)
+    int32_t causal;           // SNB_CAUSAL_* work-skipping hint of a batched attention product
+    int64_t causal_offset;    // query q sees keys 0..=q+causal_offset
 };
 
 template <int BN>
@@ -80,12 +82,13 @@ struct TcConfig {
 
 struct TcUnit {
     int32_t batch, m0, n0, kb_begin, kb_end, split;
+    bool skip;  // every output of the tile is a masked score (SNB_CAUSAL_SKIP_MASKED_OUTPUT): no work at all
 };
 
 // Work-unit order: K split outermost (the tiles of one split run side by side, so concurrent CTAs share operand
 // slices in L2 and the splits of one tile never reduce into C at the same time), then the batch, then output tiles
 // with the M or the N tile index fastest, whichever keeps the larger operand streaming through DRAM once.
-__device__ __forceinline__ TcUnit tc_decode_unit(const TcParams& p, int32_t unit, int BN) {
+__device__ __forceinline__ TcUnit tc_decode_unit(const TcParams& p, int32_t unit, int BN, int BK) {
     TcUnit u;
     const int32_t tiles = p.count * p.m_tiles * p.n_tiles;
     u.split = unit / tiles;
@@ -106,6 +109,23 @@ __device__ __forceinline__ TcUnit tc_decode_unit(const TcParams& p, int32_t unit
     u.n0 = nt * BN;
     u.kb_begin = u.split * p.k_blocks_per_split;
     u.kb_end = min(p.k_blocks, u.kb_begin + p.k_blocks_per_split);
+    u.skip = false;
+    // Causal attention products (never split): skip work whose operands or results the causal softmax voids.
+    if (p.causal == 1) {
+        // all (row, col) of the tile masked: the tile's smallest col - row exceeds the offset
+        u.skip = static_cast<int64_t>(u.n0) - (u.m0 + TC_BM - 1) > p.causal_offset;
+    } else if (p.causal == 2) {
+        // left[row, key] is zero for key > row + offset: stop after the last key any row of the tile sees
+        const int64_t last_key = static_cast<int64_t>(u.m0) + TC_BM - 1 + p.causal_offset;
+        const int64_t lim = last_key / BK + 1;
+        if (lim < u.kb_end) u.kb_end = static_cast<int32_t>(lim);
+    } else if (p.causal == 3) {
+        // left[key, query] is zero for query < key - offset: start at the first query any row of the tile sees
+        const int64_t first_query = static_cast<int64_t>(u.m0) - p.causal_offset;
+        if (first_query > 0) u.kb_begin = max(u.kb_begin, static_cast<int32_t>(first_query / BK));
+    }
+    // Keep at least one K slice (its masked contributions are zero) so the accumulator is always written.
+    if (u.kb_begin >= u.kb_end) u.kb_begin = u.kb_end - 1;
     return u;
 }
 
@@ -339,7 +359,8 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
             uint32_t phase = 0;
             bool ok = true;
             for (int32_t unit = blockIdx.x; unit < p.num_units && ok; unit += gridDim.x) {
-                const TcUnit u = tc_decode_unit(p, unit, BN);
+                const TcUnit u = tc_decode_unit(p, unit, BN, BK);
+                if (u.skip) continue;
                 const int32_t ba = p.a_batched ? u.batch : 0;
                 const int32_t bb = p.b_batched ? u.batch : 0;
                 // Bring this tile's epilogue inputs into L2 now; the epilogue reads them one main loop later.
@@ -396,8 +417,9 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
             int iter = 0;
             bool ok = true;
             bool issued = false;
-            for (int32_t unit = blockIdx.x; unit < p.num_units && ok; unit += gridDim.x, ++iter) {
-                const TcUnit u = tc_decode_unit(p, unit, BN);
+            for (int32_t unit = blockIdx.x; unit < p.num_units && ok; unit += gridDim.x) {
+                const TcUnit u = tc_decode_unit(p, unit, BN, BK);
+                if (u.skip) continue;
                 const int acc = iter & 1;
                 const uint32_t acc_phase = (iter >> 1) & 1;
                 if (!mbar_wait(smem_addr(&acc_empty[acc]), acc_phase ^ 1u)) { ok = false; break; }
@@ -422,6 +444,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
                 }
                 if (!ok) break;
                 umma_commit(smem_addr(&acc_full[acc]));
+                ++iter;
             }
             if (!ok && issued) {
                 // Let every MMA already issued finish before TMEM is released.
@@ -438,8 +461,9 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
         const int group = (warp - TC_EPI_WARP0) >> 2;
         uint8_t* box = epi + (warp - TC_EPI_WARP0) * TC_EPI_BOX_BYTES;
         int iter = 0;
-        for (int32_t unit = blockIdx.x; unit < p.num_units; unit += gridDim.x, ++iter) {
-            const TcUnit u = tc_decode_unit(p, unit, BN);
+        for (int32_t unit = blockIdx.x; unit < p.num_units; unit += gridDim.x) {
+            const TcUnit u = tc_decode_unit(p, unit, BN, BK);
+            if (u.skip) continue;
             const int acc = iter & 1;
             const uint32_t acc_phase = (iter >> 1) & 1;
             if (!mbar_wait(smem_addr(&acc_full[acc]), acc_phase)) break;
@@ -478,6 +502,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
             tcgen05_fence_before_sync();
             __syncwarp();
             if (lane == 0) mbar_arrive(smem_addr(&acc_empty[acc]));
+            ++iter;
         }
         if (lane == 0) bulk_wait_group<0>();
         __syncwarp();

@@ -24,6 +24,8 @@ struct GemmRequest {
     void* pre;
     const void* gelu_input;
     const void* residual;
+    int causal;
+    int64_t causal_offset;
 };
 
 struct DeviceInfo {
@@ -43,9 +45,12 @@ int tc_gemm_try(cudaStream_t stream, const GemmRequest& r, bool* launched, std::
 int simt_gemm(cudaStream_t stream, const GemmRequest& r, std::string* err);
 
 int causal_softmax(cudaStream_t stream, float* scores, uint64_t rows, uint64_t queries, uint64_t keys, float scale,
-                   uint64_t query_offset, std::string* err);
+                   uint64_t query_offset, uint16_t* probs_bf16, std::string* err);
 int softmax_backward(cudaStream_t stream, const float* probabilities, float* grad, uint64_t rows, uint64_t cols,
                      std::string* err);
+int causal_softmax_backward(cudaStream_t stream, const float* probabilities, float* grad, uint64_t rows,
+                            uint64_t queries, uint64_t cols, uint64_t query_offset, uint16_t* grad_bf16,
+                            std::string* err);
 
 // Launches a one-thread kernel whose mbarrier wait nothing completes; it gives up after limit_ns.
 int bounded_wait_probe(cudaStream_t stream, uint64_t limit_ns, std::string* err);

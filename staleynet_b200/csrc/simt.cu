@@ -132,9 +132,10 @@ __global__ void __launch_bounds__(ST_THREADS) simt_gemm_kernel(const void* __res
 }
 
 // One warp per row (kernels/attention.rs:153-180): max of the scaled visible scores, exponentials, normalisation;
-// keys after q + query_offset become 0 and are never read.
+// keys after q + query_offset become 0 and are never read. With probs_bf16 the probabilities are also written as
+// bf16 (the operand of bf16 P*V and P^T*dO products).
 __global__ void causal_softmax_kernel(float* scores, int64_t rows, int64_t queries, int64_t keys, float scale,
-                                      int64_t query_offset) {
+                                      int64_t query_offset, __nv_bfloat16* probs_bf16) {
     const int64_t row = (static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x) / 32;
     const int lane = threadIdx.x % 32;
     if (row >= rows) return;
@@ -154,7 +155,12 @@ __global__ void causal_softmax_kernel(float* scores, int64_t rows, int64_t queri
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) total += __shfl_xor_sync(0xffffffffu, total, o);
     const float normaliser = 1.0f / total;
-    for (int64_t k = lane; k < keys; k += 32) values[k] = k < visible ? values[k] * normaliser : 0.0f;
+    __nv_bfloat16* out16 = probs_bf16 ? probs_bf16 + row * keys : nullptr;
+    for (int64_t k = lane; k < keys; k += 32) {
+        const float p = k < visible ? values[k] * normaliser : 0.0f;
+        values[k] = p;
+        if (out16) out16[k] = __float2bfloat16_rn(p);
+    }
 }
 
 // grad <- p * (grad - sum(grad * p)) per row, one warp per row (kernels/attention.rs:190-207).
@@ -169,6 +175,30 @@ __global__ void softmax_backward_kernel(const float* probabilities, float* grad,
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) projection += __shfl_xor_sync(0xffffffffu, projection, o);
     for (int64_t c = lane; c < cols; c += 32) g[c] = p[c] * (g[c] - projection);
+}
+
+// The same for causal probabilities: only the visible keys 0..=q+query_offset are read (p is 0 after them, so the
+// sum and the result are unchanged), masked gradient entries are never read and become 0; optional bf16 copy.
+__global__ void causal_softmax_backward_kernel(const float* probabilities, float* grad, int64_t rows,
+                                               int64_t queries, int64_t cols, int64_t query_offset,
+                                               __nv_bfloat16* grad_bf16) {
+    const int64_t row = (static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x) / 32;
+    const int lane = threadIdx.x % 32;
+    if (row >= rows) return;
+    const float* p = probabilities + row * cols;
+    float* g = grad + row * cols;
+    int64_t visible = row % queries + query_offset + 1;
+    if (visible > cols) visible = cols;
+    float projection = 0.0f;
+    for (int64_t c = lane; c < visible; c += 32) projection += g[c] * p[c];
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) projection += __shfl_xor_sync(0xffffffffu, projection, o);
+    __nv_bfloat16* out16 = grad_bf16 ? grad_bf16 + row * cols : nullptr;
+    for (int64_t c = lane; c < cols; c += 32) {
+        const float d = c < visible ? p[c] * (g[c] - projection) : 0.0f;
+        g[c] = d;
+        if (out16) out16[c] = __float2bfloat16_rn(d);
+    }
 }
 
 }  // namespace
@@ -214,7 +244,7 @@ int simt_gemm(cudaStream_t stream, const GemmRequest& r, std::string* err) {
 }
 
 int causal_softmax(cudaStream_t stream, float* scores, uint64_t rows, uint64_t queries, uint64_t keys, float scale,
-                   uint64_t query_offset, std::string* err) {
+                   uint64_t query_offset, uint16_t* probs_bf16, std::string* err) {
     if (rows == 0) return SNB_OK;
     const int threads = 256;
     const uint64_t blocks = (rows * 32 + threads - 1) / threads;
@@ -224,10 +254,31 @@ int causal_softmax(cudaStream_t stream, float* scores, uint64_t rows, uint64_t q
     }
     causal_softmax_kernel<<<static_cast<unsigned>(blocks), threads, 0, stream>>>(
         scores, static_cast<int64_t>(rows), static_cast<int64_t>(queries), static_cast<int64_t>(keys), scale,
-        static_cast<int64_t>(query_offset));
+        static_cast<int64_t>(query_offset), reinterpret_cast<__nv_bfloat16*>(probs_bf16));
     cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess) {
         *err = cuda_message("causal_softmax_kernel launch", e);
+        return SNB_ERR_CUDA;
+    }
+    return SNB_OK;
+}
+
+int causal_softmax_backward(cudaStream_t stream, const float* probabilities, float* grad, uint64_t rows,
+                            uint64_t queries, uint64_t cols, uint64_t query_offset, uint16_t* grad_bf16,
+                            std::string* err) {
+    if (rows == 0) return SNB_OK;
+    const int threads = 256;
+    const uint64_t blocks = (rows * 32 + threads - 1) / threads;
+    if (blocks > 0x7fffffffull) {
+        *err = "causal_softmax_backward: too many rows";
+        return SNB_ERR_UNSUPPORTED;
+    }
+    causal_softmax_backward_kernel<<<static_cast<unsigned>(blocks), threads, 0, stream>>>(
+        probabilities, grad, static_cast<int64_t>(rows), static_cast<int64_t>(queries), static_cast<int64_t>(cols),
+        static_cast<int64_t>(query_offset), reinterpret_cast<__nv_bfloat16*>(grad_bf16));
+    cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess) {
+        *err = cuda_message("causal_softmax_backward_kernel launch", e);
         return SNB_ERR_CUDA;
     }
     return SNB_OK;

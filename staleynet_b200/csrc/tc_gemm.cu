@@ -201,7 +201,8 @@ int tc_gemm_try(cudaStream_t stream, const GemmRequest& r, bool* launched, std::
     const int64_t k_blocks = (p.inner + bk - 1) / bk;
     const int64_t tiles = static_cast<int64_t>(r.count) * m_tiles * n_tiles;
     if (tiles > (1ll << 30)) return SNB_OK;
-    const bool plain_epilogue = !out_bf16 && r.activation == SNB_ACTIVATION_NONE && r.pre == nullptr;
+    const bool plain_epilogue =
+        !out_bf16 && r.activation == SNB_ACTIVATION_NONE && r.pre == nullptr && r.causal == SNB_CAUSAL_NONE;
     const int splits = plain_epilogue ? choose_splits(tiles, k_blocks, dev.sm_count) : 1;
     const int64_t kb_per_split = (k_blocks + splits - 1) / splits;
     const int64_t splits_used = (k_blocks + kb_per_split - 1) / kb_per_split;  // every split has >= 1 slice
@@ -308,6 +309,8 @@ int tc_gemm_try(cudaStream_t stream, const GemmRequest& r, bool* launched, std::
     kp.residual = r.residual;
     kp.gelu_input = r.gelu_input;
     kp.out_batch_stride = static_cast<int64_t>(c_batched ? p.output_batch_stride : 0);
+    kp.causal = r.causal;
+    kp.causal_offset = r.causal_offset;
 
     const int grid = static_cast<int>(std::min<int64_t>(units, dev.sm_count));
     if (bf16_in) {

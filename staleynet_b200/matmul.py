@@ -194,7 +194,8 @@ class Gpu:
         check(code)
 
     def gemm(self, spec: MatmulSpec, left, right, output, *, bias=None, activation: int = _ffi.ACTIVATION_NONE,
-             pre_activation=None, gelu_input=None, residual=None) -> None:
+             pre_activation=None, gelu_input=None, residual=None, causal: int = _ffi.CAUSAL_NONE,
+             causal_offset: int = 0) -> None:
         """`Gpu.matmul` with the caller's elementwise follow-up fused into the epilogue (snb_gemm)."""
         import torch
 
@@ -220,6 +221,8 @@ class Gpu:
         args.pre_activation = _ptr(pre_activation) if pre_activation is not None else None
         args.gelu_input = _ptr(gelu_input) if gelu_input is not None else None
         args.residual = _ptr(residual) if residual is not None else None
+        args.causal = causal
+        args.causal_offset = causal_offset
         check(self.lib.snb_gemm(self._stream_handle(), ctypes.byref(args)))
 
     def causal_softmax(self, scores, queries: int, scale: float, query_offset: int) -> None:
@@ -230,6 +233,21 @@ class Gpu:
             raise AssertionError("causal_softmax: rows must be a multiple of queries")
         check(self.lib.snb_causal_softmax(self._stream_handle(), _ptr(scores), scores.numel(), rows, queries, keys,
                                           scale, query_offset))
+
+    def causal_softmax_bf16(self, scores, queries: int, scale: float, query_offset: int, probabilities_bf16) -> None:
+        """causal_softmax that also writes the probabilities as bf16 (snb_causal_softmax_bf16)."""
+        _require_cuda(scores, probabilities_bf16)
+        rows, keys = scores.shape
+        check(self.lib.snb_causal_softmax_bf16(self._stream_handle(), _ptr(scores), scores.numel(), rows, queries,
+                                               keys, scale, query_offset, _ptr(probabilities_bf16)))
+
+    def causal_softmax_backward(self, probabilities, grad, queries: int, query_offset: int, grad_bf16=None) -> None:
+        """softmax_backward reading only the visible keys of causal probabilities (snb_causal_softmax_backward)."""
+        _require_cuda(probabilities, grad, grad_bf16)
+        rows, cols = probabilities.shape
+        check(self.lib.snb_causal_softmax_backward(self._stream_handle(), _ptr(probabilities), _ptr(grad), rows,
+                                                   queries, cols, query_offset,
+                                                   _ptr(grad_bf16) if grad_bf16 is not None else None))
 
     def softmax_backward(self, probabilities, grad) -> None:
         """`Gpu::softmax_backward` (ops/attention.rs:83-100)."""
