@@ -131,9 +131,27 @@ __global__ void __launch_bounds__(ST_THREADS) simt_gemm_kernel(const void* __res
     }
 }
 
-// One warp per row (kernels/attention.rs:153-180): max of the scaled visible scores, exponentials, normalisation;
-// keys after q + query_offset become 0 and are never read. With probs_bf16 the probabilities are also written as
-// bf16 (the operand of bf16 P*V and P^T*dO products).
+// Online (max, sum) pair of a softmax: sum of exp(x - max) over the values seen so far.
+struct MaxSum {
+    float m, s;
+};
+
+__device__ __forceinline__ MaxSum maxsum_add(MaxSum a, float x) {
+    if (x > a.m) return {x, a.s * expf(a.m - x) + 1.0f};
+    return {a.m, a.s + expf(x - a.m)};
+}
+
+__device__ __forceinline__ MaxSum maxsum_merge(MaxSum a, MaxSum b) {
+    const float m = fmaxf(a.m, b.m);
+    const float s = (a.s > 0.0f ? a.s * expf(a.m - m) : 0.0f) + (b.s > 0.0f ? b.s * expf(b.m - m) : 0.0f);
+    return {m, s};
+}
+
+// One warp per row (kernels/attention.rs:153-180): p = exp(s*x - max) / sum over the visible keys
+// 0..=q+query_offset, 0 after them; masked scores are never read. One read pass accumulates (max, sum) online,
+// a second reads the visible scores again and writes the whole row (f32 in place and, with probs_bf16, bf16).
+// VEC = 4 moves 16 bytes per lane and step (rows start 16-byte aligned).
+template <int VEC>
 __global__ void causal_softmax_kernel(float* scores, int64_t rows, int64_t queries, int64_t keys, float scale,
                                       int64_t query_offset, __nv_bfloat16* probs_bf16) {
     const int64_t row = (static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x) / 32;
@@ -142,24 +160,54 @@ __global__ void causal_softmax_kernel(float* scores, int64_t rows, int64_t queri
     float* values = scores + row * keys;
     int64_t visible = row % queries + query_offset + 1;
     if (visible > keys) visible = keys;
-    float maximum = -3.0e38f;
-    for (int64_t k = lane; k < visible; k += 32) maximum = fmaxf(maximum, values[k] * scale);
+    MaxSum acc{-3.0e38f, 0.0f};
+    for (int64_t k0 = static_cast<int64_t>(lane) * VEC; k0 < visible; k0 += 32 * VEC) {
+        float x[VEC];
+        if constexpr (VEC == 4) {
+            const float4 v = *reinterpret_cast<const float4*>(values + k0);
+            x[0] = v.x; x[1] = v.y; x[2] = v.z; x[3] = v.w;
+        } else {
+            x[0] = values[k0];
+        }
 #pragma unroll
-    for (int o = 16; o > 0; o >>= 1) maximum = fmaxf(maximum, __shfl_xor_sync(0xffffffffu, maximum, o));
-    float total = 0.0f;
-    for (int64_t k = lane; k < visible; k += 32) {
-        const float e = expf(values[k] * scale - maximum);
-        values[k] = e;
-        total += e;
+        for (int i = 0; i < VEC; ++i)
+            if (k0 + i < visible) acc = maxsum_add(acc, x[i] * scale);
     }
 #pragma unroll
-    for (int o = 16; o > 0; o >>= 1) total += __shfl_xor_sync(0xffffffffu, total, o);
-    const float normaliser = 1.0f / total;
+    for (int o = 16; o > 0; o >>= 1) {
+        MaxSum other{__shfl_xor_sync(0xffffffffu, acc.m, o), __shfl_xor_sync(0xffffffffu, acc.s, o)};
+        acc = maxsum_merge(acc, other);
+    }
+    const float normaliser = 1.0f / acc.s;
     __nv_bfloat16* out16 = probs_bf16 ? probs_bf16 + row * keys : nullptr;
-    for (int64_t k = lane; k < keys; k += 32) {
-        const float p = k < visible ? values[k] * normaliser : 0.0f;
-        values[k] = p;
-        if (out16) out16[k] = __float2bfloat16_rn(p);
+    for (int64_t k0 = static_cast<int64_t>(lane) * VEC; k0 < keys; k0 += 32 * VEC) {
+        float p[VEC];
+        if (k0 < visible) {
+            float x[VEC];
+            if constexpr (VEC == 4) {
+                const float4 v = *reinterpret_cast<const float4*>(values + k0);
+                x[0] = v.x; x[1] = v.y; x[2] = v.z; x[3] = v.w;
+            } else {
+                x[0] = values[k0];
+            }
+#pragma unroll
+            for (int i = 0; i < VEC; ++i) p[i] = k0 + i < visible ? expf(x[i] * scale - acc.m) * normaliser : 0.0f;
+        } else {
+#pragma unroll
+            for (int i = 0; i < VEC; ++i) p[i] = 0.0f;
+        }
+        if constexpr (VEC == 4) {
+            *reinterpret_cast<float4*>(values + k0) = make_float4(p[0], p[1], p[2], p[3]);
+            if (out16) {
+                __nv_bfloat162 lo = __floats2bfloat162_rn(p[0], p[1]);
+                __nv_bfloat162 hi = __floats2bfloat162_rn(p[2], p[3]);
+                uint2 packed = make_uint2(*reinterpret_cast<uint32_t*>(&lo), *reinterpret_cast<uint32_t*>(&hi));
+                *reinterpret_cast<uint2*>(out16 + k0) = packed;
+            }
+        } else {
+            values[k0] = p[0];
+            if (out16) out16[k0] = __float2bfloat16_rn(p[0]);
+        }
     }
 }
 
@@ -179,6 +227,7 @@ __global__ void softmax_backward_kernel(const float* probabilities, float* grad,
 
 // The same for causal probabilities: only the visible keys 0..=q+query_offset are read (p is 0 after them, so the
 // sum and the result are unchanged), masked gradient entries are never read and become 0; optional bf16 copy.
+template <int VEC>
 __global__ void causal_softmax_backward_kernel(const float* probabilities, float* grad, int64_t rows,
                                                int64_t queries, int64_t cols, int64_t query_offset,
                                                __nv_bfloat16* grad_bf16) {
@@ -190,14 +239,51 @@ __global__ void causal_softmax_backward_kernel(const float* probabilities, float
     int64_t visible = row % queries + query_offset + 1;
     if (visible > cols) visible = cols;
     float projection = 0.0f;
-    for (int64_t c = lane; c < visible; c += 32) projection += g[c] * p[c];
+    for (int64_t c0 = static_cast<int64_t>(lane) * VEC; c0 < visible; c0 += 32 * VEC) {
+        if constexpr (VEC == 4) {
+            const float4 pv = *reinterpret_cast<const float4*>(p + c0);
+            const float4 gv = *reinterpret_cast<const float4*>(g + c0);
+            const float pp[4] = {pv.x, pv.y, pv.z, pv.w};
+            const float gg[4] = {gv.x, gv.y, gv.z, gv.w};
+#pragma unroll
+            for (int i = 0; i < 4; ++i)
+                if (c0 + i < visible) projection += gg[i] * pp[i];
+        } else {
+            projection += g[c0] * p[c0];
+        }
+    }
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) projection += __shfl_xor_sync(0xffffffffu, projection, o);
     __nv_bfloat16* out16 = grad_bf16 ? grad_bf16 + row * cols : nullptr;
-    for (int64_t c = lane; c < cols; c += 32) {
-        const float d = c < visible ? p[c] * (g[c] - projection) : 0.0f;
-        g[c] = d;
-        if (out16) out16[c] = __float2bfloat16_rn(d);
+    for (int64_t c0 = static_cast<int64_t>(lane) * VEC; c0 < cols; c0 += 32 * VEC) {
+        float d[VEC];
+        if (c0 < visible) {
+            if constexpr (VEC == 4) {
+                const float4 pv = *reinterpret_cast<const float4*>(p + c0);
+                const float4 gv = *reinterpret_cast<const float4*>(g + c0);
+                const float pp[4] = {pv.x, pv.y, pv.z, pv.w};
+                const float gg[4] = {gv.x, gv.y, gv.z, gv.w};
+#pragma unroll
+                for (int i = 0; i < 4; ++i) d[i] = c0 + i < visible ? pp[i] * (gg[i] - projection) : 0.0f;
+            } else {
+                d[0] = p[c0] * (g[c0] - projection);
+            }
+        } else {
+#pragma unroll
+            for (int i = 0; i < VEC; ++i) d[i] = 0.0f;
+        }
+        if constexpr (VEC == 4) {
+            *reinterpret_cast<float4*>(g + c0) = make_float4(d[0], d[1], d[2], d[3]);
+            if (out16) {
+                __nv_bfloat162 lo = __floats2bfloat162_rn(d[0], d[1]);
+                __nv_bfloat162 hi = __floats2bfloat162_rn(d[2], d[3]);
+                *reinterpret_cast<uint2*>(out16 + c0) =
+                    make_uint2(*reinterpret_cast<uint32_t*>(&lo), *reinterpret_cast<uint32_t*>(&hi));
+            }
+        } else {
+            g[c0] = d[0];
+            if (out16) out16[c0] = __float2bfloat16_rn(d[0]);
+        }
     }
 }
 
@@ -252,9 +338,16 @@ int causal_softmax(cudaStream_t stream, float* scores, uint64_t rows, uint64_t q
         *err = "causal_softmax: too many rows";
         return SNB_ERR_UNSUPPORTED;
     }
-    causal_softmax_kernel<<<static_cast<unsigned>(blocks), threads, 0, stream>>>(
-        scores, static_cast<int64_t>(rows), static_cast<int64_t>(queries), static_cast<int64_t>(keys), scale,
-        static_cast<int64_t>(query_offset), reinterpret_cast<__nv_bfloat16*>(probs_bf16));
+    const bool vec = keys % 4 == 0 && reinterpret_cast<uintptr_t>(scores) % 16 == 0 &&
+                     reinterpret_cast<uintptr_t>(probs_bf16) % 8 == 0;
+    if (vec)
+        causal_softmax_kernel<4><<<static_cast<unsigned>(blocks), threads, 0, stream>>>(
+            scores, static_cast<int64_t>(rows), static_cast<int64_t>(queries), static_cast<int64_t>(keys), scale,
+            static_cast<int64_t>(query_offset), reinterpret_cast<__nv_bfloat16*>(probs_bf16));
+    else
+        causal_softmax_kernel<1><<<static_cast<unsigned>(blocks), threads, 0, stream>>>(
+            scores, static_cast<int64_t>(rows), static_cast<int64_t>(queries), static_cast<int64_t>(keys), scale,
+            static_cast<int64_t>(query_offset), reinterpret_cast<__nv_bfloat16*>(probs_bf16));
     cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess) {
         *err = cuda_message("causal_softmax_kernel launch", e);
@@ -273,9 +366,18 @@ int causal_softmax_backward(cudaStream_t stream, const float* probabilities, flo
         *err = "causal_softmax_backward: too many rows";
         return SNB_ERR_UNSUPPORTED;
     }
-    causal_softmax_backward_kernel<<<static_cast<unsigned>(blocks), threads, 0, stream>>>(
-        probabilities, grad, static_cast<int64_t>(rows), static_cast<int64_t>(queries), static_cast<int64_t>(cols),
-        static_cast<int64_t>(query_offset), reinterpret_cast<__nv_bfloat16*>(grad_bf16));
+    const bool vec = cols % 4 == 0 && reinterpret_cast<uintptr_t>(probabilities) % 16 == 0 &&
+                     reinterpret_cast<uintptr_t>(grad) % 16 == 0 && reinterpret_cast<uintptr_t>(grad_bf16) % 8 == 0;
+    if (vec)
+        causal_softmax_backward_kernel<4><<<static_cast<unsigned>(blocks), threads, 0, stream>>>(
+            probabilities, grad, static_cast<int64_t>(rows), static_cast<int64_t>(queries),
+            static_cast<int64_t>(cols), static_cast<int64_t>(query_offset),
+            reinterpret_cast<__nv_bfloat16*>(grad_bf16));
+    else
+        causal_softmax_backward_kernel<1><<<static_cast<unsigned>(blocks), threads, 0, stream>>>(
+            probabilities, grad, static_cast<int64_t>(rows), static_cast<int64_t>(queries),
+            static_cast<int64_t>(cols), static_cast<int64_t>(query_offset),
+            reinterpret_cast<__nv_bfloat16*>(grad_bf16));
     cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess) {
         *err = cuda_message("causal_softmax_backward_kernel launch", e);
