@@ -117,7 +117,8 @@ enum {
     SNB_PATH_NONE = 0,
     SNB_PATH_TENSOR_CORE = 1, /* tcgen05 + TMA persistent kernel */
     SNB_PATH_SIMT = 2,        /* strided SIMT kernel: any strides and alignments, exact f32 FMA */
-    SNB_PATH_EMPTY = 3        /* nothing to compute (rows or cols is 0) */
+    SNB_PATH_EMPTY = 3,       /* nothing to compute (rows or cols is 0) */
+    SNB_PATH_TENSOR_CORE_PAIR = 4 /* tcgen05 kernel on CTA pairs (cta_group::2, 256 x 256 tiles) */
 };
 
 /* Batched strided GEMM on f32 operands: replaces `Gpu::matmul` (ops/matmul.rs:146-171).

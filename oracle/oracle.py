@@ -7,6 +7,7 @@ reported CPU baseline; the product library never loads it. The C file restates t
 from __future__ import annotations
 
 import ctypes
+import os
 import shutil
 import subprocess
 import threading
@@ -41,7 +42,7 @@ def build(force: bool = False) -> Path:
     if cc is None:
         raise RuntimeError("gcc not found")
     BUILD_DIR.mkdir(exist_ok=True)
-    tmp = LIB_PATH.with_suffix(".so.tmp")
+    tmp = LIB_PATH.with_suffix(f".so.{os.getpid()}.tmp")  # concurrent builders (spawned test ranks) never collide
     cmd = [cc, "-O2", "-fPIC", "-shared", "-fopenmp", "-ffp-contract=off", "-o", str(tmp), str(SOURCE), "-lm"]
     subprocess.run(cmd, check=True, capture_output=True, text=True)
     tmp.replace(LIB_PATH)

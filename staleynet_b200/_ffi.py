@@ -42,6 +42,8 @@ PATH_NONE = 0
 PATH_TENSOR_CORE = 1
 PATH_SIMT = 2
 PATH_EMPTY = 3
+PATH_TENSOR_CORE_PAIR = 4
+TENSOR_CORE_PATHS = (PATH_TENSOR_CORE, PATH_TENSOR_CORE_PAIR)
 
 EXPORTED_SYMBOLS = (
     "snb_matmul",

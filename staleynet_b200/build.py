@@ -69,7 +69,7 @@ def build_library(force: bool = False, verbose_ptxas: bool = False) -> Path:
             objs.append(obj)
             if verbose_ptxas and log.strip():
                 print(log)
-    tmp = LIB_PATH.with_suffix(".so.tmp")
+    tmp = LIB_PATH.with_suffix(f".so.{os.getpid()}.tmp")
     cmd = [nvcc, *ARCH_FLAGS, "-shared", "-o", str(tmp), *map(str, objs), "-lcuda"]
     res = subprocess.run(cmd, capture_output=True, text=True)
     if res.returncode != 0:

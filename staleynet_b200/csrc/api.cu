@@ -55,10 +55,11 @@ int run(cudaStream_t stream, const GemmRequest& r, uint64_t left_len, uint64_t r
 
     std::string err;
     bool launched = false;
-    int rc = tc_gemm_try(stream, r, &launched, &err);
+    int path = SNB_PATH_NONE;
+    int rc = tc_gemm_try(stream, r, &launched, &path, &err);
     if (rc != SNB_OK) return fail(rc, err);
     if (launched) {
-        t_last_path = SNB_PATH_TENSOR_CORE;
+        t_last_path = path;
         return SNB_OK;
     }
     rc = simt_gemm(stream, r, &err);

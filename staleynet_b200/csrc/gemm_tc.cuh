@@ -88,7 +88,7 @@ struct TcUnit {
 // Work-unit order: K split outermost (the tiles of one split run side by side, so concurrent CTAs share operand
 // slices in L2 and the splits of one tile never reduce into C at the same time), then the batch, then output tiles
 // with the M or the N tile index fastest, whichever keeps the larger operand streaming through DRAM once.
-__device__ __forceinline__ TcUnit tc_decode_unit(const TcParams& p, int32_t unit, int BN, int BK) {
+__device__ __forceinline__ TcUnit tc_decode_unit(const TcParams& p, int32_t unit, int BN, int BK, int BM = TC_BM) {
     TcUnit u;
     const int32_t tiles = p.count * p.m_tiles * p.n_tiles;
     u.split = unit / tiles;
@@ -105,7 +105,7 @@ __device__ __forceinline__ TcUnit tc_decode_unit(const TcParams& p, int32_t unit
         mt = rest % p.m_tiles;
         u.batch = rest / p.m_tiles;
     }
-    u.m0 = mt * TC_BM;
+    u.m0 = mt * BM;
     u.n0 = nt * BN;
     u.kb_begin = u.split * p.k_blocks_per_split;
     u.kb_end = min(p.k_blocks, u.kb_begin + p.k_blocks_per_split);

@@ -1,0 +1,255 @@
+// gemm_tc_pair.cuh — the tensor-core GEMM on CTA pairs: one tcgen05.mma.cta_group::2 computes a 256 x 256 tile
+// for a cluster of two CTAs (one per SM). Each CTA stages its own 128 rows of A and its own 128 columns of B, so a
+// K slice costs each SM 32 KB of L2 traffic instead of the 48 KB of a 128 x 256 single-CTA tile: a third less
+// L2 -> SM traffic per FLOP, which is what limits the single-CTA kernel's main loop on B200.
+//
+// Roles per CTA (320 threads, as the single-CTA kernel):
+//   warp 0     TMA producer in both CTAs: loads this CTA's A rows and B columns into its 6-stage ring; the
+//              completion bytes of both CTAs are counted on the first CTA's `full` barrier (cta_group::2 loads).
+//   warp 1     allocates / frees the pair's TMEM (cta_group::2) in both CTAs; in the first CTA one elected thread
+//              issues the pair MMAs and commits each ring slot back to both CTAs' `empty` barriers and each
+//              finished accumulator to both CTAs' `acc_full` barriers (one plain commit per CTA).
+//   warps 2-9  epilogue in both CTAs, on this CTA's 128 rows x 256 columns of the accumulator (same code as the
+//              single-CTA kernel); every warp of both CTAs arrives on the first CTA's `acc_empty` barrier.
+#pragma once
+
+#include "gemm_tc.cuh"
+
+namespace snb {
+
+constexpr int TC2_BM = 256;  // rows per CTA pair (128 per CTA)
+constexpr int TC2_BN = 256;  // columns per pair tile (128 staged per CTA)
+
+struct Tc2Config {
+    static constexpr int STAGE_A = 128 * 128;
+    static constexpr int STAGE_B = (TC2_BN / 2) * 128;
+    static constexpr int STAGE = STAGE_A + STAGE_B;
+    static constexpr int STAGES = 6;
+    static constexpr int EPI_BYTES = TC_EPI_WARPS * TC_EPI_BOX_BYTES;
+    static constexpr int TMEM_COLS = 2 * TC2_BN;
+    static constexpr int BARRIER_BYTES = 256;
+    static constexpr int SMEM_BYTES = 1024 + STAGES * STAGE + EPI_BYTES + BARRIER_BYTES;
+    static_assert(SMEM_BYTES <= 232448, "shared memory budget of one sm_100 CTA");
+};
+
+template <typename E, bool OUT_BF16>
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(TC_THREADS, 1)
+    tc_gemm_pair_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constant__ CUtensorMap tm_b,
+                        const __grid_constant__ CUtensorMap tm_c, const __grid_constant__ CUtensorMap tm_pre,
+                        const __grid_constant__ CUtensorMap tm_res, const __grid_constant__ CUtensorMap tm_gin,
+                        const TcParams p) {
+    using Cfg = Tc2Config;
+    constexpr int BN = TC2_BN;
+    constexpr int ESIZE = sizeof(E);
+    constexpr int BK = 128 / ESIZE;
+    constexpr int UMMA_K = 32 / ESIZE;
+    constexpr int MN_BOX = 128 / ESIZE;
+    constexpr bool IS_BF16 = ESIZE == 2;
+    constexpr uint32_t FORMAT = IS_BF16 ? 1u : 2u;
+    constexpr int CHUNK = OUT_BF16 ? 64 : 32;
+
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    uint8_t* ring = smem;
+    uint8_t* epi = smem + Cfg::STAGES * Cfg::STAGE;
+    uint64_t* bars = reinterpret_cast<uint64_t*>(epi + Cfg::EPI_BYTES);
+    uint64_t* full = bars;
+    uint64_t* empty = bars + Cfg::STAGES;
+    uint64_t* acc_full = bars + 2 * Cfg::STAGES;
+    uint64_t* acc_empty = acc_full + 2;
+    uint64_t* drain = acc_empty + 2;
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
+
+    const int warp = threadIdx.x >> 5;
+    const int lane = threadIdx.x & 31;
+    const uint32_t rank = cluster_cta_rank();
+    const bool leader = rank == 0;
+    const int32_t first_unit = static_cast<int32_t>(blockIdx.x >> 1);
+    const int32_t unit_step = static_cast<int32_t>(gridDim.x >> 1);
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < Cfg::STAGES; ++s) {
+            mbar_init(smem_addr(&full[s]), 1);
+            mbar_init(smem_addr(&empty[s]), 1);
+        }
+        for (int a = 0; a < 2; ++a) {
+            mbar_init(smem_addr(&acc_full[a]), 1);
+            mbar_init(smem_addr(&acc_empty[a]), 2 * TC_EPI_WARPS);  // every epilogue warp of both CTAs
+        }
+        mbar_init(smem_addr(drain), 1);
+        fence_mbarrier_init();
+        fence_proxy_async_shared();
+    }
+    if (warp == 0 && lane == 0) {
+        tma_prefetch_descriptor(&tm_a);
+        tma_prefetch_descriptor(&tm_b);
+        tma_prefetch_descriptor(&tm_c);
+    }
+    if (warp == 1) {
+        tmem_alloc_pair(smem_addr(tmem_slot), Cfg::TMEM_COLS);
+        tmem_relinquish_alloc_permit_pair();
+    }
+    tcgen05_fence_before_sync();
+    cluster_sync();  // both CTAs' barriers exist before either CTA signals the other's
+    tcgen05_fence_after_sync();
+    const uint32_t tmem_base = *tmem_slot;
+
+    if (warp == 0) {
+        // ------------------------------------------------------------------ TMA producer (both CTAs)
+        if (elect_one()) {
+            int stage = 0;
+            uint32_t phase = 0;
+            bool ok = true;
+            for (int32_t unit = first_unit; unit < p.num_units && ok; unit += unit_step) {
+                const TcUnit u = tc_decode_unit(p, unit, BN, BK, TC2_BM);
+                const int32_t ba = p.a_batched ? u.batch : 0;
+                const int32_t bb = p.b_batched ? u.batch : 0;
+                const int32_t m0 = u.m0 + 128 * static_cast<int32_t>(rank);  // this CTA's rows
+                const int32_t n0 = u.n0 + (BN / 2) * static_cast<int32_t>(rank);  // this CTA's columns of B
+                if (u.split == 0) {
+                    if (p.residual != nullptr) tma_prefetch_l2_3d(&tm_res, u.n0, m0, u.batch);
+                    if (p.activation == 2) tma_prefetch_l2_3d(&tm_gin, u.n0, m0, u.batch);
+                }
+                for (int32_t kb = u.kb_begin; kb < u.kb_end; ++kb) {
+                    if (!mbar_wait_cluster(smem_addr(&empty[stage]), phase ^ 1u)) { ok = false; break; }
+                    const uint32_t fb_local = smem_addr(&full[stage]);
+                    if (leader) mbar_arrive_expect_tx(fb_local, 2 * Cfg::STAGE);  // both CTAs' bytes
+                    const uint32_t fb = map_to_cta(fb_local, 0);
+                    const uint32_t sa = smem_addr(ring + stage * Cfg::STAGE);
+                    const uint32_t sb = sa + Cfg::STAGE_A;
+                    const int32_t k0 = kb * BK;
+                    if (!p.a_mn_major) {
+                        tma_load_3d_pair(sa, &tm_a, fb, k0, m0, ba);
+                    } else {
+#pragma unroll
+                        for (int j = 0; j < 128 / MN_BOX; ++j)
+                            tma_load_3d_pair(sa + j * (BK * 128), &tm_a, fb, m0 + j * MN_BOX, k0, ba);
+                    }
+                    if (!p.b_mn_major) {
+                        tma_load_3d_pair(sb, &tm_b, fb, k0, n0, bb);
+                    } else {
+#pragma unroll
+                        for (int j = 0; j < (BN / 2) / MN_BOX; ++j)
+                            tma_load_3d_pair(sb + j * (BK * 128), &tm_b, fb, n0 + j * MN_BOX, k0, bb);
+                    }
+                    if (++stage == Cfg::STAGES) { stage = 0; phase ^= 1u; }
+                }
+            }
+        }
+        __syncwarp();
+    } else if (warp == 1) {
+        // ------------------------------------------------------------------ MMA issuer (first CTA)
+        if (leader && elect_one()) {
+            const uint32_t idesc = make_instr_desc(FORMAT, p.a_mn_major, p.b_mn_major, TC2_BM, BN);
+            constexpr uint32_t MN_LAYOUT = IS_BF16 ? SNB_LAYOUT_SWIZZLE_128B : SNB_LAYOUT_SWIZZLE_128B_BASE32B;
+            constexpr uint32_t MN_SBO = IS_BF16 ? 1024 : 512;
+            const uint32_t a_lbo = p.a_mn_major ? BK * 128 : 16;
+            const uint32_t b_lbo = p.b_mn_major ? BK * 128 : 16;
+            const uint32_t a_sbo = p.a_mn_major ? MN_SBO : 1024;
+            const uint32_t b_sbo = p.b_mn_major ? MN_SBO : 1024;
+            const uint32_t a_layout = p.a_mn_major ? MN_LAYOUT : SNB_LAYOUT_SWIZZLE_128B;
+            const uint32_t b_layout = p.b_mn_major ? MN_LAYOUT : SNB_LAYOUT_SWIZZLE_128B;
+            const uint32_t a_kstep = p.a_mn_major ? UMMA_K * 128 : 32;
+            const uint32_t b_kstep = p.b_mn_major ? UMMA_K * 128 : 32;
+            int stage = 0;
+            uint32_t phase = 0;
+            int iter = 0;
+            bool ok = true;
+            bool issued = false;
+            for (int32_t unit = first_unit; unit < p.num_units && ok; unit += unit_step) {
+                const TcUnit u = tc_decode_unit(p, unit, BN, BK, TC2_BM);
+                const int acc = iter & 1;
+                const uint32_t acc_phase = (iter >> 1) & 1;
+                if (!mbar_wait_cluster(smem_addr(&acc_empty[acc]), acc_phase ^ 1u)) { ok = false; break; }
+                tcgen05_fence_after_sync();
+                const uint32_t d_tmem = tmem_base + acc * BN;
+                for (int32_t kb = u.kb_begin; kb < u.kb_end; ++kb) {
+                    if (!mbar_wait_cluster(smem_addr(&full[stage]), phase)) { ok = false; break; }
+                    tcgen05_fence_after_sync();
+                    const uint32_t sa = smem_addr(ring + stage * Cfg::STAGE);
+                    const uint32_t sb = sa + Cfg::STAGE_A;
+#pragma unroll
+                    for (int k = 0; k < BK / UMMA_K; ++k) {
+                        const uint64_t ad = make_smem_desc(sa + k * a_kstep, a_lbo, a_sbo, a_layout);
+                        const uint64_t bd = make_smem_desc(sb + k * b_kstep, b_lbo, b_sbo, b_layout);
+                        const uint32_t accumulate = (kb > u.kb_begin || k > 0) ? 1u : 0u;
+                        if (IS_BF16) umma_bf16_pair(d_tmem, ad, bd, idesc, accumulate);
+                        else umma_tf32_pair(d_tmem, ad, bd, idesc, accumulate);
+                    }
+                    issued = true;
+                    const uint32_t eb = smem_addr(&empty[stage]);
+                    umma_commit_pair(map_to_cta(eb, 0));
+                    umma_commit_pair(map_to_cta(eb, 1));
+                    if (++stage == Cfg::STAGES) { stage = 0; phase ^= 1u; }
+                }
+                if (!ok) break;
+                const uint32_t fb = smem_addr(&acc_full[acc]);
+                umma_commit_pair(map_to_cta(fb, 0));
+                umma_commit_pair(map_to_cta(fb, 1));
+                ++iter;
+            }
+            if (!ok && issued) {
+                umma_commit_pair(map_to_cta(smem_addr(drain), 0));
+                mbar_wait(smem_addr(drain), 0);
+            }
+        }
+        __syncwarp();
+    } else if (warp >= TC_EPI_WARP0) {
+        // ------------------------------------------------------------------ epilogue (both CTAs)
+        const int q = warp & 3;
+        const int group = (warp - TC_EPI_WARP0) >> 2;
+        uint8_t* box = epi + (warp - TC_EPI_WARP0) * TC_EPI_BOX_BYTES;
+        int iter = 0;
+        for (int32_t unit = first_unit; unit < p.num_units; unit += unit_step) {
+            const TcUnit u = tc_decode_unit(p, unit, BN, BK, TC2_BM);
+            const int acc = iter & 1;
+            const uint32_t acc_phase = (iter >> 1) & 1;
+            if (!mbar_wait_cluster(smem_addr(&acc_full[acc]), acc_phase)) break;
+            tcgen05_fence_after_sync();
+            const int32_t row0 = u.m0 + 128 * static_cast<int32_t>(rank) + q * 32;
+            const int32_t row = row0 + lane;
+            const bool first_split = u.split == 0;
+            const int64_t out_base =
+                static_cast<int64_t>(u.batch) * p.out_batch_stride + static_cast<int64_t>(row) * p.N;
+            const uint32_t t_lane = tmem_base + (static_cast<uint32_t>(q * 32) << 16) + acc * BN;
+
+            for (int c = group * CHUNK; c < BN && row0 < p.M && u.n0 + c < p.N; c += 2 * CHUNK) {
+                const int32_t col0 = u.n0 + c;
+                for (int pass = p.has_pre ? 0 : 1; pass < 2; ++pass) {
+                    if (lane == 0) bulk_wait_group_read<0>();
+                    __syncwarp();
+#pragma unroll
+                    for (int h = 0; h < CHUNK / 32; ++h) {
+                        float2 v[16];
+                        epilogue_half<OUT_BF16>(p, t_lane + c + 32 * h, col0 + 32 * h, row, out_base, first_split,
+                                                pass == 0, v);
+                        stage_half<OUT_BF16>(box, lane, h, v);
+                    }
+                    fence_proxy_async_shared();
+                    __syncwarp();
+                    if (lane == 0) {
+                        if (pass == 0) tma_store_3d(&tm_pre, smem_addr(box), col0, row0, u.batch);
+                        else if (p.reduce) tma_reduce_add_3d(&tm_c, smem_addr(box), col0, row0, u.batch);
+                        else tma_store_3d(&tm_c, smem_addr(box), col0, row0, u.batch);
+                        bulk_commit_group();
+                    }
+                }
+            }
+            tcgen05_fence_before_sync();
+            __syncwarp();
+            if (lane == 0) mbar_arrive_cluster(map_to_cta(smem_addr(&acc_empty[acc]), 0));
+            ++iter;
+        }
+        if (lane == 0) bulk_wait_group<0>();
+        __syncwarp();
+    }
+
+    tcgen05_fence_before_sync();
+    cluster_sync();  // both CTAs are done with the pair's TMEM and with each other's barriers
+    if (warp == 1) {
+        tcgen05_fence_after_sync();
+        tmem_dealloc_pair(tmem_base, Cfg::TMEM_COLS);
+    }
+}
+
+}  // namespace snb

@@ -37,9 +37,10 @@ struct DeviceInfo {
 // Properties of the current device (cached per device).
 int current_device_info(DeviceInfo* info, std::string* err);
 
-// Runs the product on the tcgen05 kernel if its layout allows TMA (unit strides, 16-byte alignment);
-// *launched says whether it did. Returns SNB_OK or an error code (with *err set).
-int tc_gemm_try(cudaStream_t stream, const GemmRequest& r, bool* launched, std::string* err);
+// Runs the product on a tcgen05 kernel if its layout allows TMA (unit strides, 16-byte alignment); *launched
+// says whether it did and *path which kernel (SNB_PATH_TENSOR_CORE or SNB_PATH_TENSOR_CORE_PAIR). Returns SNB_OK
+// or an error code (with *err set).
+int tc_gemm_try(cudaStream_t stream, const GemmRequest& r, bool* launched, int* path, std::string* err);
 
 // Runs the product on the strided SIMT kernel (any layout).
 int simt_gemm(cudaStream_t stream, const GemmRequest& r, std::string* err);

@@ -7,6 +7,7 @@
 #include <mutex>
 
 #include "gemm_tc.cuh"
+#include "gemm_tc_pair.cuh"
 #include "internal.h"
 
 namespace snb {
@@ -131,6 +132,34 @@ int launch_bn(int bn, cudaStream_t s, const CUtensorMap* maps, const TcParams& p
     }
 }
 
+template <typename E, bool OUT_BF16>
+int launch_pair(cudaStream_t stream, const CUtensorMap* m, const TcParams& p, int grid, std::string* err) {
+    constexpr int smem = Tc2Config::SMEM_BYTES;
+    static int configured_device = -1;
+    static std::mutex mu;
+    int dev = 0;
+    cudaGetDevice(&dev);
+    {
+        std::lock_guard<std::mutex> lock(mu);
+        if (configured_device != dev) {
+            cudaError_t e = cudaFuncSetAttribute(tc_gemm_pair_kernel<E, OUT_BF16>,
+                                                 cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+            if (e != cudaSuccess) {
+                *err = cuda_message("cudaFuncSetAttribute(tc_gemm_pair_kernel)", e);
+                return SNB_ERR_CUDA;
+            }
+            configured_device = dev;
+        }
+    }
+    tc_gemm_pair_kernel<E, OUT_BF16><<<grid, TC_THREADS, smem, stream>>>(m[0], m[1], m[2], m[3], m[4], m[5], p);
+    cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess) {
+        *err = cuda_message("tc_gemm_pair_kernel launch", e);
+        return SNB_ERR_CUDA;
+    }
+    return SNB_OK;
+}
+
 // K splits for a problem of `tiles` output tiles and `kb` K slices on `sms` SMs: minimises the critical path
 // ceil(tiles*s/sms) * ceil(kb/s) (waves times slices per unit), keeping at least 4 K slices per split.
 int choose_splits(int64_t tiles, int64_t kb, int sms) {
@@ -151,8 +180,9 @@ int choose_splits(int64_t tiles, int64_t kb, int sms) {
 
 }  // namespace
 
-int tc_gemm_try(cudaStream_t stream, const GemmRequest& r, bool* launched, std::string* err) {
+int tc_gemm_try(cudaStream_t stream, const GemmRequest& r, bool* launched, int* path, std::string* err) {
     *launched = false;
+    *path = SNB_PATH_TENSOR_CORE;
     const snb_product& p = r.p;
     if (p.inner == 0 || p.rows == 0 || p.cols == 0) return SNB_OK;
     if (r.precision != SNB_PRECISION_TF32 && r.precision != SNB_PRECISION_BF16) return SNB_OK;
@@ -196,14 +226,23 @@ int tc_gemm_try(cudaStream_t stream, const GemmRequest& r, bool* launched, std::
 
     const int bn = p.cols <= 64 ? 64 : (p.cols <= 128 ? 128 : 256);
     const int bk = 128 / esize;
-    const int64_t m_tiles = (p.rows + TC_BM - 1) / TC_BM;
+    // Wide, tall products with long K run on CTA pairs (256 x 256 tiles, a third less L2 traffic per FLOP). With
+    // short K (K=768: 12 slices per tile) a pair's main loop must wait for the slower of its two CTAs' epilogues,
+    // which costs more than the pair saves (measured on the training step's shapes), so those stay on single
+    // CTAs. The causal attention hints are implemented by the single-CTA kernel only.
+    constexpr int64_t kPairMinKBytes = 4096;  // K >= 2048 bf16 / 1024 f32
+    const bool pair = bn == 256 && p.rows > TC_BM && r.causal == SNB_CAUSAL_NONE && dev.sm_count >= 2 &&
+                      static_cast<int64_t>(p.inner) * esize >= kPairMinKBytes;
+    const int bm = pair ? TC2_BM : TC_BM;
+    const int workers = pair ? dev.sm_count / 2 : dev.sm_count;
+    const int64_t m_tiles = (p.rows + bm - 1) / bm;
     const int64_t n_tiles = (p.cols + bn - 1) / bn;
     const int64_t k_blocks = (p.inner + bk - 1) / bk;
     const int64_t tiles = static_cast<int64_t>(r.count) * m_tiles * n_tiles;
     if (tiles > (1ll << 30)) return SNB_OK;
     const bool plain_epilogue =
         !out_bf16 && r.activation == SNB_ACTIVATION_NONE && r.pre == nullptr && r.causal == SNB_CAUSAL_NONE;
-    const int splits = plain_epilogue ? choose_splits(tiles, k_blocks, dev.sm_count) : 1;
+    const int splits = plain_epilogue ? choose_splits(tiles, k_blocks, workers) : 1;
     const int64_t kb_per_split = (k_blocks + splits - 1) / splits;
     const int64_t splits_used = (k_blocks + kb_per_split - 1) / kb_per_split;  // every split has >= 1 slice
 
@@ -231,7 +270,8 @@ int tc_gemm_try(cudaStream_t stream, const GemmRequest& r, bool* launched, std::
             return SNB_OK;
     } else {
         if (!encode_3d(&tb, in_dt, esize, r.B, p.inner, p.cols, lb.batched ? r.count : 1, lb.ld,
-                       lb.batched ? p.right.batch_stride : lb.ld * p.cols, bk, static_cast<uint32_t>(bn), err))
+                       lb.batched ? p.right.batch_stride : lb.ld * p.cols, bk, static_cast<uint32_t>(pair ? bn / 2 : bn),
+                       err))
             return SNB_OK;
     }
     const CUtensorMapDataType out_dt = out_bf16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT32;
@@ -312,6 +352,20 @@ int tc_gemm_try(cudaStream_t stream, const GemmRequest& r, bool* launched, std::
     kp.causal = r.causal;
     kp.causal_offset = r.causal_offset;
 
+    if (pair) {
+        const int grid = 2 * static_cast<int>(std::min<int64_t>(units, workers));
+        if (bf16_in) {
+            rc = out_bf16 ? launch_pair<__nv_bfloat16, true>(stream, maps, kp, grid, err)
+                          : launch_pair<__nv_bfloat16, false>(stream, maps, kp, grid, err);
+        } else {
+            rc = launch_pair<float, false>(stream, maps, kp, grid, err);
+        }
+        if (rc == SNB_OK) {
+            *launched = true;
+            *path = SNB_PATH_TENSOR_CORE_PAIR;
+        }
+        return rc;
+    }
     const int grid = static_cast<int>(std::min<int64_t>(units, dev.sm_count));
     if (bf16_in) {
         rc = out_bf16 ? launch_bn<__nv_bfloat16, true>(bn, stream, maps, kp, grid, err)

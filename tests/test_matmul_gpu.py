@@ -90,7 +90,7 @@ def test_matmul_matches_reference_for_every_storage_and_kernel(gpu, rows, cols, 
             elif (rows, cols, inner) in TMA_SIZES:
                 esize = 2 if kernel is MatmulKernel.BF16_TENSOR_CORE else 4
                 if tma_eligible(spec, esize):
-                    assert path == _ffi.PATH_TENSOR_CORE, f"{kernel} {spec} did not take the tensor-core path"
+                    assert path in _ffi.TENSOR_CORE_PATHS, f"{kernel} {spec} did not take the tensor-core path"
     gpu.device_status()
 
 
@@ -104,7 +104,7 @@ def test_bf16_tensor_core_is_exact_up_to_summation_order(gpu, lt, rt):
     initial = o.lcg_values(batch * rows * cols, 6)
     expected = expected_product(spec, left, right, initial)
     actual, path = run_on_gpu(gpu, MatmulKernel.BF16_TENSOR_CORE, spec, left, right, initial)
-    assert path == _ffi.PATH_TENSOR_CORE
+    assert path in _ffi.TENSOR_CORE_PATHS
     assert o.relative_error(expected, actual) < 2e-5
 
 
@@ -117,7 +117,7 @@ def test_tf32_rounding_of_the_tensor_core_path(gpu):
     right = o.lcg_values(inner * cols, 8)
     zero = np.zeros(rows * cols, np.float32)
     actual, path = run_on_gpu(gpu, MatmulKernel.TENSOR_CORE, spec, left, right, zero)
-    assert path == _ffi.PATH_TENSOR_CORE
+    assert path in _ffi.TENSOR_CORE_PATHS
     exact = expected_product(spec, left, right, zero)
     rounded = expected_product(spec, o.round_tf32(left), o.round_tf32(right), zero)
     err_exact = o.relative_error(exact, actual)
@@ -150,7 +150,7 @@ def test_model_shaped_products(gpu, case):
     o.matmul_rows(to_oracle(spec), 1, left, right, expected, 0, spec.rows)
     for kernel in (MatmulKernel.TENSOR_CORE, MatmulKernel.BF16_TENSOR_CORE):
         actual, path = run_on_gpu(gpu, kernel, spec, left, right, initial)
-        assert path == _ffi.PATH_TENSOR_CORE
+        assert path in _ffi.TENSOR_CORE_PATHS
         assert o.relative_error(expected, actual) < kernel.tolerance()
         assert o.relative_frobenius(expected, actual) < (2e-3 if kernel is MatmulKernel.TENSOR_CORE else 1e-2)
     gpu.device_status()
@@ -194,11 +194,11 @@ def test_batched_attention_products_match_the_reference_layouts(gpu):
     qt, kt, vt = (torch.from_numpy(a).cuda() for a in (q, k, v))
     scores = torch.zeros(count * S, S, device="cuda")
     gpu.matmul(scores_spec, qt, kt, scores)
-    assert _ffi.last_path() == _ffi.PATH_TENSOR_CORE
+    assert _ffi.last_path() in _ffi.TENSOR_CORE_PATHS
     gpu.causal_softmax(scores, S, scale, 0)
     ctx = torch.zeros(count * S * d, device="cuda")
     gpu.matmul(mix_spec, scores, vt, ctx)
-    assert _ffi.last_path() == _ffi.PATH_TENSOR_CORE
+    assert _ffi.last_path() in _ffi.TENSOR_CORE_PATHS
     torch.cuda.synchronize()
     assert o.relative_error(exp_scores, scores.cpu().numpy().ravel()) < 2e-3
     assert o.relative_error(exp_ctx, ctx.cpu().numpy()) < 2e-3
@@ -257,7 +257,7 @@ def test_fused_linear_forward_bias_gelu_and_residual(gpu, out_dtype):
     out = torch.empty(T * f, device="cuda", dtype=odt)
     pre_t = torch.empty(T * f, device="cuda", dtype=odt)
     gpu.gemm(spec, xt, wt, out, bias=bt, activation=_ffi.ACTIVATION_GELU, pre_activation=pre_t, residual=rt)
-    assert _ffi.last_path() == _ffi.PATH_TENSOR_CORE
+    assert _ffi.last_path() in _ffi.TENSOR_CORE_PATHS
     torch.cuda.synchronize()
     if out_dtype == "bf16":
         res_used = rt.float().cpu().numpy()
@@ -282,7 +282,7 @@ def test_fused_gelu_backward_epilogue(gpu):
     out = torch.empty(T * f, device="cuda")
     gpu.gemm(spec, torch.from_numpy(dy).cuda().bfloat16(), torch.from_numpy(w2).cuda().bfloat16(), out,
              activation=_ffi.ACTIVATION_GELU_GRAD, gelu_input=torch.from_numpy(pre).cuda())
-    assert _ffi.last_path() == _ffi.PATH_TENSOR_CORE
+    assert _ffi.last_path() in _ffi.TENSOR_CORE_PATHS
     torch.cuda.synchronize()
     assert o.relative_error(expected, out.cpu().numpy()) < 1e-4
 
@@ -312,6 +312,84 @@ def test_bounded_wait_gives_up_and_the_context_stays_usable(gpu):
     left, right = o.lcg_values(128 * 64, 1), o.lcg_values(64 * 256, 2)
     zero = np.zeros(128 * 256, np.float32)
     actual, path = run_on_gpu(gpu, MatmulKernel.TENSOR_CORE, spec, left, right, zero)
-    assert path == _ffi.PATH_TENSOR_CORE
+    assert path in _ffi.TENSOR_CORE_PATHS
     assert o.relative_error(expected_product(spec, left, right, zero), actual) < MatmulKernel.TENSOR_CORE.tolerance()
+    gpu.device_status()
+
+
+PAIR_SIZES = [(300, 264, 2056), (257, 520, 2048), (1024, 768, 4096)]
+
+
+@pytest.mark.parametrize("rows,cols,inner", PAIR_SIZES)
+@pytest.mark.parametrize("batch", [1, 3])
+def test_cta_pair_kernel_matches_reference_for_every_storage(gpu, rows, cols, inner, batch):
+    """Long-K products run on CTA pairs (cta_group::2): every storage, batched, scale + accumulate, against the
+    oracle on the same bf16-rounded inputs (summation order only) and on f32 inputs in tf32."""
+    for spec in variants(rows, cols, inner, batch):
+        left = o.lcg_values(batch * rows * inner, 1)
+        right = o.lcg_values(batch * inner * cols, 2)
+        initial = o.lcg_values(batch * rows * cols, 3)
+        lb, _ = o.round_bf16(left)
+        rb, _ = o.round_bf16(right)
+        expected = initial.copy()
+        o.matmul_rows(to_oracle(spec), batch, lb, rb, expected, 0, rows)
+        actual, path = run_on_gpu(gpu, MatmulKernel.BF16_TENSOR_CORE, spec, lb, rb, initial)
+        assert path == _ffi.PATH_TENSOR_CORE_PAIR, f"{spec} did not run on CTA pairs"
+        assert o.relative_error(expected, actual) < 2e-5, spec
+        expected = initial.copy()
+        o.matmul_rows(to_oracle(spec), batch, left, right, expected, 0, rows)
+        actual, path = run_on_gpu(gpu, MatmulKernel.TENSOR_CORE, spec, left, right, initial)
+        assert path == _ffi.PATH_TENSOR_CORE_PAIR
+        assert o.relative_error(expected, actual) < MatmulKernel.TENSOR_CORE.tolerance(), spec
+    gpu.device_status()
+
+
+@pytest.mark.parametrize("epilogue", ["bias_residual_bf16", "gelu_pre_bf16", "gelu_grad_f32", "split_k_overwrite"])
+def test_cta_pair_kernel_fused_epilogues(gpu, epilogue):
+    """The pair kernel's epilogue (the single-CTA code on each CTA's 128 rows) with every fused option."""
+    T, n, k = 384, 520, 2048
+    x = o.lcg_values(T * k, 71)
+    w = o.lcg_values(k * n, 72) * 0.05
+    b = o.lcg_values(n, 73)
+    res = o.lcg_values(T * n, 74)
+    gin = o.lcg_values(T * n, 75) * 2
+    xb, _ = o.round_bf16(x)
+    wb, _ = o.round_bf16(w)
+    spec = MatmulSpec.new(T, n, k)
+    acc = np.zeros(T * n, np.float32)
+    o.matmul_rows(to_oracle(spec), 1, xb, wb, acc, 0, T)
+    xt, wt = torch.from_numpy(x).cuda().bfloat16(), torch.from_numpy(w).cuda().bfloat16()
+    if epilogue == "bias_residual_bf16":
+        rt = torch.from_numpy(res).cuda().bfloat16()
+        out = torch.empty(T * n, device="cuda", dtype=torch.bfloat16)
+        gpu.gemm(spec, xt, wt, out, bias=torch.from_numpy(b).cuda(), residual=rt)
+        expected = acc + np.tile(b, T) + rt.float().cpu().numpy()
+        tol = 1e-2
+    elif epilogue == "gelu_pre_bf16":
+        out = torch.empty(T * n, device="cuda", dtype=torch.bfloat16)
+        pre = torch.empty(T * n, device="cuda", dtype=torch.bfloat16)
+        gpu.gemm(spec, xt, wt, out, bias=torch.from_numpy(b).cuda(), activation=_ffi.ACTIVATION_GELU,
+                 pre_activation=pre)
+        expected = o.gelu(acc + np.tile(b, T))
+        assert o.relative_error(acc + np.tile(b, T), pre.float().cpu().numpy()) < 1e-2
+        tol = 1e-2
+    elif epilogue == "gelu_grad_f32":
+        out = torch.empty(T * n, device="cuda")
+        gpu.gemm(spec, xt, wt, out, activation=_ffi.ACTIVATION_GELU_GRAD, gelu_input=torch.from_numpy(gin).cuda())
+        expected = acc * o.gelu_derivative(gin)
+        tol = 1e-4
+    else:
+        spec = MatmulSpec.new(n, T, k)  # rows 520 x cols 384: few tiles, K split across the grid
+        acc = np.zeros(n * T, np.float32)
+        wt2 = torch.from_numpy(o.lcg_values(n * k, 76)).cuda().bfloat16()
+        xt2 = torch.from_numpy(o.lcg_values(k * T, 77)).cuda().bfloat16()
+        o.matmul_rows(to_oracle(spec), 1, wt2.float().cpu().numpy().ravel(), xt2.float().cpu().numpy().ravel(), acc,
+                      0, n)
+        out = torch.full((n * T,), 5.0, device="cuda")
+        gpu.gemm(spec, wt2, xt2, out)
+        expected = acc
+        tol = 2e-5
+    assert _ffi.last_path() == _ffi.PATH_TENSOR_CORE_PAIR
+    torch.cuda.synchronize()
+    assert o.relative_error(expected, out.float().cpu().numpy()) < tol
     gpu.device_status()
