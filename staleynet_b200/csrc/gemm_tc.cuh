@@ -66,13 +66,15 @@ struct TcParams {
     int64_t causal_offset;    // query q sees keys 0..=q+causal_offset
 };
 
-template <int BN>
+// NBOX = staging boxes per epilogue warp: 2 lets a chunk be staged while the previous chunk's TMA store still reads
+// its box (worth it for GELU epilogues), at the price of one ring stage for BN = 256.
+template <int BN, int NBOX>
 struct TcConfig {
     static constexpr int STAGE_A = TC_BM * 128;
     static constexpr int STAGE_B = BN * 128;
     static constexpr int STAGE = STAGE_A + STAGE_B;
-    static constexpr int STAGES = BN == 256 ? 4 : (BN == 128 ? 6 : 8);
-    static constexpr int EPI_BYTES = TC_EPI_WARPS * TC_EPI_BOX_BYTES;  // one staging box per epilogue warp
+    static constexpr int STAGES = BN == 256 ? (NBOX == 2 ? 3 : 4) : (BN == 128 ? 4 : 6);
+    static constexpr int EPI_BYTES = TC_EPI_WARPS * NBOX * TC_EPI_BOX_BYTES;
     static constexpr int TMEM_COLS = 2 * BN;
     static constexpr int BARRIER_BYTES = 256;
     static constexpr int SMEM_BYTES = 1024 + STAGES * STAGE + EPI_BYTES + BARRIER_BYTES;
@@ -244,12 +246,14 @@ __device__ __forceinline__ void stage_half(uint8_t* box, int lane, int h, const 
 }
 
 // The epilogue function for 32 columns [col, col + 32) of one output row, starting from the TMEM accumulator:
-//   x = scale * acc + bias;  pre_only: return x;  y = activation(x) (+ residual).
+//   x = scale * acc + bias;  (x staged into pre_box when given);  pre_only: return x;
+//   y = activation(x) (+ residual).
 // The first auxiliary input (GELU input, else residual) is requested before waiting for TMEM so the two latencies
 // overlap; only when both are present is the residual read afterwards.
 template <bool OUT_BF16>
 __device__ __forceinline__ void epilogue_half(const TcParams& p, uint32_t taddr, int32_t col, int32_t row,
-                                              int64_t out_base, bool first_split, bool pre_only, float2 (&v)[16]) {
+                                              int64_t out_base, bool first_split, uint8_t* pre_box, int h,
+                                              float2 (&v)[16], bool pre_only) {
     uint32_t x[32];
     tmem_load_32x32b_x32(taddr, x);
     const int valid = p.N - col;  // columns of this piece inside the matrix (a multiple of 4 or 8)
@@ -276,6 +280,7 @@ __device__ __forceinline__ void epilogue_half(const TcParams& p, uint32_t taddr,
             v[2 * j + 1] = __fadd2_rn(v[2 * j + 1], make_float2(b.z, b.w));
         }
     }
+    if (pre_box != nullptr) stage_half<OUT_BF16>(pre_box, threadIdx.x & 31, h, v);  // x before the activation
     if (pre_only) return;
     if (p.activation == 1) {
 #pragma unroll
@@ -295,20 +300,84 @@ __device__ __forceinline__ void epilogue_half(const TcParams& p, uint32_t taddr,
     }
 }
 
-template <typename E, int BN, bool OUT_BF16>
+// One epilogue warp's share of a finished accumulator tile: the column chunks c = group*CHUNK, +2*CHUNK, ... of
+// its 32 rows. Each chunk is staged in a 128-byte-row box and written by a TMA store (or reduce-add). With two boxes
+// they alternate, so staging one chunk overlaps the TMA engine's read of the previous one, and a GELU forward that
+// keeps its pre-activation writes both boxes from one TMEM read; with one box the pre-activation is staged and
+// stored first, then the output from a second TMEM read.
+template <bool OUT_BF16, int BN, int NBOX>
+__device__ __forceinline__ void epilogue_tile(const TcParams& p, const CUtensorMap* tm_c, const CUtensorMap* tm_pre,
+                                              const TcUnit& u, int32_t row0, uint32_t t_lane, int group,
+                                              uint8_t* boxes, int& ebox) {
+    constexpr int CHUNK = OUT_BF16 ? 64 : 32;
+    const int lane = threadIdx.x & 31;
+    const int32_t row = row0 + lane;
+    const bool first_split = u.split == 0;
+    const int64_t out_base = static_cast<int64_t>(u.batch) * p.out_batch_stride + static_cast<int64_t>(row) * p.N;
+    for (int c = group * CHUNK; c < BN && row0 < p.M && u.n0 + c < p.N; c += 2 * CHUNK) {
+        const int32_t col0 = u.n0 + c;
+        if constexpr (NBOX == 2) {
+            uint8_t* box = boxes + ebox * TC_EPI_BOX_BYTES;
+            uint8_t* pre_box = p.has_pre ? boxes + (ebox ^ 1) * TC_EPI_BOX_BYTES : nullptr;
+            if (lane == 0) {
+                if (p.has_pre) bulk_wait_group_read<0>();  // both boxes are rewritten
+                else bulk_wait_group_read<1>();            // only the store before last used this box
+            }
+            __syncwarp();
+#pragma unroll
+            for (int h = 0; h < CHUNK / 32; ++h) {
+                float2 v[16];
+                epilogue_half<OUT_BF16>(p, t_lane + c + 32 * h, col0 + 32 * h, row, out_base, first_split, pre_box,
+                                        h, v, false);
+                stage_half<OUT_BF16>(box, lane, h, v);
+            }
+            fence_proxy_async_shared();
+            __syncwarp();
+            if (lane == 0) {
+                if (pre_box != nullptr) tma_store_3d(tm_pre, smem_addr(pre_box), col0, row0, u.batch);
+                if (p.reduce) tma_reduce_add_3d(tm_c, smem_addr(box), col0, row0, u.batch);
+                else tma_store_3d(tm_c, smem_addr(box), col0, row0, u.batch);
+                bulk_commit_group();
+            }
+            if (!p.has_pre) ebox ^= 1;
+        } else {
+            uint8_t* box = boxes;
+            for (int pass = p.has_pre ? 0 : 1; pass < 2; ++pass) {
+                if (lane == 0) bulk_wait_group_read<0>();  // the box's previous TMA store has read it
+                __syncwarp();
+#pragma unroll
+                for (int h = 0; h < CHUNK / 32; ++h) {
+                    float2 v[16];
+                    epilogue_half<OUT_BF16>(p, t_lane + c + 32 * h, col0 + 32 * h, row, out_base, first_split,
+                                            nullptr, h, v, pass == 0);
+                    stage_half<OUT_BF16>(box, lane, h, v);
+                }
+                fence_proxy_async_shared();
+                __syncwarp();
+                if (lane == 0) {
+                    if (pass == 0) tma_store_3d(tm_pre, smem_addr(box), col0, row0, u.batch);
+                    else if (p.reduce) tma_reduce_add_3d(tm_c, smem_addr(box), col0, row0, u.batch);
+                    else tma_store_3d(tm_c, smem_addr(box), col0, row0, u.batch);
+                    bulk_commit_group();
+                }
+            }
+        }
+    }
+}
+
+template <typename E, int BN, bool OUT_BF16, int NBOX>
 __global__ void __launch_bounds__(TC_THREADS, 1)
     tc_gemm_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constant__ CUtensorMap tm_b,
                    const __grid_constant__ CUtensorMap tm_c, const __grid_constant__ CUtensorMap tm_pre,
                    const __grid_constant__ CUtensorMap tm_res, const __grid_constant__ CUtensorMap tm_gin,
                    const TcParams p) {
-    using Cfg = TcConfig<BN>;
+    using Cfg = TcConfig<BN, NBOX>;
     constexpr int ESIZE = sizeof(E);
     constexpr int BK = 128 / ESIZE;      // K elements per ring slot (one 128-byte swizzle row)
     constexpr int UMMA_K = 32 / ESIZE;   // K elements per tcgen05.mma (32 bytes)
     constexpr int MN_BOX = 128 / ESIZE;  // M/N elements per 128-byte row of an MN-major box
     constexpr bool IS_BF16 = ESIZE == 2;
     constexpr uint32_t FORMAT = IS_BF16 ? 1u : 2u;  // instruction-descriptor A/B format: bf16 = 1, tf32 = 2
-    constexpr int CHUNK = OUT_BF16 ? 64 : 32;       // output columns per staged 128-byte box row
 
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -459,7 +528,8 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
         // quadrant take alternate chunks of the tile's columns.
         const int q = warp & 3;
         const int group = (warp - TC_EPI_WARP0) >> 2;
-        uint8_t* box = epi + (warp - TC_EPI_WARP0) * TC_EPI_BOX_BYTES;
+        uint8_t* boxes = epi + (warp - TC_EPI_WARP0) * NBOX * TC_EPI_BOX_BYTES;
+        int ebox = 0;
         int iter = 0;
         for (int32_t unit = blockIdx.x; unit < p.num_units; unit += gridDim.x) {
             const TcUnit u = tc_decode_unit(p, unit, BN, BK);
@@ -469,36 +539,9 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
             if (!mbar_wait(smem_addr(&acc_full[acc]), acc_phase)) break;
             tcgen05_fence_after_sync();
             const int32_t row0 = u.m0 + q * 32;
-            const int32_t row = row0 + lane;
-            const bool first_split = u.split == 0;
-            const int64_t out_base =
-                static_cast<int64_t>(u.batch) * p.out_batch_stride + static_cast<int64_t>(row) * p.N;
             const uint32_t t_lane = tmem_base + (static_cast<uint32_t>(q * 32) << 16) + acc * BN;
 
-            for (int c = group * CHUNK; c < BN && row0 < p.M && u.n0 + c < p.N; c += 2 * CHUNK) {
-                const int32_t col0 = u.n0 + c;
-                // Pass 0 writes the pre-activation box (GELU forward with pre_activation), pass 1 the output box;
-                // pass 0 re-reads nothing but TMEM, so no row of values is held across passes.
-                for (int pass = p.has_pre ? 0 : 1; pass < 2; ++pass) {
-                    if (lane == 0) bulk_wait_group_read<0>();  // the box's previous TMA store has read it
-                    __syncwarp();
-#pragma unroll
-                    for (int h = 0; h < CHUNK / 32; ++h) {
-                        float2 v[16];
-                        epilogue_half<OUT_BF16>(p, t_lane + c + 32 * h, col0 + 32 * h, row, out_base, first_split,
-                                                pass == 0, v);
-                        stage_half<OUT_BF16>(box, lane, h, v);
-                    }
-                    fence_proxy_async_shared();
-                    __syncwarp();
-                    if (lane == 0) {
-                        if (pass == 0) tma_store_3d(&tm_pre, smem_addr(box), col0, row0, u.batch);
-                        else if (p.reduce) tma_reduce_add_3d(&tm_c, smem_addr(box), col0, row0, u.batch);
-                        else tma_store_3d(&tm_c, smem_addr(box), col0, row0, u.batch);
-                        bulk_commit_group();
-                    }
-                }
-            }
+            epilogue_tile<OUT_BF16, BN, NBOX>(p, &tm_c, &tm_pre, u, row0, t_lane, group, boxes, ebox);
             tcgen05_fence_before_sync();
             __syncwarp();
             if (lane == 0) mbar_arrive(smem_addr(&acc_empty[acc]));

@@ -25,7 +25,7 @@ struct Tc2Config {
     static constexpr int STAGE_B = (TC2_BN / 2) * 128;
     static constexpr int STAGE = STAGE_A + STAGE_B;
     static constexpr int STAGES = 6;
-    static constexpr int EPI_BYTES = TC_EPI_WARPS * TC_EPI_BOX_BYTES;
+    static constexpr int EPI_BYTES = TC_EPI_WARPS * TC_EPI_BOX_BYTES;  // one staging box per epilogue warp
     static constexpr int TMEM_COLS = 2 * TC2_BN;
     static constexpr int BARRIER_BYTES = 256;
     static constexpr int SMEM_BYTES = 1024 + STAGES * STAGE + EPI_BYTES + BARRIER_BYTES;
@@ -46,7 +46,6 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(TC_THREADS, 1)
     constexpr int MN_BOX = 128 / ESIZE;
     constexpr bool IS_BF16 = ESIZE == 2;
     constexpr uint32_t FORMAT = IS_BF16 ? 1u : 2u;
-    constexpr int CHUNK = OUT_BF16 ? 64 : 32;
 
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -198,7 +197,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(TC_THREADS, 1)
         // ------------------------------------------------------------------ epilogue (both CTAs)
         const int q = warp & 3;
         const int group = (warp - TC_EPI_WARP0) >> 2;
-        uint8_t* box = epi + (warp - TC_EPI_WARP0) * TC_EPI_BOX_BYTES;
+        uint8_t* boxes = epi + (warp - TC_EPI_WARP0) * TC_EPI_BOX_BYTES;
+        int ebox = 0;
         int iter = 0;
         for (int32_t unit = first_unit; unit < p.num_units; unit += unit_step) {
             const TcUnit u = tc_decode_unit(p, unit, BN, BK, TC2_BM);
@@ -207,34 +207,9 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(TC_THREADS, 1)
             if (!mbar_wait_cluster(smem_addr(&acc_full[acc]), acc_phase)) break;
             tcgen05_fence_after_sync();
             const int32_t row0 = u.m0 + 128 * static_cast<int32_t>(rank) + q * 32;
-            const int32_t row = row0 + lane;
-            const bool first_split = u.split == 0;
-            const int64_t out_base =
-                static_cast<int64_t>(u.batch) * p.out_batch_stride + static_cast<int64_t>(row) * p.N;
             const uint32_t t_lane = tmem_base + (static_cast<uint32_t>(q * 32) << 16) + acc * BN;
 
-            for (int c = group * CHUNK; c < BN && row0 < p.M && u.n0 + c < p.N; c += 2 * CHUNK) {
-                const int32_t col0 = u.n0 + c;
-                for (int pass = p.has_pre ? 0 : 1; pass < 2; ++pass) {
-                    if (lane == 0) bulk_wait_group_read<0>();
-                    __syncwarp();
-#pragma unroll
-                    for (int h = 0; h < CHUNK / 32; ++h) {
-                        float2 v[16];
-                        epilogue_half<OUT_BF16>(p, t_lane + c + 32 * h, col0 + 32 * h, row, out_base, first_split,
-                                                pass == 0, v);
-                        stage_half<OUT_BF16>(box, lane, h, v);
-                    }
-                    fence_proxy_async_shared();
-                    __syncwarp();
-                    if (lane == 0) {
-                        if (pass == 0) tma_store_3d(&tm_pre, smem_addr(box), col0, row0, u.batch);
-                        else if (p.reduce) tma_reduce_add_3d(&tm_c, smem_addr(box), col0, row0, u.batch);
-                        else tma_store_3d(&tm_c, smem_addr(box), col0, row0, u.batch);
-                        bulk_commit_group();
-                    }
-                }
-            }
+            epilogue_tile<OUT_BF16, BN, 1>(p, &tm_c, &tm_pre, u, row0, t_lane, group, boxes, ebox);
             tcgen05_fence_before_sync();
             __syncwarp();
             if (lane == 0) mbar_arrive_cluster(map_to_cta(smem_addr(&acc_empty[acc]), 0));

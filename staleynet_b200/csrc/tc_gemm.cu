@@ -92,11 +92,11 @@ bool encode_3d(CUtensorMap* map, CUtensorMapDataType dt, int esize, const void* 
     return true;
 }
 
-template <typename E, int BN, bool OUT_BF16>
+template <typename E, int BN, bool OUT_BF16, int NBOX>
 int launch(cudaStream_t stream, const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& tc,
            const CUtensorMap& tp, const CUtensorMap& tr, const CUtensorMap& tg, const TcParams& p, int grid,
            std::string* err) {
-    constexpr int smem = TcConfig<BN>::SMEM_BYTES;
+    constexpr int smem = TcConfig<BN, NBOX>::SMEM_BYTES;
     static int configured_device = -1;
     static std::mutex mu;
     int dev = 0;
@@ -105,7 +105,7 @@ int launch(cudaStream_t stream, const CUtensorMap& ta, const CUtensorMap& tb, co
         std::lock_guard<std::mutex> lock(mu);
         // cudaFuncSetAttribute is per device; redo it when the current device changes.
         if (configured_device != dev) {
-            cudaError_t e = cudaFuncSetAttribute(tc_gemm_kernel<E, BN, OUT_BF16>,
+            cudaError_t e = cudaFuncSetAttribute(tc_gemm_kernel<E, BN, OUT_BF16, NBOX>,
                                                  cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
             if (e != cudaSuccess) {
                 *err = cuda_message("cudaFuncSetAttribute(tc_gemm_kernel)", e);
@@ -114,7 +114,7 @@ int launch(cudaStream_t stream, const CUtensorMap& ta, const CUtensorMap& tb, co
             configured_device = dev;
         }
     }
-    tc_gemm_kernel<E, BN, OUT_BF16><<<grid, TC_THREADS, smem, stream>>>(ta, tb, tc, tp, tr, tg, p);
+    tc_gemm_kernel<E, BN, OUT_BF16, NBOX><<<grid, TC_THREADS, smem, stream>>>(ta, tb, tc, tp, tr, tg, p);
     cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess) {
         *err = cuda_message("tc_gemm_kernel launch", e);
@@ -123,12 +123,17 @@ int launch(cudaStream_t stream, const CUtensorMap& ta, const CUtensorMap& tb, co
     return SNB_OK;
 }
 
+// BN = 256 tiles with a GELU / GELU' epilogue stage through two boxes per warp (3 ring stages); other BN = 256
+// tiles keep 4 ring stages and one box. Narrower tiles have room for both.
 template <typename E, bool OUT_BF16>
-int launch_bn(int bn, cudaStream_t s, const CUtensorMap* maps, const TcParams& p, int grid, std::string* err) {
+int launch_bn(int bn, bool heavy_epilogue, cudaStream_t s, const CUtensorMap* m, const TcParams& p, int grid,
+              std::string* err) {
     switch (bn) {
-        case 64: return launch<E, 64, OUT_BF16>(s, maps[0], maps[1], maps[2], maps[3], maps[4], maps[5], p, grid, err);
-        case 128: return launch<E, 128, OUT_BF16>(s, maps[0], maps[1], maps[2], maps[3], maps[4], maps[5], p, grid, err);
-        default: return launch<E, 256, OUT_BF16>(s, maps[0], maps[1], maps[2], maps[3], maps[4], maps[5], p, grid, err);
+        case 64: return launch<E, 64, OUT_BF16, 2>(s, m[0], m[1], m[2], m[3], m[4], m[5], p, grid, err);
+        case 128: return launch<E, 128, OUT_BF16, 2>(s, m[0], m[1], m[2], m[3], m[4], m[5], p, grid, err);
+        default:
+            if (heavy_epilogue) return launch<E, 256, OUT_BF16, 2>(s, m[0], m[1], m[2], m[3], m[4], m[5], p, grid, err);
+            return launch<E, 256, OUT_BF16, 1>(s, m[0], m[1], m[2], m[3], m[4], m[5], p, grid, err);
     }
 }
 
@@ -367,11 +372,12 @@ int tc_gemm_try(cudaStream_t stream, const GemmRequest& r, bool* launched, int* 
         return rc;
     }
     const int grid = static_cast<int>(std::min<int64_t>(units, dev.sm_count));
+    const bool heavy = r.activation != SNB_ACTIVATION_NONE;
     if (bf16_in) {
-        rc = out_bf16 ? launch_bn<__nv_bfloat16, true>(bn, stream, maps, kp, grid, err)
-                      : launch_bn<__nv_bfloat16, false>(bn, stream, maps, kp, grid, err);
+        rc = out_bf16 ? launch_bn<__nv_bfloat16, true>(bn, heavy, stream, maps, kp, grid, err)
+                      : launch_bn<__nv_bfloat16, false>(bn, heavy, stream, maps, kp, grid, err);
     } else {
-        rc = launch_bn<float, false>(bn, stream, maps, kp, grid, err);
+        rc = launch_bn<float, false>(bn, heavy, stream, maps, kp, grid, err);
     }
     if (rc == SNB_OK) *launched = true;
     return rc;
