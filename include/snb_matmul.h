@@ -203,6 +203,18 @@ SNB_API int snb_last_path(void);
  * read completed, else SNB_ERR_DEVICE_TIMEOUT. Synchronizes the device. */
 SNB_API int snb_device_status(void);
 
+/* Causal attention forward in one tcgen05 kernel, without materialising the scores:
+ *   out[b, q, :] = sum over keys k <= q + query_offset (k < keys) of softmax_k(scale * Q[b,q].K[b,k]) V[b,k,:]
+ * — the reference's QK^T product, causal_softmax and P.V product (layers/attention.rs:206-213) composed — and
+ * lse[b, q] = log sum_k exp(scale * Q[b,q].K[b,k]) over the same keys (may be NULL), from which a backward pass can
+ * rebuild the probabilities. q is [count, queries, 64], k and v are [count, keys, 64], all bf16 (16-byte aligned);
+ * out is [count, queries, 64] of out_type (SNB_TYPE_F32 or SNB_TYPE_BF16). head_dim must be 64. Probabilities are
+ * rounded to bf16 for the P.V product (as the bf16 attention products do). No reference counterpart: the reference
+ * always materialises the [queries, keys] scores. */
+SNB_API int snb_causal_attention_forward(void* stream, const uint16_t* q, const uint16_t* k, const uint16_t* v,
+                                         uint64_t count, uint64_t queries, uint64_t keys, uint64_t head_dim,
+                                         float scale, uint64_t query_offset, void* out, int32_t out_type, float* lse);
+
 /* Failure-detection self-test: launches a one-thread kernel that waits on an mbarrier nothing completes, through
  * the bounded wait every tensor-core pipeline wait uses. The wait gives up after limit_ns (at most 1 s), records a
  * timeout in the device status word and the kernel returns normally; a following snb_device_status() reports

@@ -228,6 +228,23 @@ int snb_softmax_backward(void* stream, const float* probabilities, float* grad, 
     return rc == SNB_OK ? rc : fail(rc, err);
 }
 
+int snb_causal_attention_forward(void* stream, const uint16_t* q, const uint16_t* k, const uint16_t* v,
+                                 uint64_t count, uint64_t queries, uint64_t keys, uint64_t head_dim, float scale,
+                                 uint64_t query_offset, void* out, int32_t out_type, float* lse) {
+    t_last_path = SNB_PATH_NONE;
+    if (head_dim != 64) return fail(SNB_ERR_UNSUPPORTED, "causal_attention_forward: head_dim must be 64");
+    if (out_type != SNB_TYPE_F32 && out_type != SNB_TYPE_BF16)
+        return fail(SNB_ERR_INVALID_ARGUMENT, "causal_attention_forward: unknown output type");
+    if (count > 0 && queries > 0 && (q == nullptr || k == nullptr || v == nullptr || out == nullptr))
+        return fail(SNB_ERR_INVALID_ARGUMENT, "causal_attention_forward: null pointer");
+    std::string err;
+    int rc = fused_attention_forward(static_cast<cudaStream_t>(stream), q, k, v, count, queries, keys, scale,
+                                     query_offset, out, out_type, lse, &err);
+    if (rc != SNB_OK) return fail(rc, err);
+    t_last_path = SNB_PATH_TENSOR_CORE;
+    return SNB_OK;
+}
+
 int snb_selftest_bounded_wait(void* stream, uint64_t limit_ns) {
     if (limit_ns == 0 || limit_ns > 1000000000ull)
         return fail(SNB_ERR_INVALID_ARGUMENT, "selftest: limit_ns must lie in (0, 1 s]");

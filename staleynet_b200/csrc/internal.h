@@ -53,6 +53,11 @@ int causal_softmax_backward(cudaStream_t stream, const float* probabilities, flo
                             uint64_t queries, uint64_t cols, uint64_t query_offset, uint16_t* grad_bf16,
                             std::string* err);
 
+// Fused causal attention forward (tcgen05; head_dim 64; bf16 q/k/v [count, rows, 64]).
+int fused_attention_forward(cudaStream_t stream, const void* q, const void* k, const void* v, uint64_t count,
+                            uint64_t queries, uint64_t keys, float scale, uint64_t query_offset, void* out,
+                            int out_type, float* lse, std::string* err);
+
 // Launches a one-thread kernel whose mbarrier wait nothing completes; it gives up after limit_ns.
 int bounded_wait_probe(cudaStream_t stream, uint64_t limit_ns, std::string* err);
 

@@ -6,6 +6,7 @@
 #include <algorithm>
 #include <mutex>
 
+#include "attention_fused.cuh"
 #include "gemm_tc.cuh"
 #include "gemm_tc_pair.cuh"
 #include "internal.h"
@@ -381,6 +382,77 @@ int tc_gemm_try(cudaStream_t stream, const GemmRequest& r, bool* launched, int* 
     }
     if (rc == SNB_OK) *launched = true;
     return rc;
+}
+
+int fused_attention_forward(cudaStream_t stream, const void* q, const void* k, const void* v, uint64_t count,
+                            uint64_t queries, uint64_t keys, float scale, uint64_t query_offset, void* out,
+                            int out_type, float* lse, std::string* err) {
+    if (count == 0 || queries == 0) return SNB_OK;
+    DeviceInfo dev;
+    int rc = current_device_info(&dev, err);
+    if (rc != SNB_OK) return rc;
+    if (dev.major != 10) {
+        *err = "fused attention needs an sm_100 device";
+        return SNB_ERR_UNSUPPORTED;
+    }
+    const uint64_t lim = (1ull << 31) - 256;
+    if (count > lim || queries > lim || keys > lim || keys == 0) {
+        *err = "fused attention: sizes out of range";
+        return SNB_ERR_INVALID_ARGUMENT;
+    }
+    for (const void* ptr : {q, k, v, static_cast<const void*>(out)}) {
+        if (reinterpret_cast<uintptr_t>(ptr) % 16 != 0) {
+            *err = "fused attention: q, k, v and out must be 16-byte aligned";
+            return SNB_ERR_INVALID_ARGUMENT;
+        }
+    }
+    CUtensorMap tq, tk, tv;
+    // [count, rows, 64] bf16, rows 128 bytes apart; boxes of 128 rows x 64 (one 128-byte swizzle row each).
+    if (!encode_3d(&tq, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, q, FA_D, queries, count, FA_D, queries * FA_D, FA_D,
+                   FA_BM, err) ||
+        !encode_3d(&tk, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, k, FA_D, keys, count, FA_D, keys * FA_D, FA_D, FA_BN,
+                   err) ||
+        !encode_3d(&tv, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, v, FA_D, keys, count, FA_D, keys * FA_D, FA_D, FA_BN,
+                   err))
+        return SNB_ERR_INVALID_ARGUMENT;
+    FaParams fp{};
+    fp.count = static_cast<int32_t>(count);
+    fp.sq = static_cast<int32_t>(queries);
+    fp.sk = static_cast<int32_t>(keys);
+    const int64_t q_tiles = (static_cast<int64_t>(queries) + FA_BM - 1) / FA_BM;
+    fp.pairs = static_cast<int32_t>((q_tiles + 1) / 2);
+    fp.offset = static_cast<int64_t>(query_offset);
+    fp.scale_log2 = scale * 1.4426950408889634f;
+    fp.out_bf16 = out_type == SNB_TYPE_BF16;
+    fp.out = out;
+    fp.out_stride = static_cast<int64_t>(queries) * FA_D;
+    fp.lse = lse;
+    const int64_t grid = static_cast<int64_t>(fp.pairs) * static_cast<int64_t>(count);
+    if (grid > 0x7fffffff) {
+        *err = "fused attention: grid too large";
+        return SNB_ERR_UNSUPPORTED;
+    }
+    static int configured_device = -1;
+    static std::mutex mu;
+    {
+        std::lock_guard<std::mutex> lock(mu);
+        if (configured_device != dev.device) {
+            cudaError_t e = cudaFuncSetAttribute(fa_forward_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                                 FaSmem::BYTES);
+            if (e != cudaSuccess) {
+                *err = cuda_message("cudaFuncSetAttribute(fa_forward_kernel)", e);
+                return SNB_ERR_CUDA;
+            }
+            configured_device = dev.device;
+        }
+    }
+    fa_forward_kernel<<<static_cast<unsigned>(grid), FA_THREADS, FaSmem::BYTES, stream>>>(tq, tk, tv, fp);
+    cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess) {
+        *err = cuda_message("fa_forward_kernel launch", e);
+        return SNB_ERR_CUDA;
+    }
+    return SNB_OK;
 }
 
 namespace {

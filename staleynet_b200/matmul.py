@@ -249,6 +249,19 @@ class Gpu:
                                                    queries, cols, query_offset,
                                                    _ptr(grad_bf16) if grad_bf16 is not None else None))
 
+    def causal_attention_forward(self, q, k, v, out, scale: float, query_offset: int = 0, lse=None) -> None:
+        """Fused causal attention forward (snb_causal_attention_forward): q [count, queries, 64], k/v
+        [count, keys, 64] bf16; out f32 or bf16 [count, queries, 64]; lse f32 [count, queries] or None."""
+        import torch
+
+        _require_cuda(q, k, v, out, lse)
+        count, queries, head_dim = q.shape
+        keys = k.shape[1]
+        out_type = _ffi.TYPE_BF16 if out.dtype == torch.bfloat16 else _ffi.TYPE_F32
+        check(self.lib.snb_causal_attention_forward(self._stream_handle(), _ptr(q), _ptr(k), _ptr(v), count, queries,
+                                                    keys, head_dim, scale, query_offset, _ptr(out), out_type,
+                                                    _ptr(lse) if lse is not None else None))
+
     def softmax_backward(self, probabilities, grad) -> None:
         """`Gpu::softmax_backward` (ops/attention.rs:83-100)."""
         _require_cuda(probabilities, grad)

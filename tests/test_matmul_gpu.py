@@ -393,3 +393,41 @@ def test_cta_pair_kernel_fused_epilogues(gpu, epilogue):
     torch.cuda.synchronize()
     assert o.relative_error(expected, out.float().cpu().numpy()) < tol
     gpu.device_status()
+
+
+GOLDEN = __import__("json").loads((__import__("pathlib").Path(__file__).parent / "golden" / "reference_kats.json").read_text())
+
+
+@pytest.mark.parametrize("case", GOLDEN["matmul"], ids=lambda c: c["name"])
+def test_reference_known_answers_on_the_gpu(gpu, case):
+    """The reference's own matmul known answers (reference.rs:177-224) through every arithmetic of the C ABI."""
+    b = case["batch"]
+    spec = MatmulSpec.new(case["rows"], case["cols"], case["inner"]).scaled(case["scale"]).batched(
+        BatchStrides(b["count"], b["left"], b["right"], b["output"]))
+    if case["left_transposed"]:
+        spec = spec.left_transposed()
+    if case["right_transposed"]:
+        spec = spec.right_transposed()
+    if case["accumulate"]:
+        spec = spec.accumulate()
+    for kernel in KERNELS:
+        actual, _ = run_on_gpu(gpu, kernel, spec, np.array(case["left"], np.float32),
+                               np.array(case["right"], np.float32), np.array(case["initial"], np.float32))
+        assert actual.tolist() == case["expected"], kernel  # small integers: exact in every arithmetic
+
+
+@pytest.mark.parametrize("accumulate", [False, True])
+def test_empty_inner_dimension(gpu, accumulate):
+    """K = 0: the reference's loop leaves sum = 0, so C = scale*0 (overwrite) or C unchanged (accumulate)."""
+    spec = MatmulSpec.new(5, 7, 0).scaled(0.5)
+    if accumulate:
+        spec = spec.accumulate()
+    initial = o.lcg_values(35, 9)
+    for kernel in KERNELS:
+        dtype = torch.bfloat16 if kernel is MatmulKernel.BF16_TENSOR_CORE else torch.float32
+        gpu.matmul_kernel = kernel
+        out = torch.from_numpy(initial.copy()).cuda()
+        gpu.matmul(spec, torch.zeros(1, device="cuda", dtype=dtype), torch.zeros(1, device="cuda", dtype=dtype), out)
+        torch.cuda.synchronize()
+        expected = initial if accumulate else np.zeros(35, np.float32)
+        assert np.array_equal(out.cpu().numpy(), expected)
