@@ -208,7 +208,8 @@ SNB_API int snb_device_status(void);
  * — the reference's QK^T product, causal_softmax and P.V product (layers/attention.rs:206-213) composed — and
  * lse[b, q] = log sum_k exp(scale * Q[b,q].K[b,k]) over the same keys (may be NULL), from which a backward pass can
  * rebuild the probabilities. q is [count, queries, 64], k and v are [count, keys, 64], all bf16 (16-byte aligned);
- * out is [count, queries, 64] of out_type (SNB_TYPE_F32 or SNB_TYPE_BF16). head_dim must be 64. Probabilities are
+ * out is [count, queries, 64] of out_type (SNB_TYPE_F32 or SNB_TYPE_BF16). head_dim must be 64 and scale positive
+ * and finite (SNB_ERR_INVALID_ARGUMENT otherwise). Probabilities are
  * rounded to bf16 for the P.V product (as the bf16 attention products do). No reference counterpart: the reference
  * always materialises the [queries, keys] scores. */
 SNB_API int snb_causal_attention_forward(void* stream, const uint16_t* q, const uint16_t* k, const uint16_t* v,

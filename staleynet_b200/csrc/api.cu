@@ -3,6 +3,7 @@
 #include <cuda_runtime.h>
 
 #include <mutex>
+#include <cmath>
 #include <string>
 #include <vector>
 
@@ -235,6 +236,8 @@ int snb_causal_attention_forward(void* stream, const uint16_t* q, const uint16_t
     if (head_dim != 64) return fail(SNB_ERR_UNSUPPORTED, "causal_attention_forward: head_dim must be 64");
     if (out_type != SNB_TYPE_F32 && out_type != SNB_TYPE_BF16)
         return fail(SNB_ERR_INVALID_ARGUMENT, "causal_attention_forward: unknown output type");
+    if (!(scale > 0.0f) || !std::isfinite(scale))
+        return fail(SNB_ERR_INVALID_ARGUMENT, "causal_attention_forward: scale must be positive and finite");
     if (count > 0 && queries > 0 && (q == nullptr || k == nullptr || v == nullptr || out == nullptr))
         return fail(SNB_ERR_INVALID_ARGUMENT, "causal_attention_forward: null pointer");
     std::string err;

@@ -23,6 +23,7 @@ constexpr int FA_BN = 128;   // keys per step
 constexpr int FA_D = 64;     // head dimension
 constexpr int FA_THREADS = 384;
 constexpr int FA_TMEM_COLS = 512;
+constexpr float FA_RESCALE_SLACK = 8.0f;  // log2 of the largest unnormalised probability the softmax lets stand
 
 struct FaParams {
     int32_t count, sq, sk;   // matrices; queries and keys per matrix
@@ -195,72 +196,109 @@ __global__ void __launch_bounds__(FA_THREADS, 1)
         const int r = q * 32 + lane;     // row within the tile
         const int32_t tsteps = t == 0 ? steps0 : steps1;
         const int64_t query = static_cast<int64_t>(q_first) + t * FA_BM + r;
+        // Keys [0, row_end) are visible to this row: key <= query + offset and key < sk (row_end >= 1).
+        const int32_t row_end = static_cast<int32_t>(imin64(query + p.offset, static_cast<int64_t>(p.sk) - 1) + 1);
         const uint32_t lane_base = static_cast<uint32_t>(q * 32) << 16;
         const uint32_t s_tmem = tmem_base + lane_base + t * FA_BN;
         const uint32_t o_tmem = tmem_base + lane_base + 2 * FA_BN + t * FA_D;
         uint8_t* p_tile = p_s + t * FaSmem::P;
-        float m = -1.0e30f;  // running max of scale*log2(e)*score
-        float l = 0.0f;      // running sum of 2^(x - m)
+        const float c = p.scale_log2;
+        const float2 c2 = make_float2(c, c);
+        // Running max m (in units of log2: scale*log2(e)*score) and running sum l of 2^(x - m). m may lag the true
+        // row max by up to FA_RESCALE_SLACK: O and l are only rescaled when some row of the warp outgrows it, which
+        // keeps every exponent <= 2^FA_RESCALE_SLACK and leaves O / l unchanged.
+        float m = -1.0e30f;
+        float l = 0.0f;
         bool ok = true;
         for (int32_t j = 0; j < tsteps && ok; ++j) {
             if (!warp_wait(smem_addr(&s_full[t]), j & 1)) { ok = false; break; }
             tcgen05_fence_after_sync();
-            const int64_t key0 = static_cast<int64_t>(j) * FA_BN;
-            // Keys of this step visible to this row: key <= query + offset and key < sk.
-            const int64_t vis = imin64(imin64(query + p.offset, static_cast<int64_t>(p.sk) - 1) - key0 + 1, FA_BN);
-            // Pass 1: row max.
-            float mx = m;
-            for (int c = 0; c < FA_BN; c += 32) {
-                uint32_t x[32];
-                tmem_load_32x32b_x32(s_tmem + c, x);
+            const int32_t vis = row_end - j * FA_BN;   // visible keys of this step (>= FA_BN: all)
+            // Pass 1: row max of the raw scores (scale > 0, so it commutes with the scaling).
+            float mr[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
+#pragma unroll 1
+            for (int c0 = 0; c0 < FA_BN; c0 += 64) {
+                uint32_t xs[2][32];
+                tmem_load_32x32b_x32(s_tmem + c0, xs[0]);
+                tmem_load_32x32b_x32(s_tmem + c0 + 32, xs[1]);
                 tmem_load_wait();
+const auto X = [&](int i) { return __uint_as_float(xs[i >> 5][i & 31]); };
+                if (vis >= c0 + 64) {
 #pragma unroll
-                for (int i = 0; i < 32; ++i)
-                    if (c + i < vis) mx = fmaxf(mx, __uint_as_float(x[i]) * p.scale_log2);
+                    for (int i = 0; i < 64; ++i) mr[i & 3] = fmaxf(mr[i & 3], X(i));
+                } else {
+#pragma unroll
+                    for (int i = 0; i < 64; ++i)
+                        if (c0 + i < vis) mr[i & 3] = fmaxf(mr[i & 3], X(i));
+                }
             }
+            const float mx = fmaxf(m, fmaxf(fmaxf(mr[0], mr[1]), fmaxf(mr[2], mr[3])) * c);
+            const bool rescale = __any_sync(0xffffffffu, mx > m + FA_RESCALE_SLACK);
+            const float m_use = rescale ? mx : m;
             // P_t may be rewritten (and O_t rescaled) once step j-1's P.V product has finished.
             if (j > 0 && !warp_wait(smem_addr(&o_done[t]), (j - 1) & 1)) { ok = false; break; }
-            // Pass 2: probabilities, their sum, and the bf16 operand of P.V.
-            float sum = 0.0f;
-            for (int c = 0; c < FA_BN; c += 32) {
-                uint32_t x[32];
-                tmem_load_32x32b_x32(s_tmem + c, x);
+            // Pass 2: 2^(x - m), their sum, and the bf16 operand of P.V.
+            const float2 nm2 = make_float2(-m_use, -m_use);
+            float2 sa = make_float2(0.0f, 0.0f), sb = make_float2(0.0f, 0.0f);
+#pragma unroll 1
+            for (int c0 = 0; c0 < FA_BN; c0 += 64) {
+                uint32_t xs[2][32];
+                tmem_load_32x32b_x32(s_tmem + c0, xs[0]);
+                tmem_load_32x32b_x32(s_tmem + c0 + 32, xs[1]);
                 tmem_load_wait();
-                uint32_t w[16];
+const auto X = [&](int i) { return __uint_as_float(xs[i >> 5][i & 31]); };
+                uint32_t w[32];
+                if (vis >= c0 + 64) {
 #pragma unroll
-                for (int i = 0; i < 32; i += 2) {
-                    const float a = (c + i < vis) ? exp2_hw(__uint_as_float(x[i]) * p.scale_log2 - mx) : 0.0f;
-                    const float b = (c + i + 1 < vis) ? exp2_hw(__uint_as_float(x[i + 1]) * p.scale_log2 - mx) : 0.0f;
-                    sum += a + b;
-                    w[i / 2] = pack_bf16x2(a, b);
+                    for (int i = 0; i < 64; i += 4) {
+                        float2 e0 = __ffma2_rn(make_float2(X(i), X(i + 1)), c2, nm2);
+                        float2 e1 = __ffma2_rn(make_float2(X(i + 2), X(i + 3)), c2, nm2);
+                        e0.x = exp2_hw(e0.x);
+                        e0.y = exp2_hw(e0.y);
+                        e1.x = exp2_hw(e1.x);
+                        e1.y = exp2_hw(e1.y);
+                        sa = __fadd2_rn(sa, e0);
+                        sb = __fadd2_rn(sb, e1);
+                        w[i / 2] = pack_bf16x2(e0.x, e0.y);
+                        w[i / 2 + 1] = pack_bf16x2(e1.x, e1.y);
+                    }
+                } else {
+#pragma unroll
+                    for (int i = 0; i < 64; i += 2) {
+                        const float e0 = (c0 + i < vis) ? exp2_hw(fmaf(X(i), c, -m_use)) : 0.0f;
+                        const float e1 = (c0 + i + 1 < vis) ? exp2_hw(fmaf(X(i + 1), c, -m_use)) : 0.0f;
+                        sa = __fadd2_rn(sa, make_float2(e0, e1));
+                        w[i / 2] = pack_bf16x2(e0, e1);
+                    }
                 }
                 // Row r of the K-major 128B-swizzled operand: keys [64s, 64s+64) live in slice s.
-                uint8_t* row = p_tile + (c / 64) * (FaSmem::P / 2) + r * 128;
+                uint8_t* row = p_tile + (c0 / 64) * (FaSmem::P / 2) + r * 128;
 #pragma unroll
-                for (int g = 0; g < 4; ++g) {
-                    const int chunk = ((c % 64) / 8) + g;
-                    *reinterpret_cast<uint4*>(row + ((chunk ^ (r & 7)) << 4)) =
+                for (int g = 0; g < 8; ++g)
+                    *reinterpret_cast<uint4*>(row + ((g ^ (r & 7)) << 4)) =
                         make_uint4(w[4 * g], w[4 * g + 1], w[4 * g + 2], w[4 * g + 3]);
-                }
             }
             tcgen05_fence_before_sync();
             __syncwarp();
             if (lane == 0) mbar_arrive(smem_addr(&s_empty[t]));  // S_t may take the next step's scores
-            const float alpha = exp2_hw(m - mx);
-            if (j > 0 && __any_sync(0xffffffffu, alpha != 1.0f)) {
-                // O_t *= alpha: the row max of some row of this warp grew (the others multiply by 1).
-                for (int c = 0; c < FA_D; c += 32) {
-                    uint32_t o[32];
-                    tmem_load_32x32b_x32(o_tmem + c, o);
-                    tmem_load_wait();
+            if (rescale) {
+                const float alpha = exp2_hw(m - m_use);
+                if (j > 0) {
+                    // O_t *= alpha for the rows of this warp (alpha = 1 for rows whose max did not grow).
+                    for (int c0 = 0; c0 < FA_D; c0 += 32) {
+                        uint32_t o[32];
+                        tmem_load_32x32b_x32(o_tmem + c0, o);
+                        tmem_load_wait();
 #pragma unroll
-                    for (int i = 0; i < 32; ++i) o[i] = __float_as_uint(__uint_as_float(o[i]) * alpha);
-                    tmem_store_32x32b_x32(o_tmem + c, o);
+                        for (int i = 0; i < 32; ++i) o[i] = __float_as_uint(__uint_as_float(o[i]) * alpha);
+                        tmem_store_32x32b_x32(o_tmem + c0, o);
+                    }
+                    tmem_store_wait();
                 }
-                tmem_store_wait();
+                l *= alpha;
+                m = m_use;
             }
-            l = l * alpha + sum;
-            m = mx;
+            l += (sa.x + sa.y) + (sb.x + sb.y);
             fence_proxy_async_shared();  // P_t writes -> the tensor core's reads
             tcgen05_fence_before_sync();
             __syncwarp();
@@ -271,13 +309,13 @@ __global__ void __launch_bounds__(FA_THREADS, 1)
             const float inv = 1.0f / l;
             const bool live = query < p.sq;
             const int64_t base = static_cast<int64_t>(matrix) * p.out_stride + query * FA_D;
-            for (int c = 0; c < FA_D; c += 32) {
+            for (int c0 = 0; c0 < FA_D; c0 += 32) {
                 uint32_t o[32];
-                tmem_load_32x32b_x32(o_tmem + c, o);
+                tmem_load_32x32b_x32(o_tmem + c0, o);
                 tmem_load_wait();
                 if (!live) continue;
                 if (p.out_bf16) {
-                    uint4* dst = reinterpret_cast<uint4*>(reinterpret_cast<uint16_t*>(p.out) + base + c);
+                    uint4* dst = reinterpret_cast<uint4*>(reinterpret_cast<uint16_t*>(p.out) + base + c0);
 #pragma unroll
                     for (int g = 0; g < 4; ++g)
                         dst[g] = make_uint4(pack_bf16x2(__uint_as_float(o[8 * g]) * inv, __uint_as_float(o[8 * g + 1]) * inv),
@@ -285,7 +323,7 @@ __global__ void __launch_bounds__(FA_THREADS, 1)
                                             pack_bf16x2(__uint_as_float(o[8 * g + 4]) * inv, __uint_as_float(o[8 * g + 5]) * inv),
                                             pack_bf16x2(__uint_as_float(o[8 * g + 6]) * inv, __uint_as_float(o[8 * g + 7]) * inv));
                 } else {
-                    float4* dst = reinterpret_cast<float4*>(reinterpret_cast<float*>(p.out) + base + c);
+                    float4* dst = reinterpret_cast<float4*>(reinterpret_cast<float*>(p.out) + base + c0);
 #pragma unroll
                     for (int g = 0; g < 8; ++g)
                         dst[g] = make_float4(__uint_as_float(o[4 * g]) * inv, __uint_as_float(o[4 * g + 1]) * inv,
