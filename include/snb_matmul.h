@@ -216,6 +216,20 @@ SNB_API int snb_causal_attention_forward(void* stream, const uint16_t* q, const 
                                          uint64_t count, uint64_t queries, uint64_t keys, uint64_t head_dim,
                                          float scale, uint64_t query_offset, void* out, int32_t out_type, float* lse);
 
+/* Causal attention backward in tcgen05 kernels, without materialising the [queries, keys] probabilities or their
+ * gradients: given the forward's q, k, v, out (= snb_causal_attention_forward's output, out_type f32 or bf16) and
+ * lse, and the output gradient d_out (bf16, [count, queries, 64]), writes
+ *   dq = scale dS K, dk = scale dS^T Q, dv = P^T dO,  dS = P * (dO V^T - rowsum(dO * out)),
+ * P the causal softmax probabilities rebuilt from lse — the reference's backward (layers/attention.rs:220-267,
+ * kernels/attention.rs:182-207) with rowsum(P * dP) taken as rowsum(dO * out). dq is [count, queries, 64], dk and dv
+ * [count, keys, 64], all f32 and overwritten. P and dS are rounded to bf16 for the products (as the bf16 attention
+ * products do). Uses a stream-ordered scratch buffer of count * queries * 8 bytes (cudaMallocAsync / cudaFreeAsync
+ * on `stream`). No reference counterpart: the reference materialises P and dS. */
+SNB_API int snb_causal_attention_backward(void* stream, const uint16_t* q, const uint16_t* k, const uint16_t* v,
+                                          const void* out, int32_t out_type, const uint16_t* d_out, const float* lse,
+                                          uint64_t count, uint64_t queries, uint64_t keys, uint64_t head_dim,
+                                          float scale, uint64_t query_offset, float* dq, float* dk, float* dv);
+
 /* Failure-detection self-test: launches a one-thread kernel that waits on an mbarrier nothing completes, through
  * the bounded wait every tensor-core pipeline wait uses. The wait gives up after limit_ns (at most 1 s), records a
  * timeout in the device status word and the kernel returns normally; a following snb_device_status() reports

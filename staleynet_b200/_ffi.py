@@ -57,6 +57,7 @@ EXPORTED_SYMBOLS = (
     "snb_last_path",
     "snb_device_status",
     "snb_causal_attention_forward",
+    "snb_causal_attention_backward",
     "snb_selftest_bounded_wait",
     "snb_abi_version",
 )
@@ -151,6 +152,10 @@ def load() -> ctypes.CDLL:
                                                      c_uint64, c_uint64, c_float, c_uint64, c_void_p, c_int32,
                                                      c_void_p]
         lib.snb_causal_attention_forward.restype = c_int
+        lib.snb_causal_attention_backward.argtypes = [c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_int32,
+                                                      c_void_p, c_void_p, c_uint64, c_uint64, c_uint64, c_uint64,
+                                                      c_float, c_uint64, c_void_p, c_void_p, c_void_p]
+        lib.snb_causal_attention_backward.restype = c_int
         lib.snb_selftest_bounded_wait.argtypes = [c_void_p, c_uint64]
         lib.snb_selftest_bounded_wait.restype = c_int
         lib.snb_abi_version.argtypes = []

@@ -1,0 +1,388 @@
+// attention_fused_bwd.cuh — causal attention backward on tcgen05 without materialising the [queries, keys] scores,
+// probabilities or their gradients: the backward of the reference's QK^T product, `causal_softmax` and P.V product
+// (crates/staleynet-model/src/layers/attention.rs:220-267, kernels/attention.rs:182-207):
+//   dP = dO V^T, dV = P^T dO, dS = P * (dP - rowsum(P * dP)), dQ = scale dS K, dK = scale dS^T Q,
+// with P rebuilt per tile from the forward's log-sum-exp (P = exp(scale S - lse)) and rowsum(P * dP) taken as
+// D = rowsum(dO * O), which equals it because O = P V.
+//
+// Two kernels:
+//   fb_rowstats_kernel   per query: (-lse * log2(e), D) into a scratch buffer, one warp per query row.
+//   fb_backward_kernel   one CTA of 448 threads per 128-key tile of one matrix, looping over the query tiles whose
+//                        queries see any of its keys. Keys sit on the TMEM lanes:
+//     warp 12      TMA: K_j, V_j once; then Q_i, dO_i and the row statistics of tile i through a 2-stage ring.
+//     warp 13      allocates TMEM (S^T, dP^T: 128 f32 columns each; dV, dK, dQ: 64 each; P^T: 64 columns of bf16
+//                  pairs) and, on one elected thread, issues per query tile i:
+//                    S^T = K_j Q_i^T, dP^T = V_j dO_i^T          (M=128 keys, N=128 queries, K=64)
+//                    dV += P^T dO_i (P^T from TMEM), dK += dS^T Q_i (M=128 keys, N=64, K=128 queries)
+//                    dQ_i = dS K_j                               (M=128 queries, N=64, K=128 keys)
+//                  dS^T lives once in shared memory as a 128B-swizzled tile whose rows are keys: the dK product reads
+//                  it K-major, the dQ product reads the same bytes M-major (queries contiguous).
+//     warps 0-7    per key row (TMEM lane quadrant warp % 4) and query half (warp / 4): P = 2^(S c + nl),
+//                  dS = P (dP - D), causal and range masks applied, P^T stored bf16 into TMEM, dS^T into shared memory;
+//                  at the end dV and scale * dK written out.
+//     warps 8-11   drain dQ_i from TMEM (queries on lanes), scale it and add it into the global dQ (f32, zeroed by
+//                  the host) with TMA reduce-add, each warp through its own two 128B-swizzled 32x32 staging boxes.
+// Every mbarrier wait is bounded (see sm100_ptx.cuh).
+#pragma once
+
+#include "attention_fused.cuh"
+
+namespace snb {
+
+constexpr int FB_BK = 128;   // keys per CTA (TMEM lanes of S^T, dP^T, dV, dK)
+constexpr int FB_BQ = 128;   // queries per iteration
+constexpr int FB_D = 64;
+constexpr int FB_STAGES = 2;
+constexpr int FB_ELEM_WARPS = 8;
+constexpr int FB_DQ_WARP0 = 8;
+constexpr int FB_PRODUCER_WARP = 12;
+constexpr int FB_MMA_WARP = 13;
+constexpr int FB_THREADS = 14 * 32;
+constexpr int FB_TMEM_COLS = 512;
+constexpr int FB_S_COL = 0, FB_DP_COL = 128, FB_DV_COL = 256, FB_DK_COL = 320, FB_DQ_COL = 384, FB_P_COL = 448;
+
+struct FbParams {
+    int32_t count, sq, sk;   // matrices; queries and keys per matrix
+    int32_t q_tiles;         // query tiles per matrix
+    int64_t offset;          // query q sees keys 0..=q+offset
+    float scale;             // softmax scale
+    float scale_log2;        // scale * log2(e)
+    float* dk;               // [count, sk, 64] f32
+    float* dv;               // [count, sk, 64] f32
+};
+
+struct FbSmem {
+    static constexpr int KV = FB_BK * 128;          // K_j or V_j: 128 rows x 64 bf16
+    static constexpr int QT = FB_BQ * 128;          // Q_i or dO_i
+    static constexpr int STATS = FB_BQ * 8;         // (-lse * log2(e), D) per query
+    static constexpr int STAGE = 2 * QT + STATS;    // 33 KB, a multiple of 1 KB
+    static constexpr int DS = FB_BK * FB_BQ * 2;    // dS^T: two 64-query slices of 128 key rows x 128 bytes
+    static constexpr int DQ = FB_BQ * FB_D * 4;     // dQ staging: per dQ warp two 32x32 f32 boxes (4 KB each)
+    static constexpr int BARS = 256;
+    static constexpr int BYTES = 1024 + 2 * KV + FB_STAGES * STAGE + DS + DQ + BARS;
+    static_assert(STAGE % 1024 == 0, "swizzled tiles need 1 KB alignment");
+    static_assert(BYTES <= 232448, "shared memory budget of one sm_100 CTA");
+};
+
+// Row statistics of the backward: stats[m, 2q] = -lse[m, q] * log2(e), stats[m, 2q + 1] = D[m, q] =
+// sum_d dO[m, q, d] O[m, q, d]. One warp per (matrix, query) row; rows of stats are `stride` floats apart.
+__global__ void fb_rowstats_kernel(const void* out, int32_t out_bf16, const uint16_t* d_out, const float* lse,
+                                   float* stats, int64_t rows, int32_t sq, int64_t stride) {
+    const int64_t row = (static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
+    const int lane = threadIdx.x & 31;
+    if (row >= rows) return;
+    float o0, o1;
+    if (out_bf16) {
+        const uint32_t w = reinterpret_cast<const uint32_t*>(out)[row * 32 + lane];
+        o0 = __uint_as_float(w << 16);
+        o1 = __uint_as_float(w & 0xFFFF0000u);
+    } else {
+        const float2 f = reinterpret_cast<const float2*>(out)[row * 32 + lane];
+        o0 = f.x;
+        o1 = f.y;
+    }
+    const uint32_t g = reinterpret_cast<const uint32_t*>(d_out)[row * 32 + lane];
+    float d = fmaf(__uint_as_float(g << 16), o0, __uint_as_float(g & 0xFFFF0000u) * o1);
+#pragma unroll
+    for (int s = 16; s > 0; s >>= 1) d += __shfl_xor_sync(0xffffffffu, d, s);
+    if (lane == 0) {
+        const int64_t m = row / sq, q = row % sq;
+        stats[m * stride + 2 * q] = -lse[row] * 1.4426950408889634f;
+        stats[m * stride + 2 * q + 1] = d;
+    }
+}
+
+__global__ void __launch_bounds__(FB_THREADS, 1)
+    fb_backward_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
+                       const __grid_constant__ CUtensorMap tm_v, const __grid_constant__ CUtensorMap tm_do,
+                       const __grid_constant__ CUtensorMap tm_stats, const __grid_constant__ CUtensorMap tm_dq,
+                       const FbParams p) {
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    uint8_t* k_s = smem;
+    uint8_t* v_s = k_s + FbSmem::KV;
+    uint8_t* stage_s = v_s + FbSmem::KV;                        // FB_STAGES x (Q_i, dO_i, stats)
+    uint8_t* ds_s = stage_s + FB_STAGES * FbSmem::STAGE;
+    uint8_t* dq_s = ds_s + FbSmem::DS;
+    uint64_t* bars = reinterpret_cast<uint64_t*>(dq_s + FbSmem::DQ);
+    uint64_t* kv_full = bars;
+    uint64_t* qdo_full = bars + 1;                // [FB_STAGES]
+    uint64_t* qdo_empty = qdo_full + FB_STAGES;   // [FB_STAGES]
+    uint64_t* sdp_full = qdo_empty + FB_STAGES;   // S^T and dP^T computed
+    uint64_t* sdp_empty = sdp_full + 1;           // ... and read by the elementwise warps
+    uint64_t* pds_full = sdp_empty + 1;           // P^T (TMEM) and dS^T (shared) written
+    uint64_t* pds_empty = pds_full + 1;           // ... and read by the dV, dK, dQ products
+    uint64_t* dq_full = pds_empty + 1;
+    uint64_t* dq_empty = dq_full + 1;
+    uint64_t* acc_done = dq_empty + 1;            // every product finished: dK, dV final
+    uint64_t* drain = acc_done + 1;
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
+
+    const int warp = threadIdx.x >> 5;
+    const int lane = threadIdx.x & 31;
+    // Longest first over the whole grid: key tile 0 of every matrix is seen by the most query tiles.
+    const int32_t key_tile = static_cast<int32_t>(blockIdx.x / p.count);
+    const int32_t matrix = static_cast<int32_t>(blockIdx.x % p.count);
+    const int32_t key0 = key_tile * FB_BK;
+    // Query tiles with a query q >= key0 - offset (a query that sees some key of this tile), if any query does.
+    const int64_t q_lo = static_cast<int64_t>(key0) - p.offset;
+    const int32_t i_first = q_lo <= 0 ? 0 : static_cast<int32_t>(q_lo / FB_BQ);
+    const int32_t n_iter = q_lo > static_cast<int64_t>(p.sq) - 1 ? 0 : p.q_tiles - i_first;
+
+    if (threadIdx.x == 0) {
+        mbar_init(smem_addr(kv_full), 1);
+        for (int s = 0; s < FB_STAGES; ++s) {
+            mbar_init(smem_addr(&qdo_full[s]), 1);
+            mbar_init(smem_addr(&qdo_empty[s]), 1);
+        }
+        mbar_init(smem_addr(sdp_full), 1);
+        mbar_init(smem_addr(sdp_empty), FB_ELEM_WARPS);
+        mbar_init(smem_addr(pds_full), FB_ELEM_WARPS);
+        mbar_init(smem_addr(pds_empty), 1);
+        mbar_init(smem_addr(dq_full), 1);
+        mbar_init(smem_addr(dq_empty), 4);
+        mbar_init(smem_addr(acc_done), 1);
+        mbar_init(smem_addr(drain), 1);
+        fence_mbarrier_init();
+        fence_proxy_async_shared();
+    }
+    if (warp == FB_MMA_WARP) {
+        tmem_alloc(smem_addr(tmem_slot), FB_TMEM_COLS);
+        tmem_relinquish_alloc_permit();
+    }
+    tcgen05_fence_before_sync();
+    __syncthreads();
+    tcgen05_fence_after_sync();
+    const uint32_t tmem_base = *tmem_slot;
+
+    if (warp == FB_PRODUCER_WARP) {
+        // ------------------------------------------------------------------ TMA producer
+        if (elect_one() && n_iter > 0) {
+            const uint32_t kb = smem_addr(kv_full);
+            mbar_arrive_expect_tx(kb, 2 * FbSmem::KV);
+            tma_load_3d(smem_addr(k_s), &tm_k, kb, 0, key0, matrix);
+            tma_load_3d(smem_addr(v_s), &tm_v, kb, 0, key0, matrix);
+            int stage = 0;
+            uint32_t phase = 0;
+            for (int32_t n = 0; n < n_iter; ++n) {
+                const int32_t q0 = (i_first + n) * FB_BQ;
+                if (!mbar_wait(smem_addr(&qdo_empty[stage]), phase ^ 1u)) break;
+                const uint32_t fb = smem_addr(&qdo_full[stage]);
+                uint8_t* st = stage_s + stage * FbSmem::STAGE;
+                mbar_arrive_expect_tx(fb, FbSmem::STAGE);
+                tma_load_3d(smem_addr(st), &tm_q, fb, 0, q0, matrix);
+                tma_load_3d(smem_addr(st + FbSmem::QT), &tm_do, fb, 0, q0, matrix);
+                tma_load_3d(smem_addr(st + 2 * FbSmem::QT), &tm_stats, fb, 2 * q0, matrix, 0);
+                if (++stage == FB_STAGES) { stage = 0; phase ^= 1u; }
+            }
+        }
+        __syncwarp();
+    } else if (warp == FB_MMA_WARP) {
+        // ------------------------------------------------------------------ MMA issuer
+        if (elect_one()) {
+            constexpr uint32_t idesc_s = make_instr_desc(1u, 0u, 0u, FB_BK, FB_BQ);   // K-major x K-major
+            constexpr uint32_t idesc_kv = make_instr_desc(1u, 0u, 1u, FB_BK, FB_D);   // K-major x N-major
+            constexpr uint32_t idesc_q = make_instr_desc(1u, 1u, 1u, FB_BQ, FB_D);    // M-major x N-major
+            const uint32_t ks = smem_addr(k_s), vs = smem_addr(v_s), dss = smem_addr(ds_s);
+            bool ok = n_iter == 0 || mbar_wait(smem_addr(kv_full), 0);
+            bool issued = false;
+            int stage = 0;
+            uint32_t phase = 0;
+            for (int32_t n = 0; n < n_iter && ok; ++n) {
+                const uint32_t qs = smem_addr(stage_s + stage * FbSmem::STAGE);
+                const uint32_t dos = qs + FbSmem::QT;
+                if (!mbar_wait(smem_addr(&qdo_full[stage]), phase) ||
+                    !mbar_wait(smem_addr(sdp_empty), (n & 1) ^ 1u)) { ok = false; break; }
+                tcgen05_fence_after_sync();
+#pragma unroll
+                for (int k = 0; k < FB_D / 16; ++k) {
+                    umma_bf16(tmem_base + FB_S_COL, make_smem_desc(ks + 32 * k, 16, 1024, SNB_LAYOUT_SWIZZLE_128B),
+                              make_smem_desc(qs + 32 * k, 16, 1024, SNB_LAYOUT_SWIZZLE_128B), idesc_s, k > 0 ? 1u : 0u);
+                    umma_bf16(tmem_base + FB_DP_COL, make_smem_desc(vs + 32 * k, 16, 1024, SNB_LAYOUT_SWIZZLE_128B),
+                              make_smem_desc(dos + 32 * k, 16, 1024, SNB_LAYOUT_SWIZZLE_128B), idesc_s, k > 0 ? 1u : 0u);
+                }
+                issued = true;
+                umma_commit(smem_addr(sdp_full));
+                if (!mbar_wait(smem_addr(pds_full), n & 1)) { ok = false; break; }
+                tcgen05_fence_after_sync();
+#pragma unroll
+                for (int kk = 0; kk < FB_BQ / 16; ++kk) {
+                    // dV += P^T dO_i: queries 16kk..16kk+15 of P^T are TMEM columns 8kk..8kk+7.
+                    umma_bf16_tmem_a(tmem_base + FB_DV_COL, tmem_base + FB_P_COL + 8 * kk,
+                                     make_smem_desc(dos + kk * 2048, FbSmem::QT, 1024, SNB_LAYOUT_SWIZZLE_128B), idesc_kv,
+                                     (n > 0 || kk > 0) ? 1u : 0u);
+                    // dK += dS^T Q_i: dS^T K-major (queries contiguous, 64-query slices 16 KB apart).
+                    umma_bf16(tmem_base + FB_DK_COL,
+                              make_smem_desc(dss + (kk / 4) * (FbSmem::DS / 2) + (kk % 4) * 32, 16, 1024,
+                                             SNB_LAYOUT_SWIZZLE_128B),
+                              make_smem_desc(qs + kk * 2048, FbSmem::QT, 1024, SNB_LAYOUT_SWIZZLE_128B), idesc_kv,
+                              (n > 0 || kk > 0) ? 1u : 0u);
+                }
+                if (!mbar_wait(smem_addr(dq_empty), (n & 1) ^ 1u)) { ok = false; break; }
+                tcgen05_fence_after_sync();
+#pragma unroll
+                for (int kk = 0; kk < FB_BK / 16; ++kk) {
+                    // dQ_i = dS K_j: dS M-major from the dS^T tile (keys 16kk.. are rows, the two 64-query slices are
+                    // the M atoms 16 KB apart); K_j N-major (keys are rows).
+                    umma_bf16(tmem_base + FB_DQ_COL,
+                              make_smem_desc(dss + kk * 2048, FbSmem::DS / 2, 1024, SNB_LAYOUT_SWIZZLE_128B),
+                              make_smem_desc(ks + kk * 2048, FbSmem::KV, 1024, SNB_LAYOUT_SWIZZLE_128B), idesc_q,
+                              kk > 0 ? 1u : 0u);
+                }
+                umma_commit(smem_addr(dq_full));
+                umma_commit(smem_addr(pds_empty));
+                umma_commit(smem_addr(&qdo_empty[stage]));
+                if (++stage == FB_STAGES) { stage = 0; phase ^= 1u; }
+            }
+            if (ok) {
+                if (issued) umma_commit(smem_addr(acc_done));   // after every product above
+                else mbar_arrive(smem_addr(acc_done));          // no query tile sees these keys
+            } else if (issued) {
+                // Let every product already issued finish before TMEM is released.
+                umma_commit(smem_addr(drain));
+                mbar_wait(smem_addr(drain), 0);
+            }
+        }
+        __syncwarp();
+    } else if (warp < FB_ELEM_WARPS) {
+        // ------------------------------------------------------------------ P and dS (one key row per thread)
+        const int quad = warp & 3;          // TMEM lane quadrant
+        const int h = warp >> 2;            // query half of every tile: queries [64h, 64h + 64)
+        const int r = quad * 32 + lane;     // key row within the tile
+        const int64_t key = static_cast<int64_t>(key0) + r;
+        const uint32_t lane_base = static_cast<uint32_t>(quad * 32) << 16;
+        const uint32_t ds_row = smem_addr(ds_s + h * (FbSmem::DS / 2) + r * 128);
+        const float c = p.scale_log2;
+        bool ok = true;
+        int stage = 0;
+        uint32_t phase = 0;
+        for (int32_t n = 0; n < n_iter; ++n) {
+            const int64_t qh = static_cast<int64_t>(i_first + n) * FB_BQ + 64 * h;   // first query of this half
+            // Visible columns j of this half: qh + j >= key - offset, qh + j < sq, and key < sk.
+            const int64_t lo64 = key < p.sk ? key - p.offset - qh : 64;
+            const int64_t hi64 = static_cast<int64_t>(p.sq) - qh;
+            const int32_t lo = static_cast<int32_t>(lo64 < 0 ? 0 : (lo64 > 64 ? 64 : lo64));
+            const int32_t hi = static_cast<int32_t>(hi64 < 0 ? 0 : (hi64 > 64 ? 64 : hi64));
+            if (!warp_wait(smem_addr(sdp_full), n & 1) || !warp_wait(smem_addr(&qdo_full[stage]), phase) ||
+                (n > 0 && !warp_wait(smem_addr(pds_empty), (n - 1) & 1))) {
+                ok = false;
+                break;
+            }
+            tcgen05_fence_after_sync();
+            const float* stats = reinterpret_cast<const float*>(stage_s + stage * FbSmem::STAGE + 2 * FbSmem::QT) + 2 * 64 * h;
+#pragma unroll 1
+            for (int cc = 0; cc < 4; ++cc) {
+                uint32_t s[16], dp[16];
+                tmem_load_32x32b_x16(tmem_base + lane_base + FB_S_COL + 64 * h + 16 * cc, s);
+                tmem_load_32x32b_x16(tmem_base + lane_base + FB_DP_COL + 64 * h + 16 * cc, dp);
+                tmem_load_wait();
+                if (cc == 3) {
+                    // S^T and dP^T are in registers: the next tile's products may overwrite them.
+                    tcgen05_fence_before_sync();
+                    __syncwarp();
+                    if (lane == 0) mbar_arrive(smem_addr(sdp_empty));
+                }
+                const float4* st4 = reinterpret_cast<const float4*>(stats + 32 * cc);
+                uint32_t pw[8], dw[8];
+#pragma unroll
+                for (int j = 0; j < 16; j += 2) {
+                    const float4 nd = st4[j / 2];   // (nl, D) of columns 16cc + j and 16cc + j + 1
+                    const int col = 16 * cc + j;
+                    const float p0 = (col >= lo && col < hi) ? exp2_ftz(fmaf(__uint_as_float(s[j]), c, nd.x)) : 0.0f;
+                    const float p1 =
+                        (col + 1 >= lo && col + 1 < hi) ? exp2_ftz(fmaf(__uint_as_float(s[j + 1]), c, nd.z)) : 0.0f;
+                    pw[j / 2] = pack_bf16x2(p0, p1);
+                    dw[j / 2] = pack_bf16x2(p0 * (__uint_as_float(dp[j]) - nd.y), p1 * (__uint_as_float(dp[j + 1]) - nd.w));
+                }
+                tmem_store_32x32b_x8(tmem_base + lane_base + FB_P_COL + 32 * h + 8 * cc, pw);
+                // dS^T row r, queries 64h + 16cc ..: 16-byte chunks 2cc, 2cc + 1 of the 128-byte row, swizzled.
+                st_shared_v4(ds_row + (((2 * cc) ^ (r & 7)) << 4), dw[0], dw[1], dw[2], dw[3]);
+                st_shared_v4(ds_row + (((2 * cc + 1) ^ (r & 7)) << 4), dw[4], dw[5], dw[6], dw[7]);
+            }
+            tmem_store_wait();
+            fence_proxy_async_shared();   // dS^T writes -> the tensor core's reads
+            tcgen05_fence_before_sync();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(smem_addr(pds_full));
+            if (++stage == FB_STAGES) { stage = 0; phase ^= 1u; }
+        }
+        // dV (h = 0) or scale * dK (h = 1) of this warp's 32 key rows (zero when no query sees them). The TMEM loads
+        // are warp-collective; only the stores depend on the row.
+        if (ok && warp_wait(smem_addr(acc_done), 0)) {
+            tcgen05_fence_after_sync();
+            float* dst = (h == 0 ? p.dv : p.dk) + (static_cast<int64_t>(matrix) * p.sk + key) * FB_D;
+            const float mul = n_iter == 0 ? 0.0f : (h == 0 ? 1.0f : p.scale);
+            for (int c0 = 0; c0 < FB_D; c0 += 32) {
+                uint32_t o[32];
+                tmem_load_32x32b_x32(tmem_base + lane_base + (h == 0 ? FB_DV_COL : FB_DK_COL) + c0, o);
+                tmem_load_wait();
+                if (key < p.sk) {
+                    float4* d4 = reinterpret_cast<float4*>(dst + c0);
+#pragma unroll
+                    for (int g = 0; g < 8; ++g) {
+                        // (n_iter == 0: TMEM holds no product; multiply-by-zero of whatever it holds is replaced by
+                        // an explicit zero so that stale NaN bits cannot leak.)
+                        d4[g] = n_iter == 0 ? make_float4(0.0f, 0.0f, 0.0f, 0.0f)
+                                            : make_float4(__uint_as_float(o[4 * g]) * mul,
+                                                          __uint_as_float(o[4 * g + 1]) * mul,
+                                                          __uint_as_float(o[4 * g + 2]) * mul,
+                                                          __uint_as_float(o[4 * g + 3]) * mul);
+                    }
+                }
+            }
+        }
+    } else if (warp < FB_DQ_WARP0 + 4) {
+        // ------------------------------------------------------------------ dQ drain (one query row per thread)
+        // Each warp stages and reduces its own 32 query rows (two 32x32 f32 boxes), so the four warps never wait for
+        // one another.
+        const int quad = warp & 3;
+        const uint32_t lane_base = static_cast<uint32_t>(quad * 32) << 16;
+        uint8_t* box0 = dq_s + quad * (FbSmem::DQ / 4);   // columns 0-31 of rows 32 quad ..
+        uint8_t* box1 = box0 + FbSmem::DQ / 8;             // columns 32-63
+        for (int32_t n = 0; n < n_iter; ++n) {
+            if (!warp_wait(smem_addr(dq_full), n & 1)) break;
+            tcgen05_fence_after_sync();
+            uint32_t a[32], b[32];
+            tmem_load_32x32b_x32(tmem_base + lane_base + FB_DQ_COL, a);
+            tmem_load_32x32b_x32(tmem_base + lane_base + FB_DQ_COL + 32, b);
+            tmem_load_wait();
+            tcgen05_fence_before_sync();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(smem_addr(dq_empty));
+            // The staging boxes are free once this warp's previous reductions have read them.
+            if (lane == 0) bulk_wait_group_read<0>();
+            __syncwarp();
+            const uint32_t row0 = smem_addr(box0 + lane * 128), row1 = smem_addr(box1 + lane * 128);
+#pragma unroll
+            for (int g = 0; g < 8; ++g) {
+                const uint32_t off = (g ^ (lane & 7)) << 4;
+                st_shared_v4(row0 + off, __float_as_uint(__uint_as_float(a[4 * g]) * p.scale),
+                             __float_as_uint(__uint_as_float(a[4 * g + 1]) * p.scale),
+                             __float_as_uint(__uint_as_float(a[4 * g + 2]) * p.scale),
+                             __float_as_uint(__uint_as_float(a[4 * g + 3]) * p.scale));
+                st_shared_v4(row1 + off, __float_as_uint(__uint_as_float(b[4 * g]) * p.scale),
+                             __float_as_uint(__uint_as_float(b[4 * g + 1]) * p.scale),
+                             __float_as_uint(__uint_as_float(b[4 * g + 2]) * p.scale),
+                             __float_as_uint(__uint_as_float(b[4 * g + 3]) * p.scale));
+            }
+            fence_proxy_async_shared();
+            __syncwarp();
+            if (lane == 0) {
+                const int32_t q0 = (i_first + n) * FB_BQ + 32 * quad;
+                tma_reduce_add_3d(&tm_dq, smem_addr(box0), 0, q0, matrix);
+                tma_reduce_add_3d(&tm_dq, smem_addr(box1), 32, q0, matrix);
+                bulk_commit_group();
+            }
+        }
+        if (lane == 0) bulk_wait_group<0>();
+    }
+
+    tcgen05_fence_before_sync();
+    __syncthreads();
+    if (warp == FB_MMA_WARP) {
+        tcgen05_fence_after_sync();
+        tmem_dealloc(tmem_base, FB_TMEM_COLS);
+    }
+}
+
+}  // namespace snb

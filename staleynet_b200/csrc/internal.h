@@ -57,6 +57,12 @@ int causal_softmax_backward(cudaStream_t stream, const float* probabilities, flo
 int fused_attention_forward(cudaStream_t stream, const void* q, const void* k, const void* v, uint64_t count,
                             uint64_t queries, uint64_t keys, float scale, uint64_t query_offset, void* out,
                             int out_type, float* lse, std::string* err);
+// Fused causal attention backward (attention_fused_bwd.cuh): dq [count, queries, 64], dk and dv [count, keys, 64],
+// all f32 and overwritten, from bf16 q, k, v, d_out, the forward's output (f32 or bf16) and its log-sum-exp.
+int fused_attention_backward(cudaStream_t stream, const void* q, const void* k, const void* v, const void* out,
+                             int out_type, const void* d_out, const float* lse, uint64_t count, uint64_t queries,
+                             uint64_t keys, float scale, uint64_t query_offset, float* dq, float* dk, float* dv,
+                             std::string* err);
 
 // Launches a one-thread kernel whose mbarrier wait nothing completes; it gives up after limit_ns.
 int bounded_wait_probe(cudaStream_t stream, uint64_t limit_ns, std::string* err);

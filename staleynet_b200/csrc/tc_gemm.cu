@@ -7,6 +7,7 @@
 #include <mutex>
 
 #include "attention_fused.cuh"
+#include "attention_fused_bwd.cuh"
 #include "gemm_tc.cuh"
 #include "gemm_tc_pair.cuh"
 #include "internal.h"
@@ -450,6 +451,125 @@ int fused_attention_forward(cudaStream_t stream, const void* q, const void* k, c
     cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess) {
         *err = cuda_message("fa_forward_kernel launch", e);
+        return SNB_ERR_CUDA;
+    }
+    return SNB_OK;
+}
+
+int fused_attention_backward(cudaStream_t stream, const void* q, const void* k, const void* v, const void* out,
+                             int out_type, const void* d_out, const float* lse, uint64_t count, uint64_t queries,
+                             uint64_t keys, float scale, uint64_t query_offset, float* dq, float* dk, float* dv,
+                             std::string* err) {
+    if (count == 0) return SNB_OK;
+    DeviceInfo dev;
+    int rc = current_device_info(&dev, err);
+    if (rc != SNB_OK) return rc;
+    if (dev.major != 10) {
+        *err = "fused attention needs an sm_100 device";
+        return SNB_ERR_UNSUPPORTED;
+    }
+    const uint64_t lim = (1ull << 31) - 256;
+    if (count > lim || queries > lim || keys > lim) {
+        *err = "fused attention backward: sizes out of range";
+        return SNB_ERR_INVALID_ARGUMENT;
+    }
+    for (const void* ptr : {q, k, v, out, d_out, static_cast<const void*>(dq), static_cast<const void*>(dk),
+                            static_cast<const void*>(dv)}) {
+        if (reinterpret_cast<uintptr_t>(ptr) % 16 != 0) {
+            *err = "fused attention backward: q, k, v, out, d_out, dq, dk and dv must be 16-byte aligned";
+            return SNB_ERR_INVALID_ARGUMENT;
+        }
+    }
+    auto memset_or_fail = [&](void* ptr, uint64_t bytes, const char* what) -> int {
+        if (bytes == 0) return SNB_OK;
+        cudaError_t e = cudaMemsetAsync(ptr, 0, bytes, stream);
+        if (e != cudaSuccess) {
+            *err = cuda_message(what, e);
+            return SNB_ERR_CUDA;
+        }
+        return SNB_OK;
+    };
+    // dQ is accumulated into by TMA reductions; with no queries or no keys every gradient is zero.
+    rc = memset_or_fail(dq, count * queries * FB_D * sizeof(float), "cudaMemsetAsync(dq)");
+    if (rc != SNB_OK) return rc;
+    if (queries == 0 || keys == 0) {
+        rc = memset_or_fail(dk, count * keys * FB_D * sizeof(float), "cudaMemsetAsync(dk)");
+        if (rc == SNB_OK) rc = memset_or_fail(dv, count * keys * FB_D * sizeof(float), "cudaMemsetAsync(dv)");
+        return rc;
+    }
+    // Scratch: per query (-lse * log2(e), D), matrices `stride` floats apart (16-byte multiple for the tensor map).
+    const uint64_t stride = (2 * queries + 3) / 4 * 4;
+    float* stats = nullptr;
+    cudaError_t e = cudaMallocAsync(reinterpret_cast<void**>(&stats), count * stride * sizeof(float), stream);
+    if (e != cudaSuccess) {
+        *err = cuda_message("cudaMallocAsync(row statistics)", e);
+        return SNB_ERR_CUDA;
+    }
+    auto release = [&]() { cudaFreeAsync(stats, stream); };
+    const uint64_t rows = count * queries;
+    fb_rowstats_kernel<<<static_cast<unsigned>((rows + 7) / 8), 256, 0, stream>>>(
+        out, out_type == SNB_TYPE_BF16 ? 1 : 0, static_cast<const uint16_t*>(d_out), lse, stats,
+        static_cast<int64_t>(rows), static_cast<int32_t>(queries), static_cast<int64_t>(stride));
+    e = cudaGetLastError();
+    if (e != cudaSuccess) {
+        release();
+        *err = cuda_message("fb_rowstats_kernel launch", e);
+        return SNB_ERR_CUDA;
+    }
+    CUtensorMap tq, tk, tv, tdo, tst, tdq;
+    // [count, rows, 64] bf16 tiles of 128 rows (one 128-byte swizzle row each); the statistics as 256-float rows
+    // (128 queries); dQ as f32 boxes of 32 columns x 32 rows (128-byte swizzle rows).
+    if (!encode_3d(&tq, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, q, FB_D, queries, count, FB_D, queries * FB_D, FB_D,
+                   FB_BQ, err) ||
+        !encode_3d(&tdo, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, d_out, FB_D, queries, count, FB_D, queries * FB_D, FB_D,
+                   FB_BQ, err) ||
+        !encode_3d(&tk, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, k, FB_D, keys, count, FB_D, keys * FB_D, FB_D, FB_BK,
+                   err) ||
+        !encode_3d(&tv, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, v, FB_D, keys, count, FB_D, keys * FB_D, FB_D, FB_BK,
+                   err) ||
+        !encode_3d(&tst, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, stats, 2 * queries, count, 1, stride, stride * count,
+                   2 * FB_BQ, 1, err, CU_TENSOR_MAP_SWIZZLE_NONE) ||
+        !encode_3d(&tdq, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, dq, FB_D, queries, count, FB_D, queries * FB_D, 32, 32,
+                   err)) {
+        release();
+        return SNB_ERR_INVALID_ARGUMENT;
+    }
+    FbParams fp{};
+    fp.count = static_cast<int32_t>(count);
+    fp.sq = static_cast<int32_t>(queries);
+    fp.sk = static_cast<int32_t>(keys);
+    fp.q_tiles = static_cast<int32_t>((queries + FB_BQ - 1) / FB_BQ);
+    fp.offset = static_cast<int64_t>(query_offset);
+    fp.scale = scale;
+    fp.scale_log2 = scale * 1.4426950408889634f;
+    fp.dk = dk;
+    fp.dv = dv;
+    const int64_t grid = static_cast<int64_t>((keys + FB_BK - 1) / FB_BK) * static_cast<int64_t>(count);
+    if (grid > 0x7fffffff) {
+        release();
+        *err = "fused attention backward: grid too large";
+        return SNB_ERR_UNSUPPORTED;
+    }
+    static int configured_device = -1;
+    static std::mutex mu;
+    {
+        std::lock_guard<std::mutex> lock(mu);
+        if (configured_device != dev.device) {
+            e = cudaFuncSetAttribute(fb_backward_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, FbSmem::BYTES);
+            if (e != cudaSuccess) {
+                release();
+                *err = cuda_message("cudaFuncSetAttribute(fb_backward_kernel)", e);
+                return SNB_ERR_CUDA;
+            }
+            configured_device = dev.device;
+        }
+    }
+    fb_backward_kernel<<<static_cast<unsigned>(grid), FB_THREADS, FbSmem::BYTES, stream>>>(tq, tk, tv, tdo, tst, tdq,
+                                                                                           fp);
+    e = cudaGetLastError();
+    release();
+    if (e != cudaSuccess) {
+        *err = cuda_message("fb_backward_kernel launch", e);
         return SNB_ERR_CUDA;
     }
     return SNB_OK;
