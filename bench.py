@@ -55,6 +55,16 @@ def load_traffic(shape) -> dict:
     return json.loads(path.read_text())
 
 
+def load_kernel_traffic(kernel: str):
+    """Per-launch DRAM bytes (read + write) of one fused-attention kernel at BASELINE config 4, from the ncu capture
+    summarised in profiles/fused_attention_cfg4_kernels.json; None when no capture is committed."""
+    path = ROOT / "profiles" / "fused_attention_cfg4_kernels.json"
+    if not path.exists():
+        return None
+    entry = json.loads(path.read_text()).get(kernel)
+    return None if entry is None else entry.get("dram_bytes")
+
+
 def workload_config(shape, n_gpus: int) -> dict:
     return {
         "workload": "cfg3 12-block width-768 decoder: linear + 16x1024 codebook-head GEMMs, fwd+dX+dW, "
@@ -88,13 +98,25 @@ class ClockSampler:
         self.file = None
 
     def start(self):
+        """Starts sampling and returns once the first sample is written, so that the samples counted by stop() are
+        the ones taken after this call (inside the timed region)."""
+        self.skip = 0
         try:
             self.file = tempfile.NamedTemporaryFile("w+", suffix=".csv", delete=False)
             self.proc = subprocess.Popen(
                 ["nvidia-smi", f"--id={self.device_index}", f"--query-gpu={self.QUERY}", "--format=csv,noheader",
-                 "-lms", "200"], stdout=self.file, stderr=subprocess.DEVNULL)
+                 "-lms", "100"], stdout=self.file, stderr=subprocess.DEVNULL)
         except (OSError, FileNotFoundError):
             self.proc = None
+            return
+        deadline = time.time() + 5.0
+        while time.time() < deadline and self.proc.poll() is None:
+            self.file.flush()
+            lines = [x for x in Path(self.file.name).read_text().splitlines() if x.strip()]
+            if lines:
+                self.skip = len(lines)
+                break
+            time.sleep(0.01)
 
     def stop(self) -> dict:
         if self.proc is None:
@@ -107,6 +129,7 @@ class ClockSampler:
         self.file.flush()
         rows = [line.split(",") for line in Path(self.file.name).read_text().splitlines() if line.strip()]
         os.unlink(self.file.name)
+        rows = rows[self.skip:]   # samples taken while the timed region ran
         sm, smax, power, reasons = [], None, [], set()
         names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
         for r in rows:
@@ -376,17 +399,21 @@ def attention_cpu_baseline(s, budget_flops: float = 10e9, threads: int = 0) -> d
 
 
 def run_attention(args, rank: int, world: int, local_rank: int) -> int:
-    """the six batched causal attention products with the fp32 causal softmax (and its
-    backward) between them; one forward + backward per step."""
+    """one causal attention forward + backward per step (batch 8, 12 heads of 64, sequence 3072).
+
+    --attention-path fused (default): snb_causal_attention_forward + snb_causal_attention_backward, no [S, S] tensor.
+    --attention-path materialised: the six batched products with the fp32 causal softmax and its backward between
+    them, as the reference computes them. `value` counts the six products' causal FLOPs either way."""
     import torch
 
-    from staleynet_b200.attention import AttentionProducts, AttentionShape
+    from staleynet_b200.attention import AttentionProducts, AttentionShape, FusedAttention
 
     torch.cuda.set_device(local_rank)
     device = torch.device("cuda", local_rank)
     stream = torch.cuda.current_stream(device)
     shape = AttentionShape()
-    att = AttentionProducts(shape, device, seed=rank)
+    fused = args.attention_path == "fused"
+    att = FusedAttention(shape, device, seed=rank) if fused else AttentionProducts(shape, device, seed=rank)
     h = stream.cuda_stream
     for _ in range(args.warmup):
         att.forward(h)
@@ -395,46 +422,73 @@ def run_attention(args, rank: int, world: int, local_rank: int) -> int:
     clocks = ClockSampler(local_rank)
     clocks.start()
     start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    # The dominant kernel's launches are bracketed by their own events on the same stream.
+    marks = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(args.steps)]
     start.record(stream)
-    for _ in range(args.steps):
-        att.forward(h)
-        att.backward(h)
+    for i in range(args.steps):
+        if fused:
+            att.forward(h)
+            marks[i][0].record(stream)
+            att.backward(h)
+            marks[i][1].record(stream)
+        else:
+            att.forward(h)
+            att.backward(h)
     end.record(stream)
     torch.cuda.synchronize()
     clock_info = clocks.stop()
     ms = start.elapsed_time(end)
-    host = [torch.empty(t.numel(), dtype=t.dtype, pin_memory=True) for t in (att.q, att.k, att.v, att.d_out)]
-    for hb, t in zip(host, (att.q, att.k, att.v, att.d_out)):
+    inputs = (att.q, att.k, att.v, att.d_out)
+    host = [torch.empty(t.shape, dtype=t.dtype, pin_memory=True) for t in inputs]
+    for hb, t in zip(host, inputs):
         hb.copy_(t.cpu())
     host_out = torch.empty(1, dtype=torch.float32, pin_memory=True)
     torch.cuda.synchronize()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     e0.record(stream)
     for _ in range(args.steps):
-        for hb, t in zip(host, (att.q, att.k, att.v, att.d_out)):
+        for hb, t in zip(host, inputs):
             t.copy_(hb, non_blocking=True)
         att.forward(h)
         att.backward(h)
-        host_out.copy_(att.dq[:1], non_blocking=True)
+        host_out.copy_(att.dq.view(-1)[:1], non_blocking=True)
     e1.record(stream)
     torch.cuda.synchronize()
     e2e_ms = e0.elapsed_time(e1)
     if rank != 0:
         return 0
     peaks, source = load_peaks()
-    hbm = float(peaks.get("hbm_gbs", FALLBACK_PEAKS["hbm_gbs"]))
     sec = ms / 1e3 / args.steps
-    achieved_gbs = att.bytes / sec / 1e9
+    if fused:
+        bwd_sec = sum(a.elapsed_time(b) for a, b in marks) / 1e3 / args.steps
+        peak = float(peaks.get("bf16_tflops_sustained", FALLBACK_PEAKS["bf16_tflops"]))
+        achieved = att.backward_flops / bwd_sec / 1e12
+        traffic = load_kernel_traffic("fb_backward_kernel")
+        roofline = {"bound": "tensor", "kernel": "fb_backward_kernel (+ its row-statistics kernel and dQ memset)",
+                    "achieved": achieved, "peak": peak, "unit": "TFLOP/s", "frac": achieved / peak,
+                    "traffic": traffic, "algorithmic_flops_per_launch": att.backward_flops,
+                    "peak_source": f"{source} bf16_tflops_sustained", "ms_per_launch": bwd_sec * 1e3,
+                    "forward_ms_per_launch": (ms / args.steps) - bwd_sec * 1e3}
+        workload = ("cfg4 causal attention fwd+bwd through the fused entry points snb_causal_attention_forward/"
+                    "backward (QK^T, online softmax, P.V; then P rebuilt from the log-sum-exp, dP, dV, dS, dQ, dK), "
+                    "no [S, S] tensor")
+        l2 = "inputs 96 x 3072 x 64 bf16 per tensor (38 MB each); every K/V tile is re-read from L2 by the query tiles"
+    else:
+        hbm = float(peaks.get("hbm_gbs", FALLBACK_PEAKS["hbm_gbs"]))
+        achieved = att.bytes / sec / 1e9
+        roofline = {"bound": "hbm", "achieved": achieved, "peak": hbm, "unit": "GB/s", "frac": achieved / hbm,
+                    "traffic": None, "algorithmic_bytes_per_step": att.bytes, "peak_source": f"{source} hbm_gbs"}
+        workload = ("cfg4 batched causal attention products fwd+bwd (QK^T, P.V, dO.V^T, P^T.dO, dS.K, dS^T.Q) with "
+                    "fp32 causal softmax and its backward between them")
+        l2 = "inputs larger than L2 (scores 3.6 GB)"
     line = {
         "metric": METRIC, "value": att.flops / sec / 1e12, "unit": UNIT, "n_gpus": 1, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": ms / args.steps, "higher_is_better": True, "scaling": "weak",
         "vs_baseline": None, "dtype": "bf16", "data": "synthetic (seeded N(0,1) bf16 Q/K/V/dO)",
-        "config": {"workload": "cfg4 batched causal attention products fwd+bwd (QK^T, P.V, dO.V^T, P^T.dO, dS.K, "
-                               "dS^T.Q) with fp32 causal softmax and its backward between them",
+        "config": {"workload": workload, "attention_path": args.attention_path,
                    "batch": shape.batch, "heads": shape.heads, "head_dim": shape.head_dim, "seq_len": shape.time,
-                   "flops": "causal (visible query-key pairs) count", "l2": "inputs larger than L2 (scores 3.6 GB)"},
-        "roofline": {"bound": "hbm", "achieved": achieved_gbs, "peak": hbm, "unit": "GB/s", "frac": achieved_gbs / hbm,
-                     "traffic": None, "algorithmic_bytes_per_step": att.bytes, "peak_source": f"{source} hbm_gbs"},
+                   "flops": "causal (visible query-key pairs) count of the six products", "l2": l2},
+        "roofline": roofline,
         "e2e": {"value": att.flops / (e2e_ms / 1e3 / args.steps) / 1e12, "unit": UNIT,
                 "h2d_bytes_per_step": sum(x.numel() * x.element_size() for x in host), "d2h_bytes_per_step": 4},
         "gpu_launches": att.launches() * args.steps, "clocks": clock_info,
@@ -456,7 +510,9 @@ def main(argv=None) -> int:
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--breakdown", default=None, help="write per-GEMM kernel times of the timed region here (JSON)")
     ap.add_argument("--workload", choices=["step", "attention"], default="step",
-                    help="step: the cfg3 training-step GEMMs (default); attention: the cfg4 attention products")
+                    help="step: the cfg3 training-step GEMMs (default); attention: the cfg4 attention layer")
+    ap.add_argument("--attention-path", choices=["fused", "materialised"], default="fused",
+                    help="attention workload: fused entry points (default) or the six materialised products")
     args = ap.parse_args(argv)
     if args.warmup < 3:
         ap.error("--warmup must be at least 3")

@@ -155,3 +155,56 @@ class AttentionProducts:
 
     def launches(self) -> int:
         return 8
+
+
+def fused_algorithmic_bytes(s: AttentionShape) -> float:
+    """Bytes the fused forward + backward must move: Q, K, V, dO read (bf16), the f32 output and log-sum-exp written
+    by the forward and read back by the backward, dQ, dK, dV written (f32)."""
+    n, S, d = s.count, s.time, s.head_dim
+    head = S * d
+    fwd = 3 * head * 2 + head * 4 + S * 4
+    bwd = 4 * head * 2 + head * 4 + S * 4 + 3 * head * 4
+    return float(n) * (fwd + bwd)
+
+
+class FusedAttention:
+    """The same attention layer call through the fused entry points: snb_causal_attention_forward (output f32 and
+    log-sum-exp) and snb_causal_attention_backward (dQ, dK, dV f32), on head-major tensors [batch*heads, time, 64].
+    No [time, time] tensor exists; the backward recomputes the scores (one product more than the materialised six,
+    not counted in `flops`)."""
+
+    def __init__(self, shape: AttentionShape, device, seed: int = 0):
+        import torch
+
+        from .matmul import Gpu
+
+        s = shape
+        self.shape = s
+        n, S, d = s.count, s.time, s.head_dim
+        gen = torch.Generator(device=device)
+        gen.manual_seed(seed)
+
+        def normal():
+            return torch.randn(n, S, d, generator=gen, device=device, dtype=torch.float32).to(torch.bfloat16)
+
+        self.q, self.k, self.v, self.d_out = (normal() for _ in range(4))
+        self.out = torch.empty(n, S, d, device=device, dtype=torch.float32)
+        self.lse = torch.empty(n, S, device=device, dtype=torch.float32)
+        self.dq, self.dk, self.dv = (torch.empty(n, S, d, device=device, dtype=torch.float32) for _ in range(3))
+        self.scale = 1.0 / (d ** 0.5)
+        self.gpu = Gpu(device.index if device.index is not None else 0)
+        self.flops = product_flops(s)
+        self.backward_flops = 5 * 2.0 * s.head_dim * causal_pairs(s) * s.count
+        self.bytes = fused_algorithmic_bytes(s)
+
+    def forward(self, stream_handle: int = 0) -> None:
+        self.gpu.causal_attention_forward(self.q, self.k, self.v, self.out, self.scale, self.shape.query_offset,
+                                          self.lse)
+
+    def backward(self, stream_handle: int = 0) -> None:
+        self.gpu.causal_attention_backward(self.q, self.k, self.v, self.out, self.d_out, self.lse, self.dq, self.dk,
+                                           self.dv, self.scale, self.shape.query_offset)
+
+    def launches(self) -> int:
+        """Kernels of one forward + backward: the forward kernel, the row-statistics and backward kernels."""
+        return 3
