@@ -230,6 +230,18 @@ SNB_API int snb_causal_attention_backward(void* stream, const uint16_t* q, const
                                           uint64_t count, uint64_t queries, uint64_t keys, uint64_t head_dim,
                                           float scale, uint64_t query_offset, float* dq, float* dk, float* dv);
 
+/* snb_causal_attention_backward without any allocation: the same arguments, kernels and results, but the
+ * row-statistics scratch is a fixed 8 MiB __device__ array of the library (its address looked up once per device)
+ * instead of a stream-ordered allocation, and nothing else is allocated. Returns SNB_ERR_INVALID_ARGUMENT, before
+ * touching any buffer, when count * queries * 8 bytes (rounded up per matrix) exceed that array. The array is shared
+ * by every call on a device: calls that overlap in time (on different streams or threads) race on it and must be
+ * serialised by the caller. No reference counterpart. */
+SNB_API int snb_causal_attention_backward_noalloc(void* stream, const uint16_t* q, const uint16_t* k,
+                                                  const uint16_t* v, const void* out, int32_t out_type,
+                                                  const uint16_t* d_out, const float* lse, uint64_t count,
+                                                  uint64_t queries, uint64_t keys, uint64_t head_dim, float scale,
+                                                  uint64_t query_offset, float* dq, float* dk, float* dv);
+
 /* Failure-detection self-test: launches a one-thread kernel that waits on an mbarrier nothing completes, through
  * the bounded wait every tensor-core pipeline wait uses. The wait gives up after limit_ns (at most 1 s), records a
  * timeout in the device status word and the kernel returns normally; a following snb_device_status() reports

@@ -58,6 +58,7 @@ EXPORTED_SYMBOLS = (
     "snb_device_status",
     "snb_causal_attention_forward",
     "snb_causal_attention_backward",
+    "snb_causal_attention_backward_noalloc",
     "snb_selftest_bounded_wait",
     "snb_abi_version",
 )
@@ -156,6 +157,8 @@ def load() -> ctypes.CDLL:
                                                       c_void_p, c_void_p, c_uint64, c_uint64, c_uint64, c_uint64,
                                                       c_float, c_uint64, c_void_p, c_void_p, c_void_p]
         lib.snb_causal_attention_backward.restype = c_int
+        lib.snb_causal_attention_backward_noalloc.argtypes = lib.snb_causal_attention_backward.argtypes
+        lib.snb_causal_attention_backward_noalloc.restype = c_int
         lib.snb_selftest_bounded_wait.argtypes = [c_void_p, c_uint64]
         lib.snb_selftest_bounded_wait.restype = c_int
         lib.snb_abi_version.argtypes = []

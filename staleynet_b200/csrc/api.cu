@@ -248,26 +248,47 @@ int snb_causal_attention_forward(void* stream, const uint16_t* q, const uint16_t
     return SNB_OK;
 }
 
+namespace {
+
+int attention_backward_entry(const char* name, bool static_scratch_only, void* stream, const uint16_t* q,
+                             const uint16_t* k, const uint16_t* v, const void* out, int32_t out_type,
+                             const uint16_t* d_out, const float* lse, uint64_t count, uint64_t queries, uint64_t keys,
+                             uint64_t head_dim, float scale, uint64_t query_offset, float* dq, float* dk, float* dv) {
+    t_last_path = SNB_PATH_NONE;
+    // (Messages are built on the error paths only: the no-alloc entry allocates nothing when it succeeds.)
+    if (head_dim != 64) return fail(SNB_ERR_UNSUPPORTED, std::string(name) + ": head_dim must be 64");
+    if (out_type != SNB_TYPE_F32 && out_type != SNB_TYPE_BF16)
+        return fail(SNB_ERR_INVALID_ARGUMENT, std::string(name) + ": unknown output type");
+    if (!(scale > 0.0f) || !std::isfinite(scale))
+        return fail(SNB_ERR_INVALID_ARGUMENT, std::string(name) + ": scale must be positive and finite");
+    if (count > 0 && ((queries > 0 && (q == nullptr || d_out == nullptr || out == nullptr || lse == nullptr ||
+                                       dq == nullptr)) ||
+                      (keys > 0 && (k == nullptr || v == nullptr || dk == nullptr || dv == nullptr))))
+        return fail(SNB_ERR_INVALID_ARGUMENT, std::string(name) + ": null pointer");
+    std::string err;
+    int rc = fused_attention_backward(static_cast<cudaStream_t>(stream), q, k, v, out, out_type, d_out, lse, count,
+                                      queries, keys, scale, query_offset, dq, dk, dv, static_scratch_only, &err);
+    if (rc != SNB_OK) return fail(rc, err);
+    t_last_path = SNB_PATH_TENSOR_CORE;
+    return SNB_OK;
+}
+
+}  // namespace
+
 int snb_causal_attention_backward(void* stream, const uint16_t* q, const uint16_t* k, const uint16_t* v,
                                   const void* out, int32_t out_type, const uint16_t* d_out, const float* lse,
                                   uint64_t count, uint64_t queries, uint64_t keys, uint64_t head_dim, float scale,
                                   uint64_t query_offset, float* dq, float* dk, float* dv) {
-    t_last_path = SNB_PATH_NONE;
-    if (head_dim != 64) return fail(SNB_ERR_UNSUPPORTED, "causal_attention_backward: head_dim must be 64");
-    if (out_type != SNB_TYPE_F32 && out_type != SNB_TYPE_BF16)
-        return fail(SNB_ERR_INVALID_ARGUMENT, "causal_attention_backward: unknown output type");
-    if (!(scale > 0.0f) || !std::isfinite(scale))
-        return fail(SNB_ERR_INVALID_ARGUMENT, "causal_attention_backward: scale must be positive and finite");
-    if (count > 0 && ((queries > 0 && (q == nullptr || d_out == nullptr || out == nullptr || lse == nullptr ||
-                                       dq == nullptr)) ||
-                      (keys > 0 && (k == nullptr || v == nullptr || dk == nullptr || dv == nullptr))))
-        return fail(SNB_ERR_INVALID_ARGUMENT, "causal_attention_backward: null pointer");
-    std::string err;
-    int rc = fused_attention_backward(static_cast<cudaStream_t>(stream), q, k, v, out, out_type, d_out, lse, count,
-                                      queries, keys, scale, query_offset, dq, dk, dv, &err);
-    if (rc != SNB_OK) return fail(rc, err);
-    t_last_path = SNB_PATH_TENSOR_CORE;
-    return SNB_OK;
+    return attention_backward_entry("causal_attention_backward", false, stream, q, k, v, out, out_type, d_out, lse,
+                                    count, queries, keys, head_dim, scale, query_offset, dq, dk, dv);
+}
+
+int snb_causal_attention_backward_noalloc(void* stream, const uint16_t* q, const uint16_t* k, const uint16_t* v,
+                                          const void* out, int32_t out_type, const uint16_t* d_out, const float* lse,
+                                          uint64_t count, uint64_t queries, uint64_t keys, uint64_t head_dim,
+                                          float scale, uint64_t query_offset, float* dq, float* dk, float* dv) {
+    return attention_backward_entry("causal_attention_backward_noalloc", true, stream, q, k, v, out, out_type, d_out,
+                                    lse, count, queries, keys, head_dim, scale, query_offset, dq, dk, dv);
 }
 
 int snb_selftest_bounded_wait(void* stream, uint64_t limit_ns) {

@@ -58,11 +58,13 @@ int fused_attention_forward(cudaStream_t stream, const void* q, const void* k, c
                             uint64_t queries, uint64_t keys, float scale, uint64_t query_offset, void* out,
                             int out_type, float* lse, std::string* err);
 // Fused causal attention backward (attention_fused_bwd.cuh): dq [count, queries, 64], dk and dv [count, keys, 64],
-// all f32 and overwritten, from bf16 q, k, v, d_out, the forward's output (f32 or bf16) and its log-sum-exp.
+// all f32 and overwritten, from bf16 q, k, v, d_out, the forward's output (f32 or bf16) and its log-sum-exp. The
+// row-statistics scratch comes from cudaMallocAsync on `stream`, or with static_scratch_only from a fixed
+// __device__ array (no allocation; SNB_ERR_INVALID_ARGUMENT when it is too small; concurrent calls share it).
 int fused_attention_backward(cudaStream_t stream, const void* q, const void* k, const void* v, const void* out,
                              int out_type, const void* d_out, const float* lse, uint64_t count, uint64_t queries,
                              uint64_t keys, float scale, uint64_t query_offset, float* dq, float* dk, float* dv,
-                             std::string* err);
+                             bool static_scratch_only, std::string* err);
 
 // Launches a one-thread kernel whose mbarrier wait nothing completes; it gives up after limit_ns.
 int bounded_wait_probe(cudaStream_t stream, uint64_t limit_ns, std::string* err);

@@ -456,10 +456,43 @@ int fused_attention_forward(cudaStream_t stream, const void* q, const void* k, c
     return SNB_OK;
 }
 
+namespace {
+
+// Scratch of the no-alloc backward entry point: the row statistics live here instead of in a stream-ordered
+// allocation. One array per device image of the library, shared by every call on that device.
+constexpr uint64_t kStaticScratchBytes = 8ull << 20;
+static __device__ __align__(256) float g_attention_scratch[kStaticScratchBytes / sizeof(float)];
+
+// The scratch array's device address on the current device, looked up once per device.
+int static_scratch(float** ptr, std::string* err) {
+    static std::mutex mu;
+    static float* cached[64] = {};
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess || dev < 0 || dev >= 64) {
+        *err = cuda_message("cudaGetDevice", e);
+        return SNB_ERR_CUDA;
+    }
+    std::lock_guard<std::mutex> lock(mu);
+    if (cached[dev] == nullptr) {
+        void* p = nullptr;
+        e = cudaGetSymbolAddress(&p, g_attention_scratch);
+        if (e != cudaSuccess) {
+            *err = cuda_message("cudaGetSymbolAddress(scratch)", e);
+            return SNB_ERR_CUDA;
+        }
+        cached[dev] = static_cast<float*>(p);
+    }
+    *ptr = cached[dev];
+    return SNB_OK;
+}
+
+}  // namespace
+
 int fused_attention_backward(cudaStream_t stream, const void* q, const void* k, const void* v, const void* out,
                              int out_type, const void* d_out, const float* lse, uint64_t count, uint64_t queries,
                              uint64_t keys, float scale, uint64_t query_offset, float* dq, float* dk, float* dv,
-                             std::string* err) {
+                             bool static_scratch_only, std::string* err) {
     if (count == 0) return SNB_OK;
     DeviceInfo dev;
     int rc = current_device_info(&dev, err);
@@ -471,6 +504,15 @@ int fused_attention_backward(cudaStream_t stream, const void* q, const void* k, 
     const uint64_t lim = (1ull << 31) - 256;
     if (count > lim || queries > lim || keys > lim) {
         *err = "fused attention backward: sizes out of range";
+        return SNB_ERR_INVALID_ARGUMENT;
+    }
+    // Scratch: per query (-lse * log2(e), D), matrices `stride` floats apart (16-byte multiple for the tensor map).
+    const uint64_t stride = (2 * queries + 3) / 4 * 4;
+    const uint64_t scratch_bytes = count * stride * sizeof(float);
+    if (static_scratch_only && queries > 0 && keys > 0 && scratch_bytes > kStaticScratchBytes) {
+        *err = "fused attention backward (no-alloc): needs " + std::to_string(scratch_bytes) +
+               " bytes of row statistics (count * queries * 8, rounded), the static scratch holds " +
+               std::to_string(kStaticScratchBytes);
         return SNB_ERR_INVALID_ARGUMENT;
     }
     for (const void* ptr : {q, k, v, out, d_out, static_cast<const void*>(dq), static_cast<const void*>(dk),
@@ -497,15 +539,21 @@ int fused_attention_backward(cudaStream_t stream, const void* q, const void* k, 
         if (rc == SNB_OK) rc = memset_or_fail(dv, count * keys * FB_D * sizeof(float), "cudaMemsetAsync(dv)");
         return rc;
     }
-    // Scratch: per query (-lse * log2(e), D), matrices `stride` floats apart (16-byte multiple for the tensor map).
-    const uint64_t stride = (2 * queries + 3) / 4 * 4;
     float* stats = nullptr;
-    cudaError_t e = cudaMallocAsync(reinterpret_cast<void**>(&stats), count * stride * sizeof(float), stream);
-    if (e != cudaSuccess) {
-        *err = cuda_message("cudaMallocAsync(row statistics)", e);
-        return SNB_ERR_CUDA;
+    cudaError_t e = cudaSuccess;
+    if (static_scratch_only) {
+        rc = static_scratch(&stats, err);
+        if (rc != SNB_OK) return rc;
+    } else {
+        e = cudaMallocAsync(reinterpret_cast<void**>(&stats), scratch_bytes, stream);
+        if (e != cudaSuccess) {
+            *err = cuda_message("cudaMallocAsync(row statistics)", e);
+            return SNB_ERR_CUDA;
+        }
     }
-    auto release = [&]() { cudaFreeAsync(stats, stream); };
+    auto release = [&]() {
+        if (!static_scratch_only) cudaFreeAsync(stats, stream);
+    };
     const uint64_t rows = count * queries;
     fb_rowstats_kernel<<<static_cast<unsigned>((rows + 7) / 8), 256, 0, stream>>>(
         out, out_type == SNB_TYPE_BF16 ? 1 : 0, static_cast<const uint16_t*>(d_out), lse, stats,

@@ -263,19 +263,20 @@ class Gpu:
                                                     _ptr(lse) if lse is not None else None))
 
     def causal_attention_backward(self, q, k, v, out, d_out, lse, dq, dk, dv, scale: float,
-                                  query_offset: int = 0) -> None:
+                                  query_offset: int = 0, no_alloc: bool = False) -> None:
         """Fused causal attention backward (snb_causal_attention_backward): q, d_out [count, queries, 64] and k, v
         [count, keys, 64] bf16; out (f32 or bf16) and lse as written by causal_attention_forward; dq, dk, dv f32,
-        overwritten."""
+        overwritten. no_alloc selects snb_causal_attention_backward_noalloc (static scratch, nothing allocated;
+        overlapping calls on one device race on its scratch)."""
         import torch
 
         _require_cuda(q, k, v, out, d_out, lse, dq, dk, dv)
         count, queries, head_dim = q.shape
         keys = k.shape[1]
         out_type = _ffi.TYPE_BF16 if out.dtype == torch.bfloat16 else _ffi.TYPE_F32
-        check(self.lib.snb_causal_attention_backward(self._stream_handle(), _ptr(q), _ptr(k), _ptr(v), _ptr(out),
-                                                     out_type, _ptr(d_out), _ptr(lse), count, queries, keys, head_dim,
-                                                     scale, query_offset, _ptr(dq), _ptr(dk), _ptr(dv)))
+        fn = self.lib.snb_causal_attention_backward_noalloc if no_alloc else self.lib.snb_causal_attention_backward
+        check(fn(self._stream_handle(), _ptr(q), _ptr(k), _ptr(v), _ptr(out), out_type, _ptr(d_out), _ptr(lse), count,
+                 queries, keys, head_dim, scale, query_offset, _ptr(dq), _ptr(dk), _ptr(dv)))
 
     def softmax_backward(self, probabilities, grad) -> None:
         """`Gpu::softmax_backward` (ops/attention.rs:83-100)."""
