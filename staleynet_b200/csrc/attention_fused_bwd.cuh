@@ -9,7 +9,7 @@
 //   fb_rowstats_kernel   per query: (-lse * log2(e), D) into a scratch buffer, one warp per query row.
 //   fb_backward_kernel   one CTA of 448 threads per 128-key tile of one matrix, looping over the query tiles whose
 //                        queries see any of its keys. Keys sit on the TMEM lanes:
-//     warp 12      TMA: K_j, V_j once; then Q_i, dO_i and the row statistics of tile i through a 2-stage ring.
+//     warp 12      TMA: K_j, V_j once; then Q_i, dO_i and the row statistics of tile i through a 3-stage ring.
 //     warp 13      allocates TMEM (S^T, dP^T: 128 f32 columns each; dV, dK, dQ: 64 each; P^T: 64 columns of bf16
 //                  pairs) and, on one elected thread, issues per query tile i:
 //                    S^T = K_j Q_i^T, dP^T = V_j dO_i^T          (M=128 keys, N=128 queries, K=64)
@@ -32,7 +32,7 @@ namespace snb {
 constexpr int FB_BK = 128;   // keys per CTA (TMEM lanes of S^T, dP^T, dV, dK)
 constexpr int FB_BQ = 128;   // queries per iteration
 constexpr int FB_D = 64;
-constexpr int FB_STAGES = 2;
+constexpr int FB_STAGES = 3;
 constexpr int FB_ELEM_WARPS = 8;
 constexpr int FB_DQ_WARP0 = 8;
 constexpr int FB_PRODUCER_WARP = 12;
@@ -186,13 +186,10 @@ __global__ void __launch_bounds__(FB_THREADS, 1)
             const uint32_t ks = smem_addr(k_s), vs = smem_addr(v_s), dss = smem_addr(ds_s);
             bool ok = n_iter == 0 || mbar_wait(smem_addr(kv_full), 0);
             bool issued = false;
-            int stage = 0;
-            uint32_t phase = 0;
-            for (int32_t n = 0; n < n_iter && ok; ++n) {
-                const uint32_t qs = smem_addr(stage_s + stage * FbSmem::STAGE);
+            // S^T(n) = K_j Q_i^T and dP^T(n) = V_j dO_i^T for the tile in `stage`.
+            auto issue_scores = [&](int st) {
+                const uint32_t qs = smem_addr(stage_s + st * FbSmem::STAGE);
                 const uint32_t dos = qs + FbSmem::QT;
-                if (!mbar_wait(smem_addr(&qdo_full[stage]), phase) ||
-                    !mbar_wait(smem_addr(sdp_empty), (n & 1) ^ 1u)) { ok = false; break; }
                 tcgen05_fence_after_sync();
 #pragma unroll
                 for (int k = 0; k < FB_D / 16; ++k) {
@@ -203,6 +200,25 @@ __global__ void __launch_bounds__(FB_THREADS, 1)
                 }
                 issued = true;
                 umma_commit(smem_addr(sdp_full));
+            };
+            int stage = 0;
+            uint32_t phase = 0;
+            if (ok && n_iter > 0) {
+                ok = mbar_wait(smem_addr(&qdo_full[0]), 0);
+                if (ok) issue_scores(0);
+            }
+            for (int32_t n = 0; n < n_iter && ok; ++n) {
+                const int next_stage = stage + 1 == FB_STAGES ? 0 : stage + 1;
+                const uint32_t next_phase = next_stage == 0 ? phase ^ 1u : phase;
+                // The next tile's scores as soon as the elementwise warps hold this tile's in registers, so that
+                // they overlap this tile's remaining products.
+                if (n + 1 < n_iter) {
+                    if (!mbar_wait(smem_addr(sdp_empty), n & 1) ||
+                        !mbar_wait(smem_addr(&qdo_full[next_stage]), next_phase)) { ok = false; break; }
+                    issue_scores(next_stage);
+                }
+                const uint32_t qs = smem_addr(stage_s + stage * FbSmem::STAGE);
+                const uint32_t dos = qs + FbSmem::QT;
                 if (!mbar_wait(smem_addr(pds_full), n & 1)) { ok = false; break; }
                 tcgen05_fence_after_sync();
 #pragma unroll
@@ -232,7 +248,8 @@ __global__ void __launch_bounds__(FB_THREADS, 1)
                 umma_commit(smem_addr(dq_full));
                 umma_commit(smem_addr(pds_empty));
                 umma_commit(smem_addr(&qdo_empty[stage]));
-                if (++stage == FB_STAGES) { stage = 0; phase ^= 1u; }
+                stage = next_stage;
+                phase = next_phase;
             }
             if (ok) {
                 if (issued) umma_commit(smem_addr(acc_done));   // after every product above
@@ -263,42 +280,62 @@ __global__ void __launch_bounds__(FB_THREADS, 1)
             const int64_t hi64 = static_cast<int64_t>(p.sq) - qh;
             const int32_t lo = static_cast<int32_t>(lo64 < 0 ? 0 : (lo64 > 64 ? 64 : lo64));
             const int32_t hi = static_cast<int32_t>(hi64 < 0 ? 0 : (hi64 > 64 ? 64 : hi64));
-            if (!warp_wait(smem_addr(sdp_full), n & 1) || !warp_wait(smem_addr(&qdo_full[stage]), phase) ||
-                (n > 0 && !warp_wait(smem_addr(pds_empty), (n - 1) & 1))) {
+            if (!warp_wait(smem_addr(sdp_full), n & 1) || !warp_wait(smem_addr(&qdo_full[stage]), phase)) {
                 ok = false;
                 break;
             }
             tcgen05_fence_after_sync();
-            const float* stats = reinterpret_cast<const float*>(stage_s + stage * FbSmem::STAGE + 2 * FbSmem::QT) + 2 * 64 * h;
-#pragma unroll 1
+            // (nl, D) of query 2k, 2k+1 of this half at stats + 16 k bytes, read with explicit shared loads.
+            const uint32_t stats = smem_addr(stage_s + stage * FbSmem::STAGE + 2 * FbSmem::QT) + 8 * 64 * h;
+            // Off the diagonal and the ragged edges every column of every row of the warp is visible.
+            const bool unmasked = __all_sync(0xffffffffu, lo == 0 && hi == 64);
+            // Scores and their gradients in 16-column chunks, the next chunk's TMEM loads in flight while this one
+            // is computed.
+            uint32_t s[2][16], dp[2][16];
+            tmem_load_32x32b_x16(tmem_base + lane_base + FB_S_COL + 64 * h, s[0]);
+            tmem_load_32x32b_x16(tmem_base + lane_base + FB_DP_COL + 64 * h, dp[0]);
+            tmem_load_wait();
+#pragma unroll
             for (int cc = 0; cc < 4; ++cc) {
-                uint32_t s[16], dp[16];
-                tmem_load_32x32b_x16(tmem_base + lane_base + FB_S_COL + 64 * h + 16 * cc, s);
-                tmem_load_32x32b_x16(tmem_base + lane_base + FB_DP_COL + 64 * h + 16 * cc, dp);
-                tmem_load_wait();
-                if (cc == 3) {
-                    // S^T and dP^T are in registers: the next tile's products may overwrite them.
+                const int b = cc & 1;
+                if (cc < 3) {
+                    tmem_load_32x32b_x16(tmem_base + lane_base + FB_S_COL + 64 * h + 16 * (cc + 1), s[b ^ 1]);
+                    tmem_load_32x32b_x16(tmem_base + lane_base + FB_DP_COL + 64 * h + 16 * (cc + 1), dp[b ^ 1]);
+                }
+                uint32_t pw[8], dw[8];
+#pragma unroll
+                for (int j = 0; j < 16; j += 2) {
+                    const float4 nd = ld_shared_f4(stats + 8 * (16 * cc + j));   // (nl, D, nl, D) of columns j, j+1
+                    const int col = 16 * cc + j;
+                    float p0 = exp2_ftz(fmaf(__uint_as_float(s[b][j]), c, nd.x));
+                    float p1 = exp2_ftz(fmaf(__uint_as_float(s[b][j + 1]), c, nd.z));
+                    if (!unmasked) {
+                        p0 = (col >= lo && col < hi) ? p0 : 0.0f;
+                        p1 = (col + 1 >= lo && col + 1 < hi) ? p1 : 0.0f;
+                    }
+                    pw[j / 2] = pack_bf16x2(p0, p1);
+                    dw[j / 2] = pack_bf16x2(p0 * (__uint_as_float(dp[b][j]) - nd.y),
+                                            p1 * (__uint_as_float(dp[b][j + 1]) - nd.w));
+                }
+                if (cc == 0 && n > 0 && !warp_wait(smem_addr(pds_empty), (n - 1) & 1)) {
+                    // (P^T and dS^T of the previous tile are free once its dV, dK, dQ products finished.)
+                    ok = false;
+                }
+                if (ok) {
+                    tmem_store_32x32b_x8(tmem_base + lane_base + FB_P_COL + 32 * h + 8 * cc, pw);
+                    // dS^T row r, queries 64h + 16cc ..: 16-byte chunks 2cc, 2cc + 1 of the 128-byte row, swizzled.
+                    st_shared_v4(ds_row + (((2 * cc) ^ (r & 7)) << 4), dw[0], dw[1], dw[2], dw[3]);
+                    st_shared_v4(ds_row + (((2 * cc + 1) ^ (r & 7)) << 4), dw[4], dw[5], dw[6], dw[7]);
+                }
+                if (cc < 3) tmem_load_wait();
+                if (cc == 2) {
+                    // S^T and dP^T are all in registers: the next tile's products may overwrite them.
                     tcgen05_fence_before_sync();
                     __syncwarp();
                     if (lane == 0) mbar_arrive(smem_addr(sdp_empty));
                 }
-                const float4* st4 = reinterpret_cast<const float4*>(stats + 32 * cc);
-                uint32_t pw[8], dw[8];
-#pragma unroll
-                for (int j = 0; j < 16; j += 2) {
-                    const float4 nd = st4[j / 2];   // (nl, D) of columns 16cc + j and 16cc + j + 1
-                    const int col = 16 * cc + j;
-                    const float p0 = (col >= lo && col < hi) ? exp2_ftz(fmaf(__uint_as_float(s[j]), c, nd.x)) : 0.0f;
-                    const float p1 =
-                        (col + 1 >= lo && col + 1 < hi) ? exp2_ftz(fmaf(__uint_as_float(s[j + 1]), c, nd.z)) : 0.0f;
-                    pw[j / 2] = pack_bf16x2(p0, p1);
-                    dw[j / 2] = pack_bf16x2(p0 * (__uint_as_float(dp[j]) - nd.y), p1 * (__uint_as_float(dp[j + 1]) - nd.w));
-                }
-                tmem_store_32x32b_x8(tmem_base + lane_base + FB_P_COL + 32 * h + 8 * cc, pw);
-                // dS^T row r, queries 64h + 16cc ..: 16-byte chunks 2cc, 2cc + 1 of the 128-byte row, swizzled.
-                st_shared_v4(ds_row + (((2 * cc) ^ (r & 7)) << 4), dw[0], dw[1], dw[2], dw[3]);
-                st_shared_v4(ds_row + (((2 * cc + 1) ^ (r & 7)) << 4), dw[4], dw[5], dw[6], dw[7]);
             }
+            if (!ok) break;
             tmem_store_wait();
             fence_proxy_async_shared();   // dS^T writes -> the tensor core's reads
             tcgen05_fence_before_sync();
