@@ -242,6 +242,42 @@ SNB_API int snb_causal_attention_backward_noalloc(void* stream, const uint16_t* 
                                                   uint64_t queries, uint64_t keys, uint64_t head_dim, float scale,
                                                   uint64_t query_offset, float* dq, float* dk, float* dv);
 
+/* One classifier head of the output layer, laid out like the reference's `CrossEntropyHead` (ops/loss.rs:14-30):
+ * the head owns logit columns column_offset .. column_offset + classes of every row and reads its target at
+ * target_offset within each row of target_stride targets; grad_scale multiplies its gradient. */
+typedef struct snb_cross_entropy_head {
+    uint64_t column_offset;
+    uint64_t classes;
+    uint64_t target_stride;
+    uint64_t target_offset;
+    float grad_scale;
+    uint32_t reserved; /* 0 */
+} snb_cross_entropy_head;
+
+/* Softmax cross-entropy of one head with its gradient. Replaces `Gpu::cross_entropy` (ops/loss.rs:35-71; kernel
+ * kernels/loss.rs:54-94): for each of `rows` rows of logits [rows, cols] (f32), losses[row] = logsumexp(z) - z[target]
+ * and the head's columns of logits_grad [rows, cols] (f32) = (softmax(z) - onehot(target)) * grad_scale; a target of
+ * 0xFFFFFFFF (EMPTY_TOKEN) gives loss 0 and a zero gradient; other columns of logits_grad are left untouched. The
+ * reference's three checks are status codes in its order and words: "head exceeds logits"
+ * (column_offset + classes > cols), "losses too small" (losses_len < rows), "too few targets"
+ * (targets_len < rows * target_stride, or the last target beyond targets_len). A target >= classes (which the
+ * reference would read outside the row) gives a NaN loss and gradient instead of a fault. */
+SNB_API int snb_cross_entropy(void* stream, const float* logits, uint64_t rows, uint64_t cols,
+                              const uint32_t* targets, uint64_t targets_len, const snb_cross_entropy_head* head,
+                              float* losses, uint64_t losses_len, float* logits_grad);
+
+/* The output layer's forward and loss in two launches: `head` (a snb_gemm, count 1, writing logits [rows, codebooks *
+ * codebook_size] row-major to head->output as f32 or bf16, bias included) then the cross-entropy of every codebook
+ * head c (columns c * codebook_size .., target c of each row of `codebooks` targets, gradient scale grad_scales[c],
+ * a device array) in one launch. loss_sums[c] (device, [codebooks]) receives the sum of head c's row losses (it is
+ * zeroed first), so one small copy replaces the reference's per-codebook loss downloads (training.rs:209-235).
+ * logits_grad ([rows, codebooks * codebook_size] of grad_type) may be head->output itself when grad_type equals
+ * head->output_type: the gradient then overwrites the logits in place, each logit read once. No f32 logits need
+ * exist. No reference counterpart as one call: it replaces Linear::forward of the head plus `codebook_losses`. */
+SNB_API int snb_head_cross_entropy(void* stream, const snb_gemm_args* head, const uint32_t* targets,
+                                   uint64_t targets_len, uint64_t codebooks, uint64_t codebook_size,
+                                   const float* grad_scales, float* loss_sums, void* logits_grad, int32_t grad_type);
+
 /* Failure-detection self-test: launches a one-thread kernel that waits on an mbarrier nothing completes, through
  * the bounded wait every tensor-core pipeline wait uses. The wait gives up after limit_ns (at most 1 s), records a
  * timeout in the device status word and the kernel returns normally; a following snb_device_status() reports

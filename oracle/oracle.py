@@ -86,6 +86,8 @@ def lib() -> ctypes.CDLL:
             L.snb_oracle_gelu_derivative_fill.argtypes = [fp, fp, c_uint64]
             L.snb_oracle_causal_softmax.argtypes = [fp, c_uint64, c_uint64, c_uint64, c_float, c_uint64]
             L.snb_oracle_softmax_backward.argtypes = [fp, fp, c_uint64, c_uint64]
+            L.snb_oracle_cross_entropy.argtypes = [fp, POINTER(c_uint32), c_uint64, c_uint64, c_uint64, c_uint64,
+                                                   c_uint64, c_uint64, c_float, fp, fp]
             L.snb_oracle_max_threads.restype = c_int
             _lib = L
     return _lib
@@ -199,6 +201,16 @@ def causal_softmax(scores: np.ndarray, queries: int, keys: int, scale: float, qu
 def softmax_backward(probabilities: np.ndarray, grad: np.ndarray, cols: int) -> None:
     """reference::softmax_backward (reference.rs:122-137), in place on grad."""
     lib().snb_oracle_softmax_backward(_f(probabilities), _f(grad), grad.size // cols, cols)
+
+
+def cross_entropy(logits: np.ndarray, targets: np.ndarray, cols: int, column_offset: int, classes: int,
+                  target_stride: int, target_offset: int, grad_scale: float, losses: np.ndarray,
+                  logits_grad: np.ndarray) -> None:
+    """reference::cross_entropy (reference.rs:139-166) for one head, in place on losses and logits_grad."""
+    targets = np.ascontiguousarray(targets, dtype=np.uint32)
+    rows = losses.size
+    lib().snb_oracle_cross_entropy(_f(logits), targets.ctypes.data_as(POINTER(c_uint32)), rows, cols, column_offset,
+                                   classes, target_stride, target_offset, grad_scale, _f(losses), _f(logits_grad))
 
 
 def max_threads() -> int:

@@ -244,6 +244,34 @@ void snb_oracle_softmax_backward(const float* probabilities, float* grad, uint64
     }
 }
 
+/* reference::cross_entropy (reference.rs:139-166) for one head: per row, loss = log_partition - z[target] and the
+ * head's gradient columns ((exp(z - log_partition) - onehot) * grad_scale), f32 throughout; rows whose target is
+ * EMPTY_TOKEN (u32::MAX, kernels/mod.rs:46) get loss 0 and a zero gradient. Other columns are left untouched. */
+void snb_oracle_cross_entropy(const float* logits, const uint32_t* targets, uint64_t rows, uint64_t cols,
+                              uint64_t column_offset, uint64_t classes, uint64_t target_stride, uint64_t target_offset,
+                              float grad_scale, float* losses, float* logits_grad) {
+    for (uint64_t row = 0; row < rows; ++row) {
+        const float* z = logits + row * cols + column_offset;
+        float* g = logits_grad + row * cols + column_offset;
+        const uint32_t target = targets[row * target_stride + target_offset];
+        if (target == 0xFFFFFFFFu) {
+            losses[row] = 0.0f;
+            for (uint64_t c = 0; c < classes; ++c) g[c] = 0.0f;
+            continue;
+        }
+        float maximum = -INFINITY;
+        for (uint64_t c = 0; c < classes; ++c) maximum = fmaxf(maximum, z[c]);
+        float total = 0.0f;
+        for (uint64_t c = 0; c < classes; ++c) total += expf(z[c] - maximum);
+        const float log_partition = maximum + logf(total);
+        losses[row] = log_partition - z[target];
+        for (uint64_t c = 0; c < classes; ++c) {
+            const float one_hot = (uint64_t)target == c ? 1.0f : 0.0f;
+            g[c] = (expf(z[c] - log_partition) - one_hot) * grad_scale;
+        }
+    }
+}
+
 int snb_oracle_max_threads(void) {
 #ifdef _OPENMP
     return omp_get_max_threads();

@@ -59,6 +59,8 @@ EXPORTED_SYMBOLS = (
     "snb_causal_attention_forward",
     "snb_causal_attention_backward",
     "snb_causal_attention_backward_noalloc",
+    "snb_cross_entropy",
+    "snb_head_cross_entropy",
     "snb_selftest_bounded_wait",
     "snb_abi_version",
 )
@@ -79,6 +81,12 @@ class Product(ctypes.Structure):
         ("scale", c_float),
         ("accumulate", c_uint32),
     ]
+
+
+class CrossEntropyHead(ctypes.Structure):
+    """snb_cross_entropy_head: the reference's CrossEntropyHead (ops/loss.rs:14-30)."""
+    _fields_ = [("column_offset", c_uint64), ("classes", c_uint64), ("target_stride", c_uint64),
+                ("target_offset", c_uint64), ("grad_scale", c_float), ("reserved", c_uint32)]
 
 
 class GemmArgs(ctypes.Structure):
@@ -159,6 +167,12 @@ def load() -> ctypes.CDLL:
         lib.snb_causal_attention_backward.restype = c_int
         lib.snb_causal_attention_backward_noalloc.argtypes = lib.snb_causal_attention_backward.argtypes
         lib.snb_causal_attention_backward_noalloc.restype = c_int
+        lib.snb_cross_entropy.argtypes = [c_void_p, c_void_p, c_uint64, c_uint64, c_void_p, c_uint64,
+                                          POINTER(CrossEntropyHead), c_void_p, c_uint64, c_void_p]
+        lib.snb_cross_entropy.restype = c_int
+        lib.snb_head_cross_entropy.argtypes = [c_void_p, POINTER(GemmArgs), c_void_p, c_uint64, c_uint64, c_uint64,
+                                               c_void_p, c_void_p, c_void_p, c_int32]
+        lib.snb_head_cross_entropy.restype = c_int
         lib.snb_selftest_bounded_wait.argtypes = [c_void_p, c_uint64]
         lib.snb_selftest_bounded_wait.restype = c_int
         lib.snb_abi_version.argtypes = []

@@ -291,6 +291,62 @@ int snb_causal_attention_backward_noalloc(void* stream, const uint16_t* q, const
                                     lse, count, queries, keys, head_dim, scale, query_offset, dq, dk, dv);
 }
 
+int snb_cross_entropy(void* stream, const float* logits, uint64_t rows, uint64_t cols, const uint32_t* targets,
+                      uint64_t targets_len, const snb_cross_entropy_head* head, float* losses, uint64_t losses_len,
+                      float* logits_grad) {
+    t_last_path = SNB_PATH_NONE;
+    if (head == nullptr) return fail(SNB_ERR_INVALID_ARGUMENT, "cross_entropy: head is null");
+    // The reference's checks (ops/loss.rs:43-47), in its order and words.
+    if (head->column_offset > cols || head->classes > cols - head->column_offset)
+        return fail(SNB_ERR_INVALID_ARGUMENT, "cross_entropy: head exceeds logits");
+    if (losses_len < rows) return fail(SNB_ERR_INVALID_ARGUMENT, "cross_entropy: losses too small");
+    if (rows > 0 && (head->target_stride == 0 || targets_len / head->target_stride < rows ||
+                     (rows - 1) * head->target_stride + head->target_offset >= targets_len))
+        return fail(SNB_ERR_INVALID_ARGUMENT, "cross_entropy: too few targets");
+    if (rows == 0 || head->classes == 0) return SNB_OK;
+    if (logits == nullptr || targets == nullptr || losses == nullptr || logits_grad == nullptr)
+        return fail(SNB_ERR_INVALID_ARGUMENT, "cross_entropy: null pointer");
+    std::string err;
+    int rc = cross_entropy_launch(static_cast<cudaStream_t>(stream), logits, SNB_TYPE_F32, rows, cols, targets,
+                                  head->target_stride, 1, head->column_offset, head->classes, head->target_offset,
+                                  nullptr, head->grad_scale, losses, nullptr, logits_grad, SNB_TYPE_F32, &err);
+    if (rc != SNB_OK) return fail(rc, err);
+    t_last_path = SNB_PATH_SIMT;
+    return SNB_OK;
+}
+
+int snb_head_cross_entropy(void* stream, const snb_gemm_args* head, const uint32_t* targets, uint64_t targets_len,
+                           uint64_t codebooks, uint64_t codebook_size, const float* grad_scales, float* loss_sums,
+                           void* logits_grad, int32_t grad_type) {
+    t_last_path = SNB_PATH_NONE;
+    if (head == nullptr) return fail(SNB_ERR_INVALID_ARGUMENT, "head_cross_entropy: head is null");
+    const snb_product& p = head->product;
+    if (head->count != 1) return fail(SNB_ERR_INVALID_ARGUMENT, "head_cross_entropy: the head GEMM must have count 1");
+    if (codebooks == 0 || codebook_size == 0 || p.cols / codebooks != codebook_size || p.cols % codebooks != 0)
+        return fail(SNB_ERR_INVALID_ARGUMENT, "head_cross_entropy: logits columns differ from codebooks * codebook_size");
+    if (grad_type != SNB_TYPE_F32 && grad_type != SNB_TYPE_BF16)
+        return fail(SNB_ERR_INVALID_ARGUMENT, "head_cross_entropy: unknown gradient type");
+    if (logits_grad == head->output && grad_type != head->output_type)
+        return fail(SNB_ERR_INVALID_ARGUMENT,
+                    "head_cross_entropy: an in-place gradient must have the logits' element type");
+    if (p.rows > 0 && targets_len / codebooks < p.rows)
+        return fail(SNB_ERR_INVALID_ARGUMENT, "head_cross_entropy: too few targets");
+    if (p.rows > 0 && (targets == nullptr || grad_scales == nullptr || loss_sums == nullptr || logits_grad == nullptr))
+        return fail(SNB_ERR_INVALID_ARGUMENT, "head_cross_entropy: null pointer");
+    int rc = snb_gemm(stream, head);
+    if (rc != SNB_OK) return rc;   // (snb_gemm has set the message)
+    const int gemm_path = t_last_path;
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    cudaError_t e = cudaMemsetAsync(loss_sums, 0, codebooks * sizeof(float), s);
+    if (e != cudaSuccess) return fail(SNB_ERR_CUDA, cuda_message("cudaMemsetAsync(loss_sums)", e));
+    std::string err;
+    rc = cross_entropy_launch(s, head->output, head->output_type, p.rows, p.cols, targets, codebooks, codebooks, 0,
+                              codebook_size, 0, grad_scales, 0.0f, nullptr, loss_sums, logits_grad, grad_type, &err);
+    if (rc != SNB_OK) return fail(rc, err);
+    t_last_path = gemm_path;
+    return SNB_OK;
+}
+
 int snb_selftest_bounded_wait(void* stream, uint64_t limit_ns) {
     if (limit_ns == 0 || limit_ns > 1000000000ull)
         return fail(SNB_ERR_INVALID_ARGUMENT, "selftest: limit_ns must lie in (0, 1 s]");

@@ -57,6 +57,15 @@ int causal_softmax_backward(cudaStream_t stream, const float* probabilities, flo
 int fused_attention_forward(cudaStream_t stream, const void* q, const void* k, const void* v, uint64_t count,
                             uint64_t queries, uint64_t keys, float scale, uint64_t query_offset, void* out,
                             int out_type, float* lse, std::string* err);
+// Softmax cross-entropy with its gradient over `heads` classifiers side by side (cross_entropy.cu): head h owns
+// columns column_offset + h * classes .. and target target_offset + h of each target row. row_losses
+// ([rows * heads], head fastest) and loss_sums ([heads], added to) may be null; grad may alias logits when the
+// element types match.
+int cross_entropy_launch(cudaStream_t stream, const void* logits, int logits_type, uint64_t rows, uint64_t row_width,
+                         const uint32_t* targets, uint64_t target_stride, uint64_t heads, uint64_t column_offset,
+                         uint64_t classes, uint64_t target_offset, const float* grad_scales, float grad_scale,
+                         float* row_losses, float* loss_sums, void* grad, int grad_type, std::string* err);
+
 // Fused causal attention backward (attention_fused_bwd.cuh): dq [count, queries, 64], dk and dv [count, keys, 64],
 // all f32 and overwritten, from bf16 q, k, v, d_out, the forward's output (f32 or bf16) and its log-sum-exp. The
 // row-statistics scratch comes from cudaMallocAsync on `stream`, or with static_scratch_only from a fixed

@@ -100,6 +100,21 @@ class MatmulSpec:
         return (self.batch.count - 1) * stride + per_matrix
 
 
+EMPTY_TOKEN = 0xFFFFFFFF   # a missing target (crates/staleynet-cuda/src/kernels/mod.rs:46)
+
+
+@dataclass(frozen=True)
+class CrossEntropyHead:
+    """`CrossEntropyHead` (crates/staleynet-cuda/src/ops/loss.rs:14-30): which logit columns and which target of each
+    row one classifier owns."""
+
+    column_offset: int
+    classes: int
+    target_stride: int
+    target_offset: int
+    grad_scale: float
+
+
 class MatmulKernel(enum.Enum):
     """Arithmetic of `Gpu.matmul` (device.rs:38-67). The reference's four f32 kernels become two precisions of
     one sm_100a implementation; BF16_TENSOR_CORE is new and needs bf16 operands."""
@@ -197,6 +212,15 @@ class Gpu:
              pre_activation=None, gelu_input=None, residual=None, causal: int = _ffi.CAUSAL_NONE,
              causal_offset: int = 0) -> None:
         """`Gpu.matmul` with the caller's elementwise follow-up fused into the epilogue (snb_gemm)."""
+        args = self.gemm_args(spec, left, right, output, bias=bias, activation=activation,
+                              pre_activation=pre_activation, gelu_input=gelu_input, residual=residual, causal=causal,
+                              causal_offset=causal_offset)
+        check(self.lib.snb_gemm(self._stream_handle(), ctypes.byref(args)))
+
+    def gemm_args(self, spec: MatmulSpec, left, right, output, *, bias=None, activation: int = _ffi.ACTIVATION_NONE,
+                  pre_activation=None, gelu_input=None, residual=None, causal: int = _ffi.CAUSAL_NONE,
+                  causal_offset: int = 0) -> _ffi.GemmArgs:
+        """The snb_gemm_args of `gemm` (for entry points that take a GEMM as an argument)."""
         import torch
 
         _require_cuda(left, right, output, bias, pre_activation, gelu_input, residual)
@@ -223,7 +247,39 @@ class Gpu:
         args.residual = _ptr(residual) if residual is not None else None
         args.causal = causal
         args.causal_offset = causal_offset
-        check(self.lib.snb_gemm(self._stream_handle(), ctypes.byref(args)))
+        return args
+
+    def cross_entropy(self, logits, targets, head: "CrossEntropyHead", losses, logits_grad) -> None:
+        """`Gpu::cross_entropy` (ops/loss.rs:35-71): per-row losses and this head's gradient columns, f32."""
+        import torch
+
+        _require_cuda(logits, targets, losses, logits_grad)
+        if logits_grad.shape != logits.shape:
+            raise AssertionError("cross_entropy: gradient shape")
+        rows, cols = logits.shape
+        t = targets if targets.dtype == torch.int32 else targets.to(torch.int32)
+        h = _ffi.CrossEntropyHead(head.column_offset, head.classes, head.target_stride, head.target_offset,
+                                  head.grad_scale, 0)
+        code = self.lib.snb_cross_entropy(self._stream_handle(), _ptr(logits), rows, cols, _ptr(t), t.numel(),
+                                          ctypes.byref(h), _ptr(losses), losses.numel(), _ptr(logits_grad))
+        if code == _ffi.ERR_INVALID_ARGUMENT:
+            raise AssertionError(self.lib.snb_last_error().decode())
+        check(code)
+
+    def head_cross_entropy(self, spec: MatmulSpec, x, w, logits, targets, codebooks: int, grad_scales, loss_sums,
+                           logits_grad, *, bias=None) -> None:
+        """The output layer's forward and per-codebook cross-entropy (snb_head_cross_entropy): logits = x w (+ bias)
+        then, for every codebook c, loss_sums[c] = sum of its row losses and its gradient columns into logits_grad
+        (which may be `logits` itself for an in-place gradient). targets: [rows, codebooks] int32/uint32 bits."""
+        import torch
+
+        _require_cuda(targets, grad_scales, loss_sums, logits_grad)
+        args = self.gemm_args(spec, x, w, logits, bias=bias)
+        t = targets if targets.dtype == torch.int32 else targets.to(torch.int32)
+        grad_type = _ffi.TYPE_BF16 if logits_grad.dtype == torch.bfloat16 else _ffi.TYPE_F32
+        check(self.lib.snb_head_cross_entropy(self._stream_handle(), ctypes.byref(args), _ptr(t), t.numel(),
+                                              codebooks, spec.cols // codebooks, _ptr(grad_scales), _ptr(loss_sums),
+                                              _ptr(logits_grad), grad_type))
 
     def causal_softmax(self, scores, queries: int, scale: float, query_offset: int) -> None:
         """`Gpu::causal_softmax` (ops/attention.rs:57-81) on scores [rows, keys]."""

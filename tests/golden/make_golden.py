@@ -95,6 +95,46 @@ GELU_KATS = [
     },
 ]
 
+# Cross-entropy of one head (reference::cross_entropy, reference.rs:139-166). EMPTY_TOKEN is u32::MAX
+# (crates/staleynet-cuda/src/kernels/mod.rs:46); 7.0 marks gradient entries the head must leave untouched.
+EMPTY = 0xFFFFFFFF
+CROSS_ENTROPY_KATS = [
+    {
+        "name": "cross_entropy_writes_losses_and_gradients_for_the_target_head",
+        "source": f"{REF_FILE}:309-330",
+        "snippets": ["[1.0, 2.0, 3.0, 0.0, 0.0, 0.0, 0.0, 0.0]", "[2u32, 0]",
+                     "column_offset: 0, classes: 3, target_stride: 1, target_offset: 0, grad_scale: 1.0",
+                     "0.407_606", "1.098_612", "0.090_03", "0.244_73", "-0.334_76", "-0.666_667", "0.333_333"],
+        "logits": [1.0, 2.0, 3.0, 0.0, 0.0, 0.0, 0.0, 0.0], "targets": [2, 0], "cols": 4,
+        "head": {"column_offset": 0, "classes": 3, "target_stride": 1, "target_offset": 0, "grad_scale": 1.0},
+        "expected_losses": [[0.407606, 1e-5], [1.098612, 1e-5]],
+        "expected_grad": [[0.09003, 1e-4], [0.24473, 1e-4], [-0.33476, 1e-4], [7.0, 0.0],
+                          [-0.666667, 1e-5], [0.333333, 1e-5], [0.333333, 1e-5], [7.0, 0.0]],
+    },
+    {
+        "name": "cross_entropy_skips_empty_targets",
+        "source": f"{REF_FILE}:333-347",
+        "snippets": ["[EMPTY_TOKEN, 0]", "assert_eq!(losses[0], 0.0)", "assert_eq!(&grad[0..3], &[0.0, 0.0, 0.0])",
+                     "assert_eq!(grad[3], 7.0)", "assert!(grad[4] < 0.0 && grad[5] > 0.0 && grad[6] > 0.0)"],
+        "logits": [1.0, 2.0, 3.0, 0.0, 0.0, 0.0, 0.0, 0.0], "targets": [EMPTY, 0], "cols": 4,
+        "head": {"column_offset": 0, "classes": 3, "target_stride": 1, "target_offset": 0, "grad_scale": 1.0},
+        "expected_losses": [[0.0, 0.0], None],
+        "expected_grad": [[0.0, 0.0], [0.0, 0.0], [0.0, 0.0], [7.0, 0.0], "negative", "positive", "positive", [7.0, 0.0]],
+    },
+    {
+        "name": "cross_entropy_honours_head_offsets_and_gradient_scale",
+        "source": f"{REF_FILE}:350-366",
+        "snippets": ["[1.0, 2.0, 3.0, 4.0, 5.0, 1.0, 2.0, 3.0, 4.0, 5.0]", "[0u32, 1, 0, 0]",
+                     "column_offset: 2, classes: 2, target_stride: 2, target_offset: 1, grad_scale: 0.5",
+                     "assert_eq!(&grad[0..2], &[7.0, 7.0])", "assert_eq!(grad[4], 7.0)", "assert_eq!(grad[9], 7.0)"],
+        "logits": [1.0, 2.0, 3.0, 4.0, 5.0, 1.0, 2.0, 3.0, 4.0, 5.0], "targets": [0, 1, 0, 0], "cols": 5,
+        "head": {"column_offset": 2, "classes": 2, "target_stride": 2, "target_offset": 1, "grad_scale": 0.5},
+        "expected_losses": ["positive", "positive"],
+        "expected_grad": [[7.0, 0.0], [7.0, 0.0], "finite", "finite", [7.0, 0.0], [7.0, 0.0], [7.0, 0.0], "finite",
+                          "finite", [7.0, 0.0]],
+    },
+]
+
 # SplitMix64 is the reference's generator (crates/staleynet-model/src/random.rs:4-46). Its published output for
 # state 0 (Vigna's splitmix64.c, the algorithm of Steele, Lea & Flood 2014) pins next_u64.
 SPLITMIX_KATS = {
@@ -106,7 +146,7 @@ SPLITMIX_KATS = {
 
 def check_against_reference(reference: Path) -> None:
     lines = (reference / REF_FILE).read_text().splitlines()
-    for case in MATMUL_KATS + SOFTMAX_KATS + SOFTMAX_BACKWARD_KATS + GELU_KATS:
+    for case in MATMUL_KATS + SOFTMAX_KATS + SOFTMAX_BACKWARD_KATS + GELU_KATS + CROSS_ENTROPY_KATS:
         span = case["source"].rsplit(":", 1)[1]
         lo, hi = (int(x) for x in span.split("-"))
         text = "\n".join(lines[lo - 1:hi])
@@ -134,6 +174,7 @@ def main(argv=None) -> int:
         "causal_softmax": [{k: v for k, v in c.items() if k != "snippets"} for c in SOFTMAX_KATS],
         "softmax_backward": [{k: v for k, v in c.items() if k != "snippets"} for c in SOFTMAX_BACKWARD_KATS],
         "gelu": [{k: v for k, v in c.items() if k != "snippets"} for c in GELU_KATS],
+        "cross_entropy": [{k: v for k, v in c.items() if k != "snippets"} for c in CROSS_ENTROPY_KATS],
         "splitmix64": SPLITMIX_KATS,
     }
     (HERE / "reference_kats.json").write_text(json.dumps(out, indent=1) + "\n")

@@ -153,3 +153,34 @@ def test_f32_oracle_is_close_to_f64_on_random_data():
     o.matmul(p, 1, left, right, f32)
     o.matmul_f64(p, 1, left, right, f64)
     assert o.relative_error(f64, f32) < 1e-5
+
+
+def _check_entry(value, expected):
+    if expected is None:
+        return
+    if expected == "positive":
+        assert value > 0.0
+    elif expected == "negative":
+        assert value < 0.0
+    elif expected == "finite":
+        assert np.isfinite(value)
+    else:
+        want, tol = expected
+        assert abs(value - want) <= tol, (value, want)
+
+
+@pytest.mark.parametrize("case", KATS["cross_entropy"], ids=lambda c: c["name"])
+def test_cross_entropy_matches_the_reference_known_answers(case):
+    """reference.rs:309-366 through the oracle's restatement of reference::cross_entropy."""
+    logits = np.array(case["logits"], dtype=np.float32)
+    targets = np.array(case["targets"], dtype=np.uint32)
+    h = case["head"]
+    rows = len(case["expected_losses"])
+    losses = np.full(rows, 9.0, dtype=np.float32)
+    grad = np.full(logits.size, 7.0, dtype=np.float32)
+    o.cross_entropy(logits, targets, case["cols"], h["column_offset"], h["classes"], h["target_stride"],
+                    h["target_offset"], h["grad_scale"], losses, grad)
+    for value, expected in zip(losses, case["expected_losses"]):
+        _check_entry(float(value), expected)
+    for value, expected in zip(grad, case["expected_grad"]):
+        _check_entry(float(value), expected)
