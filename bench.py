@@ -398,6 +398,144 @@ def attention_cpu_baseline(s, budget_flops: float = 10e9, threads: int = 0) -> d
                       f"extrapolated by rows and heads; softmax passes not included"}
 
 
+def head_cpu_baseline(tokens: int, width: int, books: int, size: int, budget_flops: float = 10e9,
+                      threads: int = 0) -> dict:
+    """The oracle's reference loop on a sample of rows of the head GEMM plus reference::cross_entropy of every
+    codebook on those rows, extrapolated by rows."""
+    import numpy as np
+
+    from oracle import oracle as o
+
+    cols = books * size
+    rows = max(1, min(tokens, int(budget_flops / (2.0 * width * cols))))
+    x = np.random.default_rng(0).standard_normal(rows * width).astype(np.float32)
+    w = np.random.default_rng(1).standard_normal(width * cols).astype(np.float32) / np.float32(width ** 0.5)
+    logits = np.zeros(rows * cols, np.float32)
+    grad = np.zeros(rows * cols, np.float32)
+    losses = np.zeros(rows, np.float32)
+    targets = np.random.default_rng(2).integers(0, size, rows * books).astype(np.uint32)
+    prod = o.product(rows, cols, width, o.storage_strides(False, rows, width, 0), o.storage_strides(False, width, cols, 0), 0)
+    o.matmul_rows(prod, 1, x, w, logits, 0, rows, threads)
+    t0 = time.perf_counter()
+    used = o.matmul_rows(prod, 1, x, w, logits, 0, rows, threads)
+    for c in range(books):
+        o.cross_entropy(logits, targets, cols, c * size, size, books, c, 1.0, losses, grad)
+    seconds = (time.perf_counter() - t0) * tokens / rows
+    return {"value": 2.0 * tokens * width * cols / seconds / 1e12, "unit": UNIT, "cores": used, "kind": "port",
+            "sample": f"{rows} of {tokens} rows: head GEMM (all cores) + the 16 codebooks' cross-entropy (one core), "
+                      f"extrapolated by rows"}
+
+
+def run_head(args, rank: int, world: int, local_rank: int) -> int:
+    """BASELINE config 3's output layer, forward + loss: logits = x W + b over 16 codebooks of 1024 classes for
+    65,536 tokens, then every codebook's softmax cross-entropy and its gradient, and the loss on the host.
+
+    --head-path fused (default): snb_head_cross_entropy — bf16 logits overwritten in place by their gradient, one
+    pass, per-codebook loss sums on the device, one 64-byte copy to the host.
+    --head-path reference-shaped: the reference's sequence (training.rs:201-235) on this library — the head GEMM
+    writes f32 logits, then per codebook snb_cross_entropy (f32 gradient, per-row losses) and a download of the row
+    losses summed on the host. `value` counts the head GEMM's FLOPs either way."""
+    import torch
+
+    from staleynet_b200 import _ffi
+    from staleynet_b200.matmul import CrossEntropyHead, Gpu, MatmulSpec
+
+    torch.cuda.set_device(local_rank)
+    device = torch.device("cuda", local_rank)
+    stream = torch.cuda.current_stream(device)
+    tokens, width, books, size = args.tokens, 768, 16, 1024
+    cols = books * size
+    g = torch.Generator(device=device)
+    g.manual_seed(rank)
+    x = torch.randn(tokens, width, device=device, generator=g).bfloat16()
+    w = (torch.randn(width, cols, device=device, generator=g) / width ** 0.5).bfloat16()
+    bias = torch.zeros(cols, device=device)
+    targets = torch.randint(0, size, (tokens, books), device=device, generator=g, dtype=torch.int32)
+    scales = torch.full((books,), 1.0 / (tokens * books), device=device)
+    gpu = Gpu(local_rank)
+    spec = MatmulSpec.new(tokens, cols, width)
+    fused = args.head_path == "fused"
+    host_sums = torch.empty(books, dtype=torch.float32, pin_memory=True)
+    host_rows = torch.empty(tokens, dtype=torch.float32, pin_memory=True)
+    if fused:
+        logits = torch.empty(tokens, cols, device=device, dtype=torch.bfloat16)
+        loss_sums = torch.empty(books, device=device)
+    else:
+        logits = torch.empty(tokens, cols, device=device)
+        grad = torch.empty(tokens, cols, device=device)
+        row_losses = torch.empty(tokens, device=device)
+
+    def step():
+        if fused:
+            gpu.head_cross_entropy(spec, x, w, logits, targets, books, scales, loss_sums, logits, bias=bias)
+            host_sums.copy_(loss_sums, non_blocking=True)
+            torch.cuda.current_stream().synchronize()
+            return float(host_sums.sum()) / tokens / books
+        gpu.gemm(spec, x, w, logits, bias=bias)
+        total = 0.0
+        for c in range(books):
+            gpu.cross_entropy(logits, targets, CrossEntropyHead(c * size, size, books, c, 1.0 / (tokens * books)),
+                              row_losses, grad)
+            host_rows.copy_(row_losses, non_blocking=True)
+            torch.cuda.current_stream().synchronize()
+            total += float(host_rows.sum()) / tokens
+        return total / books
+
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize()
+    # The dominant kernels: the head GEMM alone (same output type), timed over the same number of launches.
+    ge0, ge1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    ge0.record(stream)
+    for _ in range(args.steps):
+        gpu.gemm(spec, x, w, logits, bias=bias)
+    ge1.record(stream)
+    torch.cuda.synchronize()
+    gemm_ms = ge0.elapsed_time(ge1) / args.steps
+    clocks = ClockSampler(local_rank)
+    clocks.start()
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    start.record(stream)
+    loss = 0.0
+    for _ in range(args.steps):
+        loss = step()
+    end.record(stream)
+    torch.cuda.synchronize()
+    clock_info = clocks.stop()
+    ms = start.elapsed_time(end) / args.steps
+    if rank != 0:
+        return 0
+    peaks, source = load_peaks()
+    flops = 2.0 * tokens * width * cols
+    ce_ms = max(ms - gemm_ms, 1e-6)
+    logit_bytes = tokens * cols * (2 if fused else 4)
+    ce_bytes = logit_bytes * 2 + tokens * books * 4   # logits read once, gradient written once, targets
+    hbm = float(peaks.get("hbm_gbs", FALLBACK_PEAKS["hbm_gbs"]))
+    line = {
+        "metric": METRIC, "value": flops / (ms / 1e3) / 1e12, "unit": UNIT, "n_gpus": 1, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+        "dtype": "bf16", "data": "synthetic (seeded N(0,1) activations, N(0, 1/768) weights, uniform targets)",
+        "config": {"workload": "cfg3 output layer forward + loss: 65,536 tokens x 768 -> 16 codebooks x 1024, "
+                               "softmax cross-entropy with gradient, loss on the host",
+                   "head_path": args.head_path, "tokens": tokens, "width": width, "codebooks": books,
+                   "codebook_size": size, "l2": "inputs larger than L2 (logits 2.1 GB bf16 / 4.3 GB f32)"},
+        "roofline": {"bound": "hbm", "kernel": "cross_entropy_kernel (step time minus the head GEMM's own time)",
+                     "achieved": ce_bytes / (ce_ms / 1e3) / 1e9, "peak": hbm, "unit": "GB/s",
+                     "frac": ce_bytes / (ce_ms / 1e3) / 1e9 / hbm, "traffic": None,
+                     "algorithmic_bytes_per_step": ce_bytes, "peak_source": f"{source} hbm_gbs",
+                     "head_gemm_ms": gemm_ms, "loss_ms": ce_ms,
+                     "head_gemm_tflops": flops / (gemm_ms / 1e3) / 1e12},
+        "e2e": {"value": flops / (ms / 1e3) / 1e12, "unit": UNIT, "h2d_bytes_per_step": 0,
+                "d2h_bytes_per_step": books * 4 if fused else books * tokens * 4,
+                "note": "the loss reaches the host inside every timed step; operands are resident"},
+        "gpu_launches": (2 if fused else 1 + books) * args.steps, "clocks": clock_info, "loss": loss,
+    }
+    if not args.no_cpu_baseline:
+        line["cpu_baseline"] = head_cpu_baseline(tokens, width, books, size)
+    print(json.dumps(line), flush=True)
+    return 0
+
+
 def run_attention(args, rank: int, world: int, local_rank: int) -> int:
     """one causal attention forward + backward per step (batch 8, 12 heads of 64, sequence 3072).
 
@@ -509,10 +647,13 @@ def main(argv=None) -> int:
     ap.add_argument("--cpu-sample-flops", type=float, default=20e9)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--breakdown", default=None, help="write per-GEMM kernel times of the timed region here (JSON)")
-    ap.add_argument("--workload", choices=["step", "attention"], default="step",
-                    help="step: the cfg3 training-step GEMMs (default); attention: the cfg4 attention layer")
+    ap.add_argument("--workload", choices=["step", "attention", "head"], default="step",
+                    help="step: the cfg3 training-step GEMMs (default); attention: the cfg4 attention layer; "
+                         "head: the cfg3 output layer's forward + cross-entropy")
     ap.add_argument("--attention-path", choices=["fused", "materialised"], default="fused",
                     help="attention workload: fused entry points (default) or the six materialised products")
+    ap.add_argument("--head-path", choices=["fused", "reference-shaped"], default="fused",
+                    help="head workload: snb_head_cross_entropy (default) or the reference's per-codebook sequence")
     args = ap.parse_args(argv)
     if args.warmup < 3:
         ap.error("--warmup must be at least 3")
@@ -538,6 +679,8 @@ def main(argv=None) -> int:
     try:
         if args.workload == "attention":
             return run_attention(args, rank, world, local_rank)
+        if args.workload == "head":
+            return run_head(args, rank, world, local_rank)
         return run_ours(args, shape, rank, world, local_rank)
     finally:
         if world > 1:

@@ -7,13 +7,15 @@
 // One warp per (row, head), 8 warps per block, each warp taking CE_ROWS_PER_WARP rows of one head. When a head's
 // classes are a multiple of 256 (up to 2048) and its rows are 16-byte aligned, each lane keeps its classes/32 logits
 // in registers, so every logit is read once and its gradient written once (the gradient may overwrite the logits in
-// place); otherwise three lane-strided passes over the row, as the reference does. Per-head loss sums are reduced
+// place), with base-2 exponentials (ex2.approx, relative error ~2^-22); otherwise three lane-strided passes over the
+// row with expf/logf, as the reference does. Per-head loss sums are reduced
 // per block and added with one atomic per block, so a whole training step's losses reach the host in one copy.
 #include <cuda_runtime.h>
 
 #include <cmath>
 #include <cstdint>
 #include <string>
+#include <type_traits>
 
 #include "internal.h"
 
@@ -50,6 +52,23 @@ __device__ __forceinline__ uint16_t f32_to_bf16_rne(float f) {
     return static_cast<uint16_t>((u + 0x7FFFu + ((u >> 16) & 1u)) >> 16);
 }
 
+constexpr float kLog2e = 1.4426950408889634f;
+constexpr float kLn2 = 0.6931471805599453f;
+
+// 2^x with subnormal results flushed to zero (one special-function-unit operation; relative error ~2^-22).
+__device__ __forceinline__ float exp2_approx(float x) {
+    float y;
+    asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+    return y;
+}
+
+// Two floats rounded to nearest-even bf16, `lo` in the low half.
+__device__ __forceinline__ uint32_t pack_bf16x2_rn(float lo, float hi) {
+    uint32_t r;
+    asm("cvt.rn.bf16x2.f32 %0, %1, %2;" : "=r"(r) : "f"(hi), "f"(lo));
+    return r;
+}
+
 __device__ __forceinline__ float load_logit(const CeParams& p, uint64_t i) {
     return p.logits_bf16 ? bf16_to_f32(static_cast<const uint16_t*>(p.logits)[i]) : static_cast<const float*>(p.logits)[i];
 }
@@ -71,9 +90,10 @@ __device__ __forceinline__ float warp_sum(float v) {
     return v;
 }
 
-// NV > 0: the register path with NV 8-element vectors per lane (classes == 256 * NV); NV == 0: three passes.
-template <int NV>
-__global__ void __launch_bounds__(CE_WARPS * 32) cross_entropy_kernel(const CeParams p) {
+// NV > 0: the register path with NV 8-element vectors per lane (classes == 256 * NV), logits and gradient of the
+// element types IN_BF16 / OUT_BF16; NV == 0: three passes over the row (types read from the parameters).
+template <int NV, bool IN_BF16, bool OUT_BF16>
+__global__ void __launch_bounds__(CE_WARPS * 32, NV >= 8 ? 2 : 4) cross_entropy_kernel(const CeParams p) {
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const uint32_t head = blockIdx.y;
     const float scale = p.grad_scales ? p.grad_scales[head] : p.grad_scale;
@@ -95,23 +115,26 @@ __global__ void __launch_bounds__(CE_WARPS * 32) cross_entropy_kernel(const CePa
             // The target's logit, read before any gradient may overwrite it in place.
             const float z_target = load_logit(p, base + target);
             if constexpr (NV > 0) {
+                // Base-2 arithmetic: u = z log2(e), so exp(z - m) = 2^(u - m log2(e)) by one ex2.approx each.
                 float v[NV * 8];
 #pragma unroll
                 for (int b = 0; b < NV; ++b) {
                     const uint64_t c0 = base + static_cast<uint64_t>(b * 32 + lane) * 8;
-                    if (p.logits_bf16) {
+                    if constexpr (IN_BF16) {
                         const uint4 w = *reinterpret_cast<const uint4*>(static_cast<const uint16_t*>(p.logits) + c0);
                         const uint32_t ws[4] = {w.x, w.y, w.z, w.w};
 #pragma unroll
                         for (int i = 0; i < 4; ++i) {
-                            v[b * 8 + 2 * i] = __uint_as_float(ws[i] << 16);
-                            v[b * 8 + 2 * i + 1] = __uint_as_float(ws[i] & 0xFFFF0000u);
+                            v[b * 8 + 2 * i] = __uint_as_float(ws[i] << 16) * kLog2e;
+                            v[b * 8 + 2 * i + 1] = __uint_as_float(ws[i] & 0xFFFF0000u) * kLog2e;
                         }
                     } else {
                         const float4* f = reinterpret_cast<const float4*>(static_cast<const float*>(p.logits) + c0);
                         const float4 a = f[0], b4 = f[1];
-                        v[b * 8 + 0] = a.x; v[b * 8 + 1] = a.y; v[b * 8 + 2] = a.z; v[b * 8 + 3] = a.w;
-                        v[b * 8 + 4] = b4.x; v[b * 8 + 5] = b4.y; v[b * 8 + 6] = b4.z; v[b * 8 + 7] = b4.w;
+                        v[b * 8 + 0] = a.x * kLog2e; v[b * 8 + 1] = a.y * kLog2e;
+                        v[b * 8 + 2] = a.z * kLog2e; v[b * 8 + 3] = a.w * kLog2e;
+                        v[b * 8 + 4] = b4.x * kLog2e; v[b * 8 + 5] = b4.y * kLog2e;
+                        v[b * 8 + 6] = b4.z * kLog2e; v[b * 8 + 7] = b4.w * kLog2e;
                     }
                 }
                 float maximum = kNegativeLarge;
@@ -120,23 +143,25 @@ __global__ void __launch_bounds__(CE_WARPS * 32) cross_entropy_kernel(const CePa
                 maximum = warp_max(maximum);
                 float total = 0.0f;
 #pragma unroll
-                for (int i = 0; i < NV * 8; ++i) total += expf(v[i] - maximum);
-                const float log_partition = maximum + logf(warp_sum(total));
-                loss = log_partition - z_target;
+                for (int i = 0; i < NV * 8; ++i) total += exp2_approx(v[i] - maximum);
+                const float log2_partition = maximum + __log2f(warp_sum(total));
+                loss = log2_partition * kLn2 - z_target;
 #pragma unroll
                 for (int b = 0; b < NV; ++b) {
                     const uint32_t first = static_cast<uint32_t>(b * 32 + lane) * 8;   // class of v[b * 8]
                     float g[8];
 #pragma unroll
-                    for (int i = 0; i < 8; ++i)
-                        g[i] = (expf(v[b * 8 + i] - log_partition) - (first + i == target ? 1.0f : 0.0f)) * scale;
+                    for (int i = 0; i < 8; ++i) g[i] = exp2_approx(v[b * 8 + i] - log2_partition) * scale;
+                    if (target - first < 8u) {
+                        // This lane holds the target: subtract the one-hot term there.
+#pragma unroll
+                        for (int i = 0; i < 8; ++i)
+                            if (first + i == target) g[i] -= scale;
+                    }
                     const uint64_t c0 = base + first;
-                    if (p.grad_bf16) {
-                        uint4 w;
-                        w.x = f32_to_bf16_rne(g[0]) | (static_cast<uint32_t>(f32_to_bf16_rne(g[1])) << 16);
-                        w.y = f32_to_bf16_rne(g[2]) | (static_cast<uint32_t>(f32_to_bf16_rne(g[3])) << 16);
-                        w.z = f32_to_bf16_rne(g[4]) | (static_cast<uint32_t>(f32_to_bf16_rne(g[5])) << 16);
-                        w.w = f32_to_bf16_rne(g[6]) | (static_cast<uint32_t>(f32_to_bf16_rne(g[7])) << 16);
+                    if constexpr (OUT_BF16) {
+                        const uint4 w = make_uint4(pack_bf16x2_rn(g[0], g[1]), pack_bf16x2_rn(g[2], g[3]),
+                                                   pack_bf16x2_rn(g[4], g[5]), pack_bf16x2_rn(g[6], g[7]));
                         *reinterpret_cast<uint4*>(static_cast<uint16_t*>(p.grad) + c0) = w;
                     } else {
                         float4* f = reinterpret_cast<float4*>(static_cast<float*>(p.grad) + c0);
@@ -208,6 +233,7 @@ int cross_entropy_launch(cudaStream_t stream, const void* logits, int logits_typ
                          (row_width * in_es) % 16 == 0 && (row_width * out_es) % 16 == 0 &&
                          (column_offset * in_es) % 16 == 0 && (column_offset * out_es) % 16 == 0;
     const int nv = (aligned && classes % 256 == 0 && classes <= 2048) ? static_cast<int>(classes / 256) : 0;
+    // (NV values without an instantiation below fall back to the three-pass path.)
     const uint64_t rows_per_block = static_cast<uint64_t>(CE_WARPS) * CE_ROWS_PER_WARP;
     const uint64_t bx = (rows + rows_per_block - 1) / rows_per_block;
     if (bx > 0x7fffffffull) {
@@ -216,16 +242,26 @@ int cross_entropy_launch(cudaStream_t stream, const void* logits, int logits_typ
     }
     const dim3 grid(static_cast<unsigned>(bx), static_cast<unsigned>(heads));
     const int threads = CE_WARPS * 32;
+    // Register path instantiated for the codebook sizes in use (classes = 256 * NV, NV in {1, 2, 4, 8}); any other
+    // size takes the three-pass path.
+    auto launch = [&](auto nv_c, auto in_c, auto out_c) {
+        cross_entropy_kernel<decltype(nv_c)::value, decltype(in_c)::value, decltype(out_c)::value>
+            <<<grid, threads, 0, stream>>>(p);
+    };
+    auto with_types = [&](auto nv_c) {
+        using T = std::true_type;
+        using F = std::false_type;
+        if (p.logits_bf16 && p.grad_bf16) launch(nv_c, T{}, T{});
+        else if (p.logits_bf16) launch(nv_c, T{}, F{});
+        else if (p.grad_bf16) launch(nv_c, F{}, T{});
+        else launch(nv_c, F{}, F{});
+    };
     switch (nv) {
-        case 1: cross_entropy_kernel<1><<<grid, threads, 0, stream>>>(p); break;
-        case 2: cross_entropy_kernel<2><<<grid, threads, 0, stream>>>(p); break;
-        case 3: cross_entropy_kernel<3><<<grid, threads, 0, stream>>>(p); break;
-        case 4: cross_entropy_kernel<4><<<grid, threads, 0, stream>>>(p); break;
-        case 5: cross_entropy_kernel<5><<<grid, threads, 0, stream>>>(p); break;
-        case 6: cross_entropy_kernel<6><<<grid, threads, 0, stream>>>(p); break;
-        case 7: cross_entropy_kernel<7><<<grid, threads, 0, stream>>>(p); break;
-        case 8: cross_entropy_kernel<8><<<grid, threads, 0, stream>>>(p); break;
-        default: cross_entropy_kernel<0><<<grid, threads, 0, stream>>>(p); break;
+        case 1: with_types(std::integral_constant<int, 1>{}); break;
+        case 2: with_types(std::integral_constant<int, 2>{}); break;
+        case 4: with_types(std::integral_constant<int, 4>{}); break;
+        case 8: with_types(std::integral_constant<int, 8>{}); break;
+        default: launch(std::integral_constant<int, 0>{}, std::false_type{}, std::false_type{}); break;
     }
     const cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess) {
