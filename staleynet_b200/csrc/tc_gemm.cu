@@ -167,16 +167,22 @@ int launch_pair(cudaStream_t stream, const CUtensorMap* m, const TcParams& p, in
     return SNB_OK;
 }
 
-// K splits for a problem of `tiles` output tiles and `kb` K slices on `sms` SMs: minimises the critical path
-// ceil(tiles*s/sms) * ceil(kb/s) (waves times slices per unit), keeping at least 4 K slices per split.
-int choose_splits(int64_t tiles, int64_t kb, int sms) {
+// K splits for a problem of `tiles` output tiles and `kb` K slices on `workers` SMs (or SM pairs): minimises the
+// critical path ceil(tiles*s/workers) * ceil(kb/s) (waves times slices per unit, in slice times of one worker),
+// keeping at least 4 K slices per split, plus what a split costs in output traffic at HBM speed in the same units:
+// every partial beyond the first is one more reduce-add into C, and an overwritten C is zeroed first.
+int choose_splits(int64_t tiles, int64_t kb, int workers, double slice_flops, double worker_flops, double out_bytes,
+                  bool overwrite) {
     if (kb < 8) return 1;
+    constexpr double kHbmBytesPerSecond = 6.5e12;
+    const double slices_per_byte = worker_flops / (kHbmBytesPerSecond * slice_flops);
     int best = 1;
-    int64_t best_cost = ((tiles + sms - 1) / sms) * kb;
+    double best_cost = static_cast<double>((tiles + workers - 1) / workers) * static_cast<double>(kb);
     for (int s = 2; s <= 32; ++s) {
         const int64_t per = (kb + s - 1) / s;
         if (per < 4) break;
-        const int64_t cost = ((tiles * s + sms - 1) / sms) * per;
+        const double extra = slices_per_byte * out_bytes * static_cast<double>((s - 1) + (overwrite ? 1 : 0));
+        const double cost = static_cast<double>((tiles * s + workers - 1) / workers) * static_cast<double>(per) + extra;
         if (cost < best_cost) {
             best_cost = cost;
             best = s;
@@ -249,7 +255,14 @@ int tc_gemm_try(cudaStream_t stream, const GemmRequest& r, bool* launched, int* 
     if (tiles > (1ll << 30)) return SNB_OK;
     const bool plain_epilogue =
         !out_bf16 && r.activation == SNB_ACTIVATION_NONE && r.pre == nullptr && r.causal == SNB_CAUSAL_NONE;
-    const int splits = plain_epilogue ? choose_splits(tiles, k_blocks, workers) : 1;
+    // Tensor rate of one worker (one SM, or an SM pair) and the FLOPs of one K slice of one tile.
+    const double sm_flops = (bf16_in ? 8192.0 : 4096.0) * 1.8e9;
+    const double slice_flops = 2.0 * bm * bn * bk;
+    const double out_bytes = static_cast<double>(r.count) * static_cast<double>(p.rows) * static_cast<double>(p.cols) *
+                             static_cast<double>(csize);
+    const int splits = plain_epilogue ? choose_splits(tiles, k_blocks, workers, slice_flops,
+                                                      pair ? 2.0 * sm_flops : sm_flops, out_bytes, p.accumulate == 0)
+                                      : 1;
     const int64_t kb_per_split = (k_blocks + splits - 1) / splits;
     const int64_t splits_used = (k_blocks + kb_per_split - 1) / kb_per_split;  // every split has >= 1 slice
 
