@@ -166,6 +166,10 @@ typedef struct snb_gemm_args {
     int32_t causal;             /* SNB_CAUSAL_*: structure of a batched attention product (work it may skip) */
     int32_t reserved;
     int64_t causal_offset;      /* query q sees keys 0..=q+causal_offset (the softmax's query_offset) */
+    const float* row_scale;     /* [rows] multiplier of each output row before the bias (count 1 only), or NULL:
+                                 * with the RMSNorm gain folded into the right operand (snb_scale_rows) and
+                                 * row_scale = the rows' 1/rms (snb_rms_norm_stats), left * right = rms_norm(left)
+                                 * times the unscaled right operand, without a normalised copy of left. */
 } snb_gemm_args;
 
 SNB_API int snb_gemm(void* stream, const snb_gemm_args* args);
@@ -277,6 +281,68 @@ SNB_API int snb_cross_entropy(void* stream, const float* logits, uint64_t rows, 
 SNB_API int snb_head_cross_entropy(void* stream, const snb_gemm_args* head, const uint32_t* targets,
                                    uint64_t targets_len, uint64_t codebooks, uint64_t codebook_size,
                                    const float* grad_scales, float* loss_sums, void* logits_grad, int32_t grad_type);
+
+/* ---------------------------------------------------------------------------------------------- RMSNorm, AdamW */
+
+/* RMSNorm forward (`Gpu::rms_norm_forward`, ops/normalization.rs; kernel kernels/normalization.rs:27-51): for each
+ * row of input [rows, cols] (f32), inv_rms[row] = 1/sqrt(mean(x^2) + epsilon) and output = x * inv_rms * gain.
+ * The reference's checks as status codes: "gain length" (gain_len != cols), "inv_rms too small". */
+SNB_API int snb_rms_norm_forward(void* stream, const float* input, uint64_t rows, uint64_t cols, const float* gain,
+                                 uint64_t gain_len, float* output, float* inv_rms, uint64_t inv_rms_len, float epsilon);
+
+/* RMSNorm backward (`Gpu::rms_norm_backward`; kernels/normalization.rs:53-127): input_grad = s g dy - x s^3 / cols *
+ * sum(dy g x) per row, and gain_grad[c] += sum over rows of dy x s ("gain_grad length" if gain_grad_len != cols). */
+SNB_API int snb_rms_norm_backward(void* stream, const float* output_grad, const float* input, const float* gain,
+                                  const float* inv_rms, float* input_grad, float* gain_grad, uint64_t gain_grad_len,
+                                  uint64_t rows, uint64_t cols);
+
+/* The RMSNorm statistics of the fused prologue: inv_rms[row] of input [rows, cols] (input_type f32 or bf16) and,
+ * when output is not NULL, the normalised rows x * inv_rms * gain as output_type. With output NULL, the GEMM
+ * left * (gain-scaled right, snb_scale_rows) with row_scale = inv_rms computes rms_norm(left) * right without the
+ * normalised tensor. No reference counterpart. */
+SNB_API int snb_rms_norm_stats(void* stream, const void* input, int32_t input_type, uint64_t rows, uint64_t cols,
+                               float epsilon, float* inv_rms, const float* gain, void* output, int32_t output_type);
+
+/* output[k, :] = scale[k] * input[k, :] for row-major [rows, cols] (types f32 or bf16; may be in place when the
+ * types match): folds an RMSNorm gain into the weight matrix that follows it. No reference counterpart. */
+SNB_API int snb_scale_rows(void* stream, const float* scale, const void* input, int32_t input_type, void* output,
+                           int32_t output_type, uint64_t rows, uint64_t cols);
+
+/* AdamWHyperparameters (ops/optimizer.rs:9-28). */
+typedef struct snb_adamw_hyper {
+    float learning_rate;
+    float beta1;
+    float beta2;
+    float epsilon;
+    float weight_decay; /* snb_adamw_step only; snb_adamw_step_multi takes it per tensor */
+    uint32_t step;      /* 1-based, for the bias corrections 1 - beta^step */
+} snb_adamw_hyper;
+
+/* One parameter tensor of snb_adamw_step_multi (48 bytes). */
+typedef struct snb_adamw_tensor {
+    float* parameter;
+    const float* gradient;
+    float* first_moment;
+    float* second_moment;
+    uint64_t count;
+    float weight_decay; /* 0 for gains, biases and embeddings (the reference's Decay::Exempt) */
+    uint32_t reserved;
+} snb_adamw_tensor;
+
+/* One AdamW step of one tensor (`Gpu::adamw_step`, ops/optimizer.rs:32-66; kernel kernels/optimizer.rs:47-71). */
+SNB_API int snb_adamw_step(void* stream, float* parameter, const float* gradient, float* first_moment,
+                           float* second_moment, uint64_t count, const snb_adamw_hyper* hyper);
+
+/* *result (device, one double) = sum of values[i]^2 (`Gpu::sum_of_squares`, ops/optimizer.rs:68-85, which reduces
+ * the block sums on the host instead). */
+SNB_API int snb_sum_of_squares(void* stream, const float* values, uint64_t count, double* result);
+
+/* The optimizer step of `AdamW::step` (model optimizer.rs:125-177) over up to 256 tensors in two launches and no
+ * host round trip: *gradient_square_sum (device double) = the sum of every gradient's squares; the clip factor
+ * max_gradient_norm / norm (when the norm exceeds it) and the AdamW update of every tensor follow on the device.
+ * Unlike the reference, the gradients themselves are left unscaled. No reference counterpart as one call. */
+SNB_API int snb_adamw_step_multi(void* stream, const snb_adamw_tensor* tensors, uint64_t tensor_count,
+                                 const snb_adamw_hyper* hyper, float max_gradient_norm, double* gradient_square_sum);
 
 /* Failure-detection self-test: launches a one-thread kernel that waits on an mbarrier nothing completes, through
  * the bounded wait every tensor-core pipeline wait uses. The wait gives up after limit_ns (at most 1 s), records a

@@ -88,6 +88,12 @@ def lib() -> ctypes.CDLL:
             L.snb_oracle_softmax_backward.argtypes = [fp, fp, c_uint64, c_uint64]
             L.snb_oracle_cross_entropy.argtypes = [fp, POINTER(c_uint32), c_uint64, c_uint64, c_uint64, c_uint64,
                                                    c_uint64, c_uint64, c_float, fp, fp]
+            L.snb_oracle_rms_norm_forward.argtypes = [fp, fp, c_uint64, c_uint64, c_float, fp, fp]
+            L.snb_oracle_rms_norm_backward.argtypes = [fp, fp, fp, fp, c_uint64, c_uint64, fp, fp]
+            L.snb_oracle_adamw_step.argtypes = [fp, fp, fp, fp, c_uint64, c_float, c_float, c_float, c_float, c_float,
+                                                c_uint32]
+            L.snb_oracle_sum_of_squares.argtypes = [fp, c_uint64]
+            L.snb_oracle_sum_of_squares.restype = c_double
             L.snb_oracle_max_threads.restype = c_int
             _lib = L
     return _lib
@@ -211,6 +217,37 @@ def cross_entropy(logits: np.ndarray, targets: np.ndarray, cols: int, column_off
     rows = losses.size
     lib().snb_oracle_cross_entropy(_f(logits), targets.ctypes.data_as(POINTER(c_uint32)), rows, cols, column_offset,
                                    classes, target_stride, target_offset, grad_scale, _f(losses), _f(logits_grad))
+
+
+def rms_norm_forward(x: np.ndarray, gain: np.ndarray, cols: int, epsilon: float):
+    """reference::rms_norm_forward (reference.rs:60-77): returns (output, inv_rms)."""
+    x = np.ascontiguousarray(x, dtype=np.float32)
+    gain = np.ascontiguousarray(gain, dtype=np.float32)
+    rows = x.size // cols
+    out = np.empty_like(x)
+    inv = np.empty(rows, np.float32)
+    lib().snb_oracle_rms_norm_forward(_f(x), _f(gain), rows, cols, epsilon, _f(out), _f(inv))
+    return out, inv
+
+
+def rms_norm_backward(dy: np.ndarray, x: np.ndarray, gain: np.ndarray, inv_rms: np.ndarray, cols: int):
+    """reference::rms_norm_backward (reference.rs:79-98): returns (input_grad, gain_grad)."""
+    dy, x = (np.ascontiguousarray(a, dtype=np.float32) for a in (dy, x))
+    gain, inv_rms = (np.ascontiguousarray(a, dtype=np.float32) for a in (gain, inv_rms))
+    dx = np.empty_like(x)
+    dg = np.zeros(cols, np.float32)
+    lib().snb_oracle_rms_norm_backward(_f(dy), _f(x), _f(gain), _f(inv_rms), x.size // cols, cols, _f(dx), _f(dg))
+    return dx, dg
+
+
+def adamw_step(parameter, gradient, first, second, learning_rate, beta1, beta2, epsilon, weight_decay, step) -> None:
+    """The reference's AdamW update (kernels/optimizer.rs:47-71), in place on parameter and the moments."""
+    lib().snb_oracle_adamw_step(_f(parameter), _f(np.ascontiguousarray(gradient, dtype=np.float32)), _f(first),
+                                _f(second), parameter.size, learning_rate, beta1, beta2, epsilon, weight_decay, step)
+
+
+def sum_of_squares(values: np.ndarray) -> float:
+    return lib().snb_oracle_sum_of_squares(_f(np.ascontiguousarray(values, dtype=np.float32)), values.size)
 
 
 def max_threads() -> int:

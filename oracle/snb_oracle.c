@@ -272,6 +272,71 @@ void snb_oracle_cross_entropy(const float* logits, const uint32_t* targets, uint
     }
 }
 
+/* reference::rms_norm_forward (reference.rs:60-77): per row s = 1 / sqrt(mean(x^2) + epsilon), y = x * s * g. */
+void snb_oracle_rms_norm_forward(const float* input, const float* gain, uint64_t rows, uint64_t cols, float epsilon,
+                                 float* output, float* inv_rms) {
+    for (uint64_t row = 0; row < rows; ++row) {
+        const float* x = input + row * cols;
+        float square_sum = 0.0f;
+        for (uint64_t c = 0; c < cols; ++c) square_sum += x[c] * x[c];
+        const float inverse = 1.0f / sqrtf(square_sum / (float)cols + epsilon);
+        for (uint64_t c = 0; c < cols; ++c) output[row * cols + c] = x[c] * inverse * gain[c];
+        inv_rms[row] = inverse;
+    }
+}
+
+/* reference::rms_norm_backward (reference.rs:79-98): dx = s g dy - x s^3 / cols * sum(dy g x); gain_grad += dy x s
+ * (added to, as the GPU kernel accumulates). */
+void snb_oracle_rms_norm_backward(const float* output_grad, const float* input, const float* gain,
+                                  const float* inv_rms, uint64_t rows, uint64_t cols, float* input_grad,
+                                  float* gain_grad) {
+    for (uint64_t row = 0; row < rows; ++row) {
+        const float* dy = output_grad + row * cols;
+        const float* x = input + row * cols;
+        const float inverse = inv_rms[row];
+        float projection = 0.0f;
+        for (uint64_t c = 0; c < cols; ++c) projection += dy[c] * gain[c] * x[c];
+        const float correction = inverse * inverse * inverse * projection / (float)cols;
+        for (uint64_t c = 0; c < cols; ++c) {
+            input_grad[row * cols + c] = inverse * gain[c] * dy[c] - x[c] * correction;
+            gain_grad[c] += dy[c] * x[c] * inverse;
+        }
+    }
+}
+
+/* The AdamW update of the reference's kernel (kernels/optimizer.rs:47-71) and its parity test
+ * (tests/kernels_match_reference.rs:299-327), with first_correction = 1 - beta1^step and
+ * second_correction = 1 - beta2^step as ops/optimizer.rs:44-54 computes them. */
+void snb_oracle_adamw_step(float* parameter, const float* gradient, float* first_moment, float* second_moment,
+                           uint64_t count, float learning_rate, float beta1, float beta2, float epsilon,
+                           float weight_decay, uint32_t step) {
+    float b1 = 1.0f, b2 = 1.0f;
+    for (uint32_t i = 0; i < step; ++i) {
+        b1 *= beta1;
+        b2 *= beta2;
+    }
+    const float first_correction = 1.0f - b1, second_correction = 1.0f - b2;
+    for (uint64_t i = 0; i < count; ++i) {
+        const float grad = gradient[i];
+        const float mean = beta1 * first_moment[i] + (1.0f - beta1) * grad;
+        const float variance = beta2 * second_moment[i] + (1.0f - beta2) * grad * grad;
+        first_moment[i] = mean;
+        second_moment[i] = variance;
+        const float mean_hat = mean / first_correction;
+        const float variance_hat = variance / second_correction;
+        const float weight = parameter[i];
+        const float update = mean_hat / (sqrtf(variance_hat) + epsilon) + weight_decay * weight;
+        parameter[i] = weight - learning_rate * update;
+    }
+}
+
+/* sum of squares in f64 (the reference sums its f32 partial sums as f64, ops/optimizer.rs:72-85). */
+double snb_oracle_sum_of_squares(const float* values, uint64_t count) {
+    double sum = 0.0;
+    for (uint64_t i = 0; i < count; ++i) sum += (double)values[i] * (double)values[i];
+    return sum;
+}
+
 int snb_oracle_max_threads(void) {
 #ifdef _OPENMP
     return omp_get_max_threads();

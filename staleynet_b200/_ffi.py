@@ -61,6 +61,13 @@ EXPORTED_SYMBOLS = (
     "snb_causal_attention_backward_noalloc",
     "snb_cross_entropy",
     "snb_head_cross_entropy",
+    "snb_rms_norm_forward",
+    "snb_rms_norm_backward",
+    "snb_rms_norm_stats",
+    "snb_scale_rows",
+    "snb_adamw_step",
+    "snb_sum_of_squares",
+    "snb_adamw_step_multi",
     "snb_selftest_bounded_wait",
     "snb_abi_version",
 )
@@ -89,6 +96,18 @@ class CrossEntropyHead(ctypes.Structure):
                 ("target_offset", c_uint64), ("grad_scale", c_float), ("reserved", c_uint32)]
 
 
+class AdamWHyper(ctypes.Structure):
+    """snb_adamw_hyper: the reference's AdamWHyperparameters (ops/optimizer.rs:9-28)."""
+    _fields_ = [("learning_rate", c_float), ("beta1", c_float), ("beta2", c_float), ("epsilon", c_float),
+                ("weight_decay", c_float), ("step", c_uint32)]
+
+
+class AdamWTensor(ctypes.Structure):
+    """snb_adamw_tensor."""
+    _fields_ = [("parameter", c_void_p), ("gradient", c_void_p), ("first_moment", c_void_p),
+                ("second_moment", c_void_p), ("count", c_uint64), ("weight_decay", c_float), ("reserved", c_uint32)]
+
+
 class GemmArgs(ctypes.Structure):
     _fields_ = [
         ("product", Product),
@@ -112,6 +131,7 @@ class GemmArgs(ctypes.Structure):
         ("causal", c_int32),
         ("reserved", c_int32),
         ("causal_offset", ctypes.c_int64),
+        ("row_scale", c_void_p),
     ]
 
 
@@ -173,6 +193,21 @@ def load() -> ctypes.CDLL:
         lib.snb_head_cross_entropy.argtypes = [c_void_p, POINTER(GemmArgs), c_void_p, c_uint64, c_uint64, c_uint64,
                                                c_void_p, c_void_p, c_void_p, c_int32]
         lib.snb_head_cross_entropy.restype = c_int
+        lib.snb_rms_norm_forward.argtypes = [c_void_p, c_void_p, c_uint64, c_uint64, c_void_p, c_uint64, c_void_p,
+                                             c_void_p, c_uint64, c_float]
+        lib.snb_rms_norm_backward.argtypes = [c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p,
+                                              c_uint64, c_uint64, c_uint64]
+        lib.snb_rms_norm_stats.argtypes = [c_void_p, c_void_p, c_int32, c_uint64, c_uint64, c_float, c_void_p,
+                                           c_void_p, c_void_p, c_int32]
+        lib.snb_scale_rows.argtypes = [c_void_p, c_void_p, c_void_p, c_int32, c_void_p, c_int32, c_uint64, c_uint64]
+        lib.snb_adamw_step.argtypes = [c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_uint64,
+                                       POINTER(AdamWHyper)]
+        lib.snb_sum_of_squares.argtypes = [c_void_p, c_void_p, c_uint64, c_void_p]
+        lib.snb_adamw_step_multi.argtypes = [c_void_p, POINTER(AdamWTensor), c_uint64, POINTER(AdamWHyper), c_float,
+                                             c_void_p]
+        for name in ("snb_rms_norm_forward", "snb_rms_norm_backward", "snb_rms_norm_stats", "snb_scale_rows",
+                     "snb_adamw_step", "snb_sum_of_squares", "snb_adamw_step_multi"):
+            getattr(lib, name).restype = c_int
         lib.snb_selftest_bounded_wait.argtypes = [c_void_p, c_uint64]
         lib.snb_selftest_bounded_wait.restype = c_int
         lib.snb_abi_version.argtypes = []

@@ -110,7 +110,7 @@ using namespace snb;
 
 extern "C" {
 
-int snb_abi_version(void) { return 100; }
+int snb_abi_version(void) { return 101; }
 
 const char* snb_last_error(void) { return t_last_error.c_str(); }
 
@@ -168,6 +168,8 @@ int snb_gemm(void* stream, const snb_gemm_args* a) {
         return fail(SNB_ERR_INVALID_ARGUMENT, "gemm: unknown activation");
     if (a->causal < SNB_CAUSAL_NONE || a->causal > SNB_CAUSAL_LEFT_T_MASKED || a->causal_offset < 0)
         return fail(SNB_ERR_INVALID_ARGUMENT, "gemm: unknown causal mode or negative offset");
+    if (a->row_scale != nullptr && a->count != 1)
+        return fail(SNB_ERR_INVALID_ARGUMENT, "gemm: row_scale needs count 1");
     GemmRequest r{};
     r.p = a->product;
     r.count = a->count;
@@ -186,6 +188,7 @@ int snb_gemm(void* stream, const snb_gemm_args* a) {
     r.residual = a->residual;
     r.causal = a->causal;
     r.causal_offset = a->causal_offset;
+    r.row_scale = a->row_scale;
     return run(static_cast<cudaStream_t>(stream), r, a->left_len, a->right_len, a->output_len);
 }
 
@@ -344,6 +347,117 @@ int snb_head_cross_entropy(void* stream, const snb_gemm_args* head, const uint32
                               codebook_size, 0, grad_scales, 0.0f, nullptr, loss_sums, logits_grad, grad_type, &err);
     if (rc != SNB_OK) return fail(rc, err);
     t_last_path = gemm_path;
+    return SNB_OK;
+}
+
+int snb_rms_norm_forward(void* stream, const float* input, uint64_t rows, uint64_t cols, const float* gain,
+                         uint64_t gain_len, float* output, float* inv_rms, uint64_t inv_rms_len, float epsilon) {
+    t_last_path = SNB_PATH_NONE;
+    // The reference's checks (ops/normalization.rs), in its order and words.
+    if (gain_len != cols) return fail(SNB_ERR_INVALID_ARGUMENT, "rms_norm_forward: gain length");
+    if (inv_rms_len < rows) return fail(SNB_ERR_INVALID_ARGUMENT, "rms_norm_forward: inv_rms too small");
+    if (rows > 0 && (input == nullptr || gain == nullptr || output == nullptr || inv_rms == nullptr))
+        return fail(SNB_ERR_INVALID_ARGUMENT, "rms_norm_forward: null pointer");
+    std::string err;
+    int rc = rms_norm_forward_launch(static_cast<cudaStream_t>(stream), input, SNB_TYPE_F32, gain, output,
+                                     SNB_TYPE_F32, inv_rms, rows, cols, epsilon, &err);
+    if (rc != SNB_OK) return fail(rc, err);
+    t_last_path = SNB_PATH_SIMT;
+    return SNB_OK;
+}
+
+int snb_rms_norm_backward(void* stream, const float* output_grad, const float* input, const float* gain,
+                          const float* inv_rms, float* input_grad, float* gain_grad, uint64_t gain_grad_len,
+                          uint64_t rows, uint64_t cols) {
+    t_last_path = SNB_PATH_NONE;
+    if (gain_grad_len != cols) return fail(SNB_ERR_INVALID_ARGUMENT, "rms_norm_backward: gain_grad length");
+    if (rows > 0 && (output_grad == nullptr || input == nullptr || gain == nullptr || inv_rms == nullptr ||
+                     input_grad == nullptr || gain_grad == nullptr))
+        return fail(SNB_ERR_INVALID_ARGUMENT, "rms_norm_backward: null pointer");
+    std::string err;
+    int rc = rms_norm_backward_launch(static_cast<cudaStream_t>(stream), output_grad, input, gain, inv_rms,
+                                      input_grad, gain_grad, rows, cols, &err);
+    if (rc != SNB_OK) return fail(rc, err);
+    t_last_path = SNB_PATH_SIMT;
+    return SNB_OK;
+}
+
+int snb_rms_norm_stats(void* stream, const void* input, int32_t input_type, uint64_t rows, uint64_t cols,
+                       float epsilon, float* inv_rms, const float* gain, void* output, int32_t output_type) {
+    t_last_path = SNB_PATH_NONE;
+    const bool types_ok = (input_type == SNB_TYPE_F32 || input_type == SNB_TYPE_BF16) &&
+                          (output == nullptr || output_type == SNB_TYPE_F32 || output_type == SNB_TYPE_BF16);
+    if (!types_ok) return fail(SNB_ERR_INVALID_ARGUMENT, "rms_norm_stats: unknown element type");
+    if (rows > 0 && (input == nullptr || inv_rms == nullptr || (output != nullptr && gain == nullptr)))
+        return fail(SNB_ERR_INVALID_ARGUMENT, "rms_norm_stats: null pointer");
+    std::string err;
+    int rc = rms_norm_forward_launch(static_cast<cudaStream_t>(stream), input, input_type, gain, output, output_type,
+                                     inv_rms, rows, cols, epsilon, &err);
+    if (rc != SNB_OK) return fail(rc, err);
+    t_last_path = SNB_PATH_SIMT;
+    return SNB_OK;
+}
+
+int snb_scale_rows(void* stream, const float* scale, const void* input, int32_t input_type, void* output,
+                   int32_t output_type, uint64_t rows, uint64_t cols) {
+    t_last_path = SNB_PATH_NONE;
+    const bool types_ok = (input_type == SNB_TYPE_F32 || input_type == SNB_TYPE_BF16) &&
+                          (output_type == SNB_TYPE_F32 || output_type == SNB_TYPE_BF16);
+    if (!types_ok) return fail(SNB_ERR_INVALID_ARGUMENT, "scale_rows: unknown element type");
+    if (input == output && input_type != output_type)
+        return fail(SNB_ERR_INVALID_ARGUMENT, "scale_rows: in place needs one element type");
+    if (rows > 0 && cols > 0 && (scale == nullptr || input == nullptr || output == nullptr))
+        return fail(SNB_ERR_INVALID_ARGUMENT, "scale_rows: null pointer");
+    std::string err;
+    int rc = scale_rows_launch(static_cast<cudaStream_t>(stream), scale, input, input_type, output, output_type, rows,
+                               cols, &err);
+    if (rc != SNB_OK) return fail(rc, err);
+    t_last_path = SNB_PATH_SIMT;
+    return SNB_OK;
+}
+
+int snb_adamw_step(void* stream, float* parameter, const float* gradient, float* first_moment, float* second_moment,
+                   uint64_t count, const snb_adamw_hyper* hyper) {
+    t_last_path = SNB_PATH_NONE;
+    if (hyper == nullptr) return fail(SNB_ERR_INVALID_ARGUMENT, "adamw_step: hyper is null");
+    if (count > 0 && (parameter == nullptr || gradient == nullptr || first_moment == nullptr || second_moment == nullptr))
+        return fail(SNB_ERR_INVALID_ARGUMENT, "adamw_step: null pointer");
+    std::string err;
+    int rc = adamw_launch(static_cast<cudaStream_t>(stream), parameter, gradient, first_moment, second_moment, count,
+                          *hyper, &err);
+    if (rc != SNB_OK) return fail(rc, err);
+    t_last_path = SNB_PATH_SIMT;
+    return SNB_OK;
+}
+
+int snb_sum_of_squares(void* stream, const float* values, uint64_t count, double* result) {
+    t_last_path = SNB_PATH_NONE;
+    if (result == nullptr || (count > 0 && values == nullptr))
+        return fail(SNB_ERR_INVALID_ARGUMENT, "sum_of_squares: null pointer");
+    std::string err;
+    int rc = sum_of_squares_launch(static_cast<cudaStream_t>(stream), values, count, result, &err);
+    if (rc != SNB_OK) return fail(rc, err);
+    t_last_path = SNB_PATH_SIMT;
+    return SNB_OK;
+}
+
+int snb_adamw_step_multi(void* stream, const snb_adamw_tensor* tensors, uint64_t tensor_count,
+                         const snb_adamw_hyper* hyper, float max_gradient_norm, double* gradient_square_sum) {
+    t_last_path = SNB_PATH_NONE;
+    if (hyper == nullptr || gradient_square_sum == nullptr || (tensor_count > 0 && tensors == nullptr))
+        return fail(SNB_ERR_INVALID_ARGUMENT, "adamw_step_multi: null pointer");
+    for (uint64_t i = 0; i < tensor_count; ++i) {
+        const snb_adamw_tensor& t = tensors[i];
+        if (t.count > 0 && (t.parameter == nullptr || t.gradient == nullptr || t.first_moment == nullptr ||
+                            t.second_moment == nullptr))
+            return fail(SNB_ERR_INVALID_ARGUMENT, "adamw_step_multi: null pointer in tensor " + std::to_string(i));
+    }
+    if (!(max_gradient_norm > 0.0f)) return fail(SNB_ERR_INVALID_ARGUMENT, "adamw_step_multi: max_gradient_norm <= 0");
+    std::string err;
+    int rc = adamw_multi_launch(static_cast<cudaStream_t>(stream), tensors, tensor_count, *hyper, max_gradient_norm,
+                                gradient_square_sum, &err);
+    if (rc != SNB_OK) return fail(rc, err);
+    t_last_path = SNB_PATH_SIMT;
     return SNB_OK;
 }
 

@@ -64,6 +64,7 @@ struct TcParams {
     int64_t out_batch_stride; // elements between output matrices (for residual / gelu_input addressing)
     int32_t causal;           // SNB_CAUSAL_* work-skipping hint of a batched attention product
     int64_t causal_offset;    // query q sees keys 0..=q+causal_offset
+    const float* row_scale;   // [M] output-row multipliers (one matrix), or nullptr
 };
 
 // NBOX = staging boxes per epilogue warp: 2 lets a chunk be staged while the previous chunk's TMA store still reads
@@ -246,7 +247,7 @@ __device__ __forceinline__ void stage_half(uint8_t* box, int lane, int h, const 
 }
 
 // The epilogue function for 32 columns [col, col + 32) of one output row, starting from the TMEM accumulator:
-//   x = scale * acc + bias;  (x staged into pre_box when given);  pre_only: return x;
+//   x = scale * row_scale[row] * acc + bias;  (x staged into pre_box when given);  pre_only: return x;
 //   y = activation(x) (+ residual).
 // The first auxiliary input (GELU input, else residual) is requested before waiting for TMEM so the two latencies
 // overlap; only when both are present is the residual read afterwards.
@@ -267,9 +268,10 @@ __device__ __forceinline__ void epilogue_half(const TcParams& p, uint32_t taddr,
 
 #pragma unroll
     for (int j = 0; j < 16; ++j) v[j] = make_float2(__uint_as_float(x[2 * j]), __uint_as_float(x[2 * j + 1]));
-    if (p.scale != 1.0f) {
+    const float s = p.row_scale != nullptr ? p.scale * (row_live ? __ldg(p.row_scale + row) : 0.0f) : p.scale;
+    if (s != 1.0f) {
 #pragma unroll
-        for (int j = 0; j < 16; ++j) v[j] = __fmul2_rn(f2(p.scale), v[j]);
+        for (int j = 0; j < 16; ++j) v[j] = __fmul2_rn(f2(s), v[j]);
     }
     if (p.bias != nullptr && first_split) {
         const float4* b4 = reinterpret_cast<const float4*>(p.bias + col);

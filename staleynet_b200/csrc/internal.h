@@ -26,6 +26,7 @@ struct GemmRequest {
     const void* residual;
     int causal;
     int64_t causal_offset;
+    const float* row_scale;   // [rows] output-row multipliers (count 1), or nullptr
 };
 
 struct DeviceInfo {
@@ -65,6 +66,20 @@ int cross_entropy_launch(cudaStream_t stream, const void* logits, int logits_typ
                          const uint32_t* targets, uint64_t target_stride, uint64_t heads, uint64_t column_offset,
                          uint64_t classes, uint64_t target_offset, const float* grad_scales, float grad_scale,
                          float* row_losses, float* loss_sums, void* grad, int grad_type, std::string* err);
+
+// RMSNorm and optimizer launches (norm_optim.cu).
+int rms_norm_forward_launch(cudaStream_t s, const void* input, int input_type, const float* gain, void* output,
+                            int output_type, float* inv_rms, uint64_t rows, uint64_t cols, float epsilon,
+                            std::string* err);
+int rms_norm_backward_launch(cudaStream_t s, const float* dy, const float* x, const float* gain, const float* inv_rms,
+                             float* dx, float* gain_grad, uint64_t rows, uint64_t cols, std::string* err);
+int scale_rows_launch(cudaStream_t s, const float* scale, const void* in, int in_type, void* out, int out_type,
+                      uint64_t rows, uint64_t cols, std::string* err);
+int adamw_launch(cudaStream_t s, float* parameter, const float* gradient, float* first, float* second, uint64_t count,
+                 const snb_adamw_hyper& h, std::string* err);
+int sum_of_squares_launch(cudaStream_t s, const float* values, uint64_t count, double* total, std::string* err);
+int adamw_multi_launch(cudaStream_t s, const snb_adamw_tensor* tensors, uint64_t n, const snb_adamw_hyper& h,
+                       float max_gradient_norm, double* square_sum, std::string* err);
 
 // Fused causal attention backward (attention_fused_bwd.cuh): dq [count, queries, 64], dk and dv [count, keys, 64],
 // all f32 and overwritten, from bf16 q, k, v, d_out, the forward's output (f32 or bf16) and its log-sum-exp. The

@@ -35,6 +35,7 @@ struct SimtParams {
     void* pre;
     const void* gelu_input;
     const void* residual;
+    const float* row_scale;   // [M] output-row multipliers (one matrix), or nullptr
 };
 
 __device__ __forceinline__ float load_any(const void* base, int64_t index, int is_bf16) {
@@ -117,7 +118,7 @@ __global__ void __launch_bounds__(ST_THREADS) simt_gemm_kernel(const void* __res
                 const int64_t col = n0 + tx + 16 * j;
                 if (row < p.M && col < p.N) {
                     const int64_t idx = b * p.c_bs + row * p.N + col;
-                    float x = p.scale * acc[i][j];
+                    float x = (p.row_scale ? p.scale * p.row_scale[row] : p.scale) * acc[i][j];
                     if (p.bias) x += p.bias[col];
                     if (p.pre) store_any(p.pre, idx, x, p.c_bf16);
                     if (p.activation == SNB_ACTIVATION_GELU) x = gelu_f(x);
@@ -313,6 +314,7 @@ int simt_gemm(cudaStream_t stream, const GemmRequest& r, std::string* err) {
     p.pre = r.pre;
     p.gelu_input = r.gelu_input;
     p.residual = r.residual;
+    p.row_scale = r.row_scale;
     const int64_t gx = (p.N + ST_TILE - 1) / ST_TILE;
     const int64_t gy = (p.M + ST_TILE - 1) / ST_TILE;
     if (gx > 0x7fffffff || gy > 65535) {

@@ -366,6 +366,7 @@ int tc_gemm_try(cudaStream_t stream, const GemmRequest& r, bool* launched, int* 
     kp.aux_bf16 = r.aux_type == SNB_TYPE_BF16;
     kp.has_pre = r.pre != nullptr;
     kp.bias = r.bias;
+    kp.row_scale = r.row_scale;
     kp.residual = r.residual;
     kp.gelu_input = r.gelu_input;
     kp.out_batch_stride = static_cast<int64_t>(c_batched ? p.output_batch_stride : 0);

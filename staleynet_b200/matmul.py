@@ -115,6 +115,18 @@ class CrossEntropyHead:
     grad_scale: float
 
 
+@dataclass(frozen=True)
+class AdamWHyperparameters:
+    """`AdamWHyperparameters` (crates/staleynet-cuda/src/ops/optimizer.rs:9-28)."""
+
+    learning_rate: float
+    beta1: float
+    beta2: float
+    epsilon: float
+    weight_decay: float
+    step: int
+
+
 class MatmulKernel(enum.Enum):
     """Arithmetic of `Gpu.matmul` (device.rs:38-67). The reference's four f32 kernels become two precisions of
     one sm_100a implementation; BF16_TENSOR_CORE is new and needs bf16 operands."""
@@ -210,16 +222,16 @@ class Gpu:
 
     def gemm(self, spec: MatmulSpec, left, right, output, *, bias=None, activation: int = _ffi.ACTIVATION_NONE,
              pre_activation=None, gelu_input=None, residual=None, causal: int = _ffi.CAUSAL_NONE,
-             causal_offset: int = 0) -> None:
+             causal_offset: int = 0, row_scale=None) -> None:
         """`Gpu.matmul` with the caller's elementwise follow-up fused into the epilogue (snb_gemm)."""
         args = self.gemm_args(spec, left, right, output, bias=bias, activation=activation,
                               pre_activation=pre_activation, gelu_input=gelu_input, residual=residual, causal=causal,
-                              causal_offset=causal_offset)
+                              causal_offset=causal_offset, row_scale=row_scale)
         check(self.lib.snb_gemm(self._stream_handle(), ctypes.byref(args)))
 
     def gemm_args(self, spec: MatmulSpec, left, right, output, *, bias=None, activation: int = _ffi.ACTIVATION_NONE,
                   pre_activation=None, gelu_input=None, residual=None, causal: int = _ffi.CAUSAL_NONE,
-                  causal_offset: int = 0) -> _ffi.GemmArgs:
+                  causal_offset: int = 0, row_scale=None) -> _ffi.GemmArgs:
         """The snb_gemm_args of `gemm` (for entry points that take a GEMM as an argument)."""
         import torch
 
@@ -247,6 +259,7 @@ class Gpu:
         args.residual = _ptr(residual) if residual is not None else None
         args.causal = causal
         args.causal_offset = causal_offset
+        args.row_scale = _ptr(row_scale) if row_scale is not None else None
         return args
 
     def cross_entropy(self, logits, targets, head: "CrossEntropyHead", losses, logits_grad) -> None:
@@ -265,6 +278,82 @@ class Gpu:
         if code == _ffi.ERR_INVALID_ARGUMENT:
             raise AssertionError(self.lib.snb_last_error().decode())
         check(code)
+
+    def rms_norm_forward(self, input, gain, output, inv_rms, epsilon: float) -> None:
+        """`Gpu::rms_norm_forward` (ops/normalization.rs): f32 [rows, cols] rows normalised by 1/rms, times gain."""
+        _require_cuda(input, gain, output, inv_rms)
+        if output.shape != input.shape:
+            raise AssertionError("rms_norm_forward: output shape")
+        rows, cols = input.shape
+        code = self.lib.snb_rms_norm_forward(self._stream_handle(), _ptr(input), rows, cols, _ptr(gain), gain.numel(),
+                                             _ptr(output), _ptr(inv_rms), inv_rms.numel(), epsilon)
+        if code == _ffi.ERR_INVALID_ARGUMENT:
+            raise AssertionError(self.lib.snb_last_error().decode())
+        check(code)
+
+    def rms_norm_backward(self, output_grad, input, gain, inv_rms, input_grad, gain_grad) -> None:
+        """`Gpu::rms_norm_backward`: input_grad written, gain_grad added to."""
+        _require_cuda(output_grad, input, gain, inv_rms, input_grad, gain_grad)
+        if output_grad.shape != input.shape:
+            raise AssertionError("rms_norm_backward: output_grad shape")
+        if input_grad.shape != input.shape:
+            raise AssertionError("rms_norm_backward: input_grad shape")
+        rows, cols = input.shape
+        code = self.lib.snb_rms_norm_backward(self._stream_handle(), _ptr(output_grad), _ptr(input), _ptr(gain),
+                                              _ptr(inv_rms), _ptr(input_grad), _ptr(gain_grad), gain_grad.numel(),
+                                              rows, cols)
+        if code == _ffi.ERR_INVALID_ARGUMENT:
+            raise AssertionError(self.lib.snb_last_error().decode())
+        check(code)
+
+    def rms_norm_stats(self, input, epsilon: float, inv_rms, gain=None, output=None) -> None:
+        """snb_rms_norm_stats: 1/rms per row of input (f32 or bf16), and the normalised rows when `output` is
+        given."""
+        import torch
+
+        _require_cuda(input, inv_rms, gain, output)
+        rows, cols = input.shape
+        t = lambda x: _ffi.TYPE_BF16 if x.dtype == torch.bfloat16 else _ffi.TYPE_F32  # noqa: E731
+        check(self.lib.snb_rms_norm_stats(self._stream_handle(), _ptr(input), t(input), rows, cols, epsilon,
+                                          _ptr(inv_rms), _ptr(gain) if gain is not None else None,
+                                          _ptr(output) if output is not None else None,
+                                          t(output) if output is not None else _ffi.TYPE_F32))
+
+    def scale_rows(self, scale, input, output) -> None:
+        """snb_scale_rows: output[k, :] = scale[k] * input[k, :]."""
+        import torch
+
+        _require_cuda(scale, input, output)
+        rows, cols = input.shape
+        t = lambda x: _ffi.TYPE_BF16 if x.dtype == torch.bfloat16 else _ffi.TYPE_F32  # noqa: E731
+        check(self.lib.snb_scale_rows(self._stream_handle(), _ptr(scale), _ptr(input), t(input), _ptr(output),
+                                      t(output), rows, cols))
+
+    def adamw_step(self, parameter, gradient, first_moment, second_moment, hyper: "AdamWHyperparameters") -> None:
+        """`Gpu::adamw_step` (ops/optimizer.rs:32-66)."""
+        _require_cuda(parameter, gradient, first_moment, second_moment)
+        if not (gradient.shape == parameter.shape == first_moment.shape == second_moment.shape):
+            raise AssertionError("adamw_step: shape mismatch")
+        h = _ffi.AdamWHyper(hyper.learning_rate, hyper.beta1, hyper.beta2, hyper.epsilon, hyper.weight_decay,
+                            hyper.step)
+        check(self.lib.snb_adamw_step(self._stream_handle(), _ptr(parameter), _ptr(gradient), _ptr(first_moment),
+                                      _ptr(second_moment), parameter.numel(), ctypes.byref(h)))
+
+    def sum_of_squares(self, values, result) -> None:
+        """snb_sum_of_squares into a one-element float64 device tensor."""
+        _require_cuda(values, result)
+        check(self.lib.snb_sum_of_squares(self._stream_handle(), _ptr(values), values.numel(), _ptr(result)))
+
+    def adamw_step_multi(self, tensors, hyper: "AdamWHyperparameters", max_gradient_norm: float,
+                         gradient_square_sum) -> None:
+        """snb_adamw_step_multi over [(parameter, gradient, first, second, weight_decay), ...]."""
+        arr = (_ffi.AdamWTensor * max(1, len(tensors)))()
+        for i, (p, g, m1, m2, wd) in enumerate(tensors):
+            _require_cuda(p, g, m1, m2)
+            arr[i] = _ffi.AdamWTensor(_ptr(p), _ptr(g), _ptr(m1), _ptr(m2), p.numel(), wd, 0)
+        h = _ffi.AdamWHyper(hyper.learning_rate, hyper.beta1, hyper.beta2, hyper.epsilon, 0.0, hyper.step)
+        check(self.lib.snb_adamw_step_multi(self._stream_handle(), arr, len(tensors), ctypes.byref(h),
+                                            max_gradient_norm, _ptr(gradient_square_sum)))
 
     def head_cross_entropy(self, spec: MatmulSpec, x, w, logits, targets, codebooks: int, grad_scales, loss_sums,
                            logits_grad, *, bias=None) -> None:

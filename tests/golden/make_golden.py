@@ -135,6 +135,36 @@ CROSS_ENTROPY_KATS = [
     },
 ]
 
+RMS_NORM_KATS = [
+    {
+        "name": "rms_norm_forward_matches_the_definition",
+        "source": f"{REF_FILE}:247-254",
+        "snippets": ["rms_norm_forward(&[3.0, 4.0], &[1.0, 1.0], 2, 0.0)", "0.282_842_7", "0.848_528_1",
+                     "1.131_370_8"],
+        "input": [3.0, 4.0], "gain": [1.0, 1.0], "cols": 2, "epsilon": 0.0,
+        "expected_inv_rms": [[0.2828427, 1e-6]], "expected_output": [[0.8485281, 1e-6], [1.1313708, 1e-6]],
+    },
+    {
+        "name": "rms_norm_backward_matches_the_hand_derived_gradient",
+        "source": f"{REF_FILE}:256-265",
+        "snippets": ["[0.282_842_7f32]", "rms_norm_backward(&[1.0, 0.0], &[3.0, 4.0], &[1.0, 1.0], &inv_rms, 2)",
+                     "0.181_0", "-0.135_8", "0.848_528_1"],
+        "output_grad": [1.0, 0.0], "input": [3.0, 4.0], "gain": [1.0, 1.0], "inv_rms": [0.2828427], "cols": 2,
+        "expected_input_grad": [[0.181, 1e-3], [-0.1358, 1e-3]], "expected_gain_grad": [[0.8485281, 1e-6], [0.0, 1e-6]],
+    },
+]
+
+# The AdamW parity test's settings (tests/kernels_match_reference.rs:299-327; its expected values are computed by
+# the formula there, which the oracle restates).
+ADAMW_CASE = {
+    "source": "crates/staleynet-cuda/tests/kernels_match_reference.rs:299-327",
+    "snippets": ["learning_rate: 1e-3, beta1: 0.9, beta2: 0.95, epsilon: 1e-8, weight_decay: 0.1, step: 2",
+                 "(initial_mean, initial_variance) = (0.01f32, 0.02f32)", "random_values(shape.len(), 16)",
+                 "random_values(shape.len(), 17)", "Shape::vector(300)"],
+    "count": 300, "parameter_seed": 16, "gradient_seed": 17, "learning_rate": 1e-3, "beta1": 0.9, "beta2": 0.95,
+    "epsilon": 1e-8, "weight_decay": 0.1, "step": 2, "initial_mean": 0.01, "initial_variance": 0.02,
+}
+
 # SplitMix64 is the reference's generator (crates/staleynet-model/src/random.rs:4-46). Its published output for
 # state 0 (Vigna's splitmix64.c, the algorithm of Steele, Lea & Flood 2014) pins next_u64.
 SPLITMIX_KATS = {
@@ -153,6 +183,18 @@ def check_against_reference(reference: Path) -> None:
         for snippet in case["snippets"]:
             if snippet not in text:
                 raise SystemExit(f"{case['name']}: {snippet!r} not found at {case['source']}")
+    for case in RMS_NORM_KATS:
+        span = case["source"].rsplit(":", 1)[1]
+        lo, hi = (int(x) for x in span.split("-"))
+        text = "\n".join(lines[lo - 1:hi])
+        for snippet in case["snippets"]:
+            if snippet not in text:
+                raise SystemExit(f"{case['name']}: {snippet!r} not found at {case['source']}")
+    test_lines = (reference / "crates/staleynet-cuda/tests/kernels_match_reference.rs").read_text().splitlines()
+    text = "\n".join(test_lines[298:327])
+    for snippet in ADAMW_CASE["snippets"]:
+        if snippet not in text:
+            raise SystemExit(f"adamw: {snippet!r} not found at {ADAMW_CASE['source']}")
     random_src = (reference / "crates/staleynet-model/src/random.rs").read_text()
     for constant in ("0x9E37_79B9_7F4A_7C15", "0xBF58_476D_1CE4_E5B9", "0x94D0_49BB_1331_11EB"):
         if constant not in random_src:
@@ -175,6 +217,8 @@ def main(argv=None) -> int:
         "softmax_backward": [{k: v for k, v in c.items() if k != "snippets"} for c in SOFTMAX_BACKWARD_KATS],
         "gelu": [{k: v for k, v in c.items() if k != "snippets"} for c in GELU_KATS],
         "cross_entropy": [{k: v for k, v in c.items() if k != "snippets"} for c in CROSS_ENTROPY_KATS],
+        "rms_norm": [{k: v for k, v in c.items() if k != "snippets"} for c in RMS_NORM_KATS],
+        "adamw": {k: v for k, v in ADAMW_CASE.items() if k != "snippets"},
         "splitmix64": SPLITMIX_KATS,
     }
     (HERE / "reference_kats.json").write_text(json.dumps(out, indent=1) + "\n")

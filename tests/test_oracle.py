@@ -184,3 +184,40 @@ def test_cross_entropy_matches_the_reference_known_answers(case):
         _check_entry(float(value), expected)
     for value, expected in zip(grad, case["expected_grad"]):
         _check_entry(float(value), expected)
+
+
+@pytest.mark.parametrize("case", KATS["rms_norm"], ids=lambda c: c["name"])
+def test_rms_norm_matches_the_reference_known_answers(case):
+    """reference.rs:247-265 through the oracle's restatement of rms_norm_forward / rms_norm_backward."""
+    if "output_grad" in case:
+        dx, dg = o.rms_norm_backward(np.array(case["output_grad"]), np.array(case["input"]), np.array(case["gain"]),
+                                     np.array(case["inv_rms"]), case["cols"])
+        for value, expected in zip(dx, case["expected_input_grad"]):
+            _check_entry(float(value), expected)
+        for value, expected in zip(dg, case["expected_gain_grad"]):
+            _check_entry(float(value), expected)
+    else:
+        out, inv = o.rms_norm_forward(np.array(case["input"]), np.array(case["gain"]), case["cols"], case["epsilon"])
+        for value, expected in zip(inv, case["expected_inv_rms"]):
+            _check_entry(float(value), expected)
+        for value, expected in zip(out, case["expected_output"]):
+            _check_entry(float(value), expected)
+
+
+def test_adamw_matches_the_reference_parity_formula():
+    """The update formula of kernels_match_reference.rs:299-327 (written out there in f32) against the oracle."""
+    c = KATS["adamw"]
+    w = o.lcg_values(c["count"], c["parameter_seed"])
+    g = o.lcg_values(c["count"], c["gradient_seed"])
+    f32 = np.float32
+    b1, b2, lr, eps, wd = f32(c["beta1"]), f32(c["beta2"]), f32(c["learning_rate"]), f32(c["epsilon"]), f32(c["weight_decay"])
+    mean = b1 * f32(c["initial_mean"]) + (f32(1) - b1) * g
+    var = b2 * f32(c["initial_variance"]) + (f32(1) - b2) * g * g
+    mean_hat = mean / (f32(1) - b1 ** 2)
+    var_hat = var / (f32(1) - b2 ** 2)
+    expected = w - lr * (mean_hat / (np.sqrt(var_hat) + eps) + wd * w)
+    p = w.copy()
+    m = np.full(c["count"], c["initial_mean"], np.float32)
+    v = np.full(c["count"], c["initial_variance"], np.float32)
+    o.adamw_step(p, g, m, v, c["learning_rate"], c["beta1"], c["beta2"], c["epsilon"], c["weight_decay"], c["step"])
+    assert o.relative_error(expected, p) < 1e-5
