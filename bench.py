@@ -536,6 +536,181 @@ def run_head(args, rank: int, world: int, local_rank: int) -> int:
     return 0
 
 
+def model_parameter_shapes(s) -> list:
+    """(name, elements, decayed) of every parameter of the BASELINE config 3 model (gpt.rs; weights decayed, gains,
+    biases and embeddings exempt as parameter.rs marks them): token and position embeddings, per block two RMSNorm
+    gains and four linears with biases, the final norm and the 16 x 1024 head."""
+    out = [("token_embedding", s.codebooks * s.codebook_size * s.width, False),
+           ("position_embedding", 2048 * s.width, False)]
+    from staleynet_b200.step import linear_shapes
+
+    for b in range(s.blocks):
+        out.append((f"block{b}.attention_norm.gain", s.width, False))
+        out.append((f"block{b}.ffn_norm.gain", s.width, False))
+        for name, i, o in linear_shapes(s):
+            out.append((f"block{b}.{name}.weight", i * o, True))
+            out.append((f"block{b}.{name}.bias", o, False))
+    out.append(("final_norm.gain", s.width, False))
+    out.append(("head.weight", s.width * s.head_width, True))
+    out.append(("head.bias", s.head_width, False))
+    return out
+
+
+def run_optimizer(args, rank: int, world: int, local_rank: int) -> int:
+    """The optimizer step of BASELINE config 3's model (~111.5 M parameters): global gradient norm, clip, AdamW.
+
+    --optimizer-path multi (default): snb_adamw_step_multi — two launches, the clip factor on the device.
+    --optimizer-path reference-shaped: AdamW::step's sequence (model optimizer.rs:125-177) on this library — per
+    tensor snb_sum_of_squares and a host read of it, then per tensor the gradient scaled and snb_adamw_step."""
+    import torch
+
+    from staleynet_b200.matmul import AdamWHyperparameters, Gpu
+    from staleynet_b200.step import ModelShape
+
+    torch.cuda.set_device(local_rank)
+    device = torch.device("cuda", local_rank)
+    stream = torch.cuda.current_stream(device)
+    shapes = model_parameter_shapes(ModelShape())
+    g = torch.Generator(device=device)
+    g.manual_seed(rank)
+    tensors = []
+    for _, n, decayed in shapes:
+        p = torch.randn(n, device=device, generator=g) * 0.02
+        grad = torch.randn(n, device=device, generator=g) * 1e-3
+        tensors.append((p, grad, torch.zeros(n, device=device), torch.zeros(n, device=device), 0.1 if decayed else 0.0))
+    elements = sum(n for _, n, _ in shapes)
+    gpu = Gpu(local_rank)
+    multi = args.optimizer_path == "multi"
+    square_sum = torch.zeros(1, device=device, dtype=torch.float64)
+    host = torch.empty(1, dtype=torch.float64, pin_memory=True)
+    state = {"step": 0}
+
+    def step():
+        state["step"] += 1
+        if multi:
+            gpu.adamw_step_multi(tensors, AdamWHyperparameters(3e-4, 0.9, 0.95, 1e-8, 0.0, state["step"]), 1.0,
+                                 square_sum)
+            return
+        total = 0.0
+        for _, grad, _, _, _ in tensors:
+            gpu.sum_of_squares(grad, square_sum)
+            host.copy_(square_sum, non_blocking=True)
+            torch.cuda.current_stream().synchronize()
+            total += float(host)
+        norm = total ** 0.5
+        clip = 1.0 / norm if norm > 1.0 else 1.0
+        for p, grad, m, v, wd in tensors:
+            if clip != 1.0:
+                grad.mul_(clip)   # the reference's gpu.scale pass (a torch op here: it is not this library's path)
+            gpu.adamw_step(p, grad, m, v, AdamWHyperparameters(3e-4, 0.9, 0.95, 1e-8, wd, state["step"]))
+
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize()
+    clocks = ClockSampler(local_rank)
+    clocks.start()
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    start.record(stream)
+    for _ in range(args.steps):
+        step()
+    end.record(stream)
+    torch.cuda.synchronize()
+    clock_info = clocks.stop()
+    ms = start.elapsed_time(end) / args.steps
+    if rank != 0:
+        return 0
+    peaks, source = load_peaks()
+    hbm = float(peaks.get("hbm_gbs", FALLBACK_PEAKS["hbm_gbs"]))
+    algorithmic = elements * 4 * (1 + 7)   # sum of squares reads the gradient; AdamW reads 4 and writes 3 arrays
+    line = {
+        "metric": "optimizer step (global norm + clip + AdamW) time", "value": ms, "unit": "ms",
+        "n_gpus": 1, "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": False,
+        "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic (seeded parameters and gradients)",
+        "config": {"workload": "cfg3 model optimizer step: 111.5 M f32 parameters in "
+                               f"{len(shapes)} tensors, gradient-norm clip at 1.0, AdamW", "optimizer_path":
+                   args.optimizer_path, "parameters": elements, "tensors": len(shapes),
+                   "l2": "inputs larger than L2 (1.8 GB of parameters, gradients and moments)"},
+        "roofline": {"bound": "hbm", "kernel": "multi_adamw_kernel + multi_sum_of_squares_kernel" if multi else
+                     "sum_of_squares_kernel + adamw_kernel per tensor",
+                     "achieved": algorithmic / (ms / 1e3) / 1e9, "peak": hbm, "unit": "GB/s",
+                     "frac": algorithmic / (ms / 1e3) / 1e9 / hbm, "traffic": None,
+                     "algorithmic_bytes_per_step": algorithmic, "peak_source": f"{source} hbm_gbs"},
+        "e2e": {"value": ms, "unit": "ms", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0 if multi else 8 * len(shapes)},
+        "gpu_launches": (2 if multi else 2 * len(shapes)) * args.steps, "clocks": clock_info,
+    }
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+def run_norm(args, rank: int, world: int, local_rank: int) -> int:
+    """RMSNorm into the next GEMM at BASELINE config 3 (65,536 tokens, 768 -> 2304, the QKV product):
+    --norm-path fused (default): snb_rms_norm_stats (1/rms only) + the GEMM on the raw rows with row_scale and the
+    gain folded into the weights; --norm-path unfused: the normalised rows written as bf16, then the GEMM."""
+    import torch
+
+    from staleynet_b200.matmul import Gpu, MatmulSpec
+
+    torch.cuda.set_device(local_rank)
+    device = torch.device("cuda", local_rank)
+    stream = torch.cuda.current_stream(device)
+    tokens, width, cols, eps = args.tokens, 768, 2304, 1e-5
+    g = torch.Generator(device=device)
+    g.manual_seed(rank)
+    x = torch.randn(tokens, width, device=device, generator=g).bfloat16()
+    gain = 1.0 + 0.1 * torch.randn(width, device=device, generator=g)
+    w = (torch.randn(width, cols, device=device, generator=g) / width ** 0.5).bfloat16()
+    bias = torch.zeros(cols, device=device)
+    y = torch.empty(tokens, cols, device=device, dtype=torch.bfloat16)
+    inv = torch.empty(tokens, device=device)
+    gpu = Gpu(local_rank)
+    spec = MatmulSpec.new(tokens, cols, width)
+    fused = args.norm_path == "fused"
+    wg = torch.empty_like(w)
+    gpu.scale_rows(gain, w, wg)      # once per optimizer step, not per use
+    xn = torch.empty_like(x)
+
+    def step():
+        if fused:
+            gpu.rms_norm_stats(x, eps, inv)
+            gpu.gemm(spec, x, wg, y, bias=bias, row_scale=inv)
+        else:
+            gpu.rms_norm_stats(x, eps, inv, gain=gain, output=xn)
+            gpu.gemm(spec, xn, w, y, bias=bias)
+
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize()
+    clocks = ClockSampler(local_rank)
+    clocks.start()
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    start.record(stream)
+    for _ in range(args.steps):
+        step()
+    end.record(stream)
+    torch.cuda.synchronize()
+    clock_info = clocks.stop()
+    ms = start.elapsed_time(end) / args.steps
+    if rank != 0:
+        return 0
+    peaks, source = load_peaks()
+    flops = 2.0 * tokens * width * cols
+    peak = float(peaks.get("bf16_tflops", FALLBACK_PEAKS["bf16_tflops"]))
+    line = {
+        "metric": METRIC, "value": flops / (ms / 1e3) / 1e12, "unit": UNIT, "n_gpus": 1, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+        "dtype": "bf16", "data": "synthetic (seeded N(0,1) rows, gains near 1)",
+        "config": {"workload": "cfg3 RMSNorm + QKV product: 65,536 x 768 -> 2304", "norm_path": args.norm_path,
+                   "tokens": tokens, "l2": "inputs larger than L2 (y: 302 MB bf16)"},
+        "roofline": {"bound": "tensor", "kernel": "tc_gemm_kernel with row_scale (+ rms statistics)",
+                     "achieved": flops / (ms / 1e3) / 1e12, "peak": peak, "unit": "TFLOP/s",
+                     "frac": flops / (ms / 1e3) / 1e12 / peak, "traffic": None, "peak_source": f"{source} bf16_tflops"},
+        "e2e": {"value": flops / (ms / 1e3) / 1e12, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+        "gpu_launches": 2 * args.steps, "clocks": clock_info,
+    }
+    print(json.dumps(line), flush=True)
+    return 0
+
+
 def run_attention(args, rank: int, world: int, local_rank: int) -> int:
     """one causal attention forward + backward per step (batch 8, 12 heads of 64, sequence 3072).
 
@@ -647,13 +822,16 @@ def main(argv=None) -> int:
     ap.add_argument("--cpu-sample-flops", type=float, default=20e9)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--breakdown", default=None, help="write per-GEMM kernel times of the timed region here (JSON)")
-    ap.add_argument("--workload", choices=["step", "attention", "head"], default="step",
+    ap.add_argument("--workload", choices=["step", "attention", "head", "optimizer", "norm"], default="step",
                     help="step: the cfg3 training-step GEMMs (default); attention: the cfg4 attention layer; "
-                         "head: the cfg3 output layer's forward + cross-entropy")
+                         "head: the cfg3 output layer's forward + cross-entropy; optimizer: the cfg3 AdamW step; "
+                         "norm: RMSNorm into the QKV product")
     ap.add_argument("--attention-path", choices=["fused", "materialised"], default="fused",
                     help="attention workload: fused entry points (default) or the six materialised products")
     ap.add_argument("--head-path", choices=["fused", "reference-shaped"], default="fused",
                     help="head workload: snb_head_cross_entropy (default) or the reference's per-codebook sequence")
+    ap.add_argument("--optimizer-path", choices=["multi", "reference-shaped"], default="multi")
+    ap.add_argument("--norm-path", choices=["fused", "unfused"], default="fused")
     args = ap.parse_args(argv)
     if args.warmup < 3:
         ap.error("--warmup must be at least 3")
@@ -681,6 +859,10 @@ def main(argv=None) -> int:
             return run_attention(args, rank, world, local_rank)
         if args.workload == "head":
             return run_head(args, rank, world, local_rank)
+        if args.workload == "optimizer":
+            return run_optimizer(args, rank, world, local_rank)
+        if args.workload == "norm":
+            return run_norm(args, rank, world, local_rank)
         return run_ours(args, shape, rank, world, local_rank)
     finally:
         if world > 1:
