@@ -55,14 +55,19 @@ def load_traffic(shape) -> dict:
     return json.loads(path.read_text())
 
 
-def load_kernel_traffic(kernel: str):
-    """Per-launch DRAM bytes (read + write) of one fused-attention kernel at BASELINE config 4, from the ncu capture
-    summarised in profiles/fused_attention_cfg4_kernels.json; None when no capture is committed."""
-    path = ROOT / "profiles" / "fused_attention_cfg4_kernels.json"
+def load_profile_traffic(summary: str, kernel: str):
+    """Per-launch DRAM bytes (read + write) of `kernel` from an ncu capture summarised in profiles/<summary>; None
+    when no capture is committed."""
+    path = ROOT / "profiles" / summary
     if not path.exists():
         return None
     entry = json.loads(path.read_text()).get(kernel)
     return None if entry is None else entry.get("dram_bytes")
+
+
+def load_kernel_traffic(kernel: str):
+    """A fused-attention kernel's DRAM bytes per launch at BASELINE config 4."""
+    return load_profile_traffic("fused_attention_cfg4_kernels.json", kernel)
 
 
 def workload_config(shape, n_gpus: int) -> dict:
@@ -521,7 +526,9 @@ def run_head(args, rank: int, world: int, local_rank: int) -> int:
                    "codebook_size": size, "l2": "inputs larger than L2 (logits 2.1 GB bf16 / 4.3 GB f32)"},
         "roofline": {"bound": "hbm", "kernel": "cross_entropy_kernel (step time minus the head GEMM's own time)",
                      "achieved": ce_bytes / (ce_ms / 1e3) / 1e9, "peak": hbm, "unit": "GB/s",
-                     "frac": ce_bytes / (ce_ms / 1e3) / 1e9 / hbm, "traffic": None,
+                     "frac": ce_bytes / (ce_ms / 1e3) / 1e9 / hbm,
+                     "traffic": load_profile_traffic("cross_entropy_cfg3_kernel.json", "cross_entropy_kernel")
+                     if fused and tokens == 65536 else None,
                      "algorithmic_bytes_per_step": ce_bytes, "peak_source": f"{source} hbm_gbs",
                      "head_gemm_ms": gemm_ms, "loss_ms": ce_ms,
                      "head_gemm_tflops": flops / (gemm_ms / 1e3) / 1e12},
