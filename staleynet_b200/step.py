@@ -140,15 +140,25 @@ class TrainingStepGemms:
         a.residual = residual.data_ptr() if residual is not None else None
         return a
 
+    def use_input(self, x) -> None:
+        """Points the step's first-block products at input activations `x` (same shape and type as x_in), so a
+        caller can upload the next step's input into a second buffer while this step runs."""
+        assert x.numel() == self.x_in.numel() and x.dtype == self.x_in.dtype
+        for a in self._input_args:
+            a.left = x.data_ptr()
+
     def _build_plan(self) -> None:
         s = self.shape
         T, w, f, V = s.tokens, s.width, s.ffn, s.head_width
         fwd, bwd = [], []
         x = self.x_in
+        self._input_args = []   # the argument blocks that read the step's input activations
         for b in range(s.blocks):
             W, B, A = self.weights[b], self.biases[b], self.acts[b]
             fwd.append(("qkv.fwd", 2.0 * T * w * 3 * w,
                         self._args(MatmulSpec.new(T, 3 * w, w), x, W["qkv"], A["qkv"], bias=B["qkv"])))
+            if b == 0:
+                self._input_args.append(fwd[-1][2])
             fwd.append(("output.fwd", 2.0 * T * w * w,
                         self._args(MatmulSpec.new(T, w, w), A["ctx"], W["output"], A["mid"], bias=B["output"],
                                    residual=x)))
@@ -194,6 +204,8 @@ class TrainingStepGemms:
             bwd.append(("qkv.dW", 2.0 * T * w * 3 * w,
                         self._args(MatmulSpec.new(w, 3 * w, T).left_transposed().accumulate(), x_b, self.g_qkv,
                                    G["qkv"])))
+            if b == 0:
+                self._input_args.append(bwd[-1][2])
             bwd.append(("qkv.dX", 2.0 * T * 3 * w * w,
                         self._args(MatmulSpec.new(T, w, 3 * w).right_transposed(), self.g_qkv, W["qkv"],
                                    self.g_in, residual=self.g_mid)))
