@@ -17,11 +17,12 @@
 //                    dQ_i = dS K_j                               (M=128 queries, N=64, K=128 keys)
 //                  dS^T lives once in shared memory as a 128B-swizzled tile whose rows are keys: the dK product reads
 //                  it K-major, the dQ product reads the same bytes M-major (queries contiguous).
-//     warps 0-7    per key row (TMEM lane quadrant warp % 4) and query half (warp / 4): P = 2^(S c + nl),
-//                  dS = P (dP - D), causal and range masks applied, P^T stored bf16 into TMEM, dS^T into shared memory;
-//                  at the end dV and scale * dK written out.
-//     warps 8-11   drain dQ_i from TMEM (queries on lanes), scale it and add it into the global dQ (f32, zeroed by
-//                  the host) with TMA reduce-add, each warp through its own two 128B-swizzled 32x32 staging boxes.
+//     warps 0-11   per key row (TMEM lane quadrant warp % 4) and query group (warp / 4: 48, 48 and 32 of the 128
+//                  queries): P = 2^(S c + nl), dS = P (dP - D), causal and range masks applied, P^T stored bf16 into
+//                  TMEM, dS^T into shared memory; at the end warps 0-7 write dV and scale * dK.
+//     warps 8-11   also drain dQ_{i-1} after their share of tile i (queries on lanes): scale it and add it into the
+//                  global dQ (f32, zeroed by the host) with TMA reduce-add, each warp through its own two
+//                  128B-swizzled 32x32 staging boxes, while dV and dK of tile i run.
 // Every mbarrier wait is bounded (see sm100_ptx.cuh).
 #pragma once
 
@@ -33,8 +34,7 @@ constexpr int FB_BK = 128;   // keys per CTA (TMEM lanes of S^T, dP^T, dV, dK)
 constexpr int FB_BQ = 128;   // queries per iteration
 constexpr int FB_D = 64;
 constexpr int FB_STAGES = 3;
-constexpr int FB_ELEM_WARPS = 8;
-constexpr int FB_DQ_WARP0 = 8;
+constexpr int FB_ELEM_WARPS = 12;   // warps 0-11: P and dS; warps 8-11 also drain dQ
 constexpr int FB_PRODUCER_WARP = 12;
 constexpr int FB_MMA_WARP = 13;
 constexpr int FB_THREADS = 14 * 32;
@@ -263,44 +263,91 @@ __global__ void __launch_bounds__(FB_THREADS, 1)
         __syncwarp();
     } else if (warp < FB_ELEM_WARPS) {
         // ------------------------------------------------------------------ P and dS (one key row per thread)
-        const int quad = warp & 3;          // TMEM lane quadrant
-        const int h = warp >> 2;            // query half of every tile: queries [64h, 64h + 64)
-        const int r = quad * 32 + lane;     // key row within the tile
+        // Warp w serves TMEM lane quadrant w % 4 and query group w / 4: 16-query chunks 0-2, 3-5 or 6-7 of every
+        // tile. The last group's warps also drain dQ, one tile behind, while dV and dK of the current tile run.
+        const int quad = warp & 3;
+        const int group = warp >> 2;
+        const int ch0 = 3 * group;                 // first chunk of the group
+        const int nch = group == 2 ? 2 : 3;        // chunks of the group
+        const int gc0 = 16 * ch0, gw = 16 * nch;   // first query column and width of the group
+        const int r = quad * 32 + lane;            // key row within the tile
         const int64_t key = static_cast<int64_t>(key0) + r;
         const uint32_t lane_base = static_cast<uint32_t>(quad * 32) << 16;
-        const uint32_t ds_row = smem_addr(ds_s + h * (FbSmem::DS / 2) + r * 128);
+        const uint32_t ds_row = smem_addr(ds_s + r * 128);   // row r of slice 0; slice s is DS/2 * s further
         const float c = p.scale_log2;
+        const bool drains = group == 2;
+        uint8_t* box0 = dq_s + quad * (FbSmem::DQ / 4);   // dQ staging: columns 0-31 of rows 32 quad ..
+        uint8_t* box1 = box0 + FbSmem::DQ / 8;             // columns 32-63
+        // dQ of tile m: scale it and add it into the global dQ through this warp's two 32x32 f32 staging boxes.
+        auto drain = [&](int32_t m) -> bool {
+            if (!warp_wait(smem_addr(dq_full), m & 1)) return false;
+            tcgen05_fence_after_sync();
+            uint32_t da[32], db[32];
+            tmem_load_32x32b_x32(tmem_base + lane_base + FB_DQ_COL, da);
+            tmem_load_32x32b_x32(tmem_base + lane_base + FB_DQ_COL + 32, db);
+            tmem_load_wait();
+            tcgen05_fence_before_sync();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(smem_addr(dq_empty));
+            // The staging boxes are free once this warp's previous reductions have read them.
+            if (lane == 0) bulk_wait_group_read<0>();
+            __syncwarp();
+            const uint32_t row0 = smem_addr(box0 + lane * 128), row1 = smem_addr(box1 + lane * 128);
+#pragma unroll
+            for (int g = 0; g < 8; ++g) {
+                const uint32_t off = (g ^ (lane & 7)) << 4;
+                st_shared_v4(row0 + off, __float_as_uint(__uint_as_float(da[4 * g]) * p.scale),
+                             __float_as_uint(__uint_as_float(da[4 * g + 1]) * p.scale),
+                             __float_as_uint(__uint_as_float(da[4 * g + 2]) * p.scale),
+                             __float_as_uint(__uint_as_float(da[4 * g + 3]) * p.scale));
+                st_shared_v4(row1 + off, __float_as_uint(__uint_as_float(db[4 * g]) * p.scale),
+                             __float_as_uint(__uint_as_float(db[4 * g + 1]) * p.scale),
+                             __float_as_uint(__uint_as_float(db[4 * g + 2]) * p.scale),
+                             __float_as_uint(__uint_as_float(db[4 * g + 3]) * p.scale));
+            }
+            fence_proxy_async_shared();
+            __syncwarp();
+            if (lane == 0) {
+                const int32_t q0 = (i_first + m) * FB_BQ + 32 * quad;
+                tma_reduce_add_3d(&tm_dq, smem_addr(box0), 0, q0, matrix);
+                tma_reduce_add_3d(&tm_dq, smem_addr(box1), 32, q0, matrix);
+                bulk_commit_group();
+            }
+            return true;
+        };
         bool ok = true;
         int stage = 0;
         uint32_t phase = 0;
         for (int32_t n = 0; n < n_iter; ++n) {
-            const int64_t qh = static_cast<int64_t>(i_first + n) * FB_BQ + 64 * h;   // first query of this half
-            // Visible columns j of this half: qh + j >= key - offset, qh + j < sq, and key < sk.
-            const int64_t lo64 = key < p.sk ? key - p.offset - qh : 64;
-            const int64_t hi64 = static_cast<int64_t>(p.sq) - qh;
-            const int32_t lo = static_cast<int32_t>(lo64 < 0 ? 0 : (lo64 > 64 ? 64 : lo64));
-            const int32_t hi = static_cast<int32_t>(hi64 < 0 ? 0 : (hi64 > 64 ? 64 : hi64));
+            const int64_t qg = static_cast<int64_t>(i_first + n) * FB_BQ + gc0;   // first query of this group
+            // Visible columns j of this group: qg + j >= key - offset, qg + j < sq, and key < sk.
+            const int64_t lo64 = key < p.sk ? key - p.offset - qg : gw;
+            const int64_t hi64 = static_cast<int64_t>(p.sq) - qg;
+            const int32_t lo = static_cast<int32_t>(lo64 < 0 ? 0 : (lo64 > gw ? gw : lo64));
+            const int32_t hi = static_cast<int32_t>(hi64 < 0 ? 0 : (hi64 > gw ? gw : hi64));
             if (!warp_wait(smem_addr(sdp_full), n & 1) || !warp_wait(smem_addr(&qdo_full[stage]), phase)) {
                 ok = false;
                 break;
             }
             tcgen05_fence_after_sync();
-            // (nl, D) of query 2k, 2k+1 of this half at stats + 16 k bytes, read with explicit shared loads.
-            const uint32_t stats = smem_addr(stage_s + stage * FbSmem::STAGE + 2 * FbSmem::QT) + 8 * 64 * h;
+            // (nl, D) of query 2k, 2k+1 of this group at stats + 16 k bytes, read with explicit shared loads.
+            const uint32_t stats = smem_addr(stage_s + stage * FbSmem::STAGE + 2 * FbSmem::QT) + 8 * gc0;
             // Off the diagonal and the ragged edges every column of every row of the warp is visible.
-            const bool unmasked = __all_sync(0xffffffffu, lo == 0 && hi == 64);
+            const bool unmasked = __all_sync(0xffffffffu, lo == 0 && hi == gw);
             // Scores and their gradients in 16-column chunks, the next chunk's TMEM loads in flight while this one
             // is computed.
             uint32_t s[2][16], dp[2][16];
-            tmem_load_32x32b_x16(tmem_base + lane_base + FB_S_COL + 64 * h, s[0]);
-            tmem_load_32x32b_x16(tmem_base + lane_base + FB_DP_COL + 64 * h, dp[0]);
+            tmem_load_32x32b_x16(tmem_base + lane_base + FB_S_COL + gc0, s[0]);
+            tmem_load_32x32b_x16(tmem_base + lane_base + FB_DP_COL + gc0, dp[0]);
             tmem_load_wait();
 #pragma unroll
-            for (int cc = 0; cc < 4; ++cc) {
+            for (int cc = 0; cc < 3; ++cc) {
+                if (cc >= nch) break;
                 const int b = cc & 1;
-                if (cc < 3) {
-                    tmem_load_32x32b_x16(tmem_base + lane_base + FB_S_COL + 64 * h + 16 * (cc + 1), s[b ^ 1]);
-                    tmem_load_32x32b_x16(tmem_base + lane_base + FB_DP_COL + 64 * h + 16 * (cc + 1), dp[b ^ 1]);
+                const int ch = ch0 + cc;
+                if (cc + 1 < nch) {
+                    tmem_load_32x32b_x16(tmem_base + lane_base + FB_S_COL + 16 * (ch + 1), s[b ^ 1]);
+                    tmem_load_32x32b_x16(tmem_base + lane_base + FB_DP_COL + 16 * (ch + 1), dp[b ^ 1]);
                 }
                 uint32_t pw[8], dw[8];
 #pragma unroll
@@ -322,13 +369,14 @@ __global__ void __launch_bounds__(FB_THREADS, 1)
                     ok = false;
                 }
                 if (ok) {
-                    tmem_store_32x32b_x8(tmem_base + lane_base + FB_P_COL + 32 * h + 8 * cc, pw);
-                    // dS^T row r, queries 64h + 16cc ..: 16-byte chunks 2cc, 2cc + 1 of the 128-byte row, swizzled.
-                    st_shared_v4(ds_row + (((2 * cc) ^ (r & 7)) << 4), dw[0], dw[1], dw[2], dw[3]);
-                    st_shared_v4(ds_row + (((2 * cc + 1) ^ (r & 7)) << 4), dw[4], dw[5], dw[6], dw[7]);
+                    tmem_store_32x32b_x8(tmem_base + lane_base + FB_P_COL + 8 * ch, pw);
+                    // dS^T row r, queries 16 ch ..: slice ch / 4, 16-byte chunks 2 (ch % 4), +1 of its 128-byte row.
+                    const uint32_t row = ds_row + (ch / 4) * (FbSmem::DS / 2);
+                    st_shared_v4(row + (((2 * (ch % 4)) ^ (r & 7)) << 4), dw[0], dw[1], dw[2], dw[3]);
+                    st_shared_v4(row + (((2 * (ch % 4) + 1) ^ (r & 7)) << 4), dw[4], dw[5], dw[6], dw[7]);
                 }
-                if (cc < 3) tmem_load_wait();
-                if (cc == 2) {
+                if (cc + 1 < nch) tmem_load_wait();
+                if (cc + 2 == nch) {
                     // S^T and dP^T are all in registers: the next tile's products may overwrite them.
                     tcgen05_fence_before_sync();
                     __syncwarp();
@@ -342,10 +390,15 @@ __global__ void __launch_bounds__(FB_THREADS, 1)
             __syncwarp();
             if (lane == 0) mbar_arrive(smem_addr(pds_full));
             if (++stage == FB_STAGES) { stage = 0; phase ^= 1u; }
+            if (drains && n > 0 && !drain(n - 1)) { ok = false; break; }
         }
-        // dV (h = 0) or scale * dK (h = 1) of this warp's 32 key rows (zero when no query sees them). The TMEM loads
-        // are warp-collective; only the stores depend on the row.
-        if (ok && warp_wait(smem_addr(acc_done), 0)) {
+        if (drains) {
+            if (ok && n_iter > 0) ok = drain(n_iter - 1);
+            if (lane == 0) bulk_wait_group<0>();
+        } else if (ok && warp_wait(smem_addr(acc_done), 0)) {
+            // dV (group 0) or scale * dK (group 1) of this warp's 32 key rows (zero when no query sees them). The
+            // TMEM loads are warp-collective; only the stores depend on the row.
+            const int h = group;
             tcgen05_fence_after_sync();
             float* dst = (h == 0 ? p.dv : p.dk) + (static_cast<int64_t>(matrix) * p.sk + key) * FB_D;
             const float mul = n_iter == 0 ? 0.0f : (h == 0 ? 1.0f : p.scale);
@@ -357,8 +410,7 @@ __global__ void __launch_bounds__(FB_THREADS, 1)
                     float4* d4 = reinterpret_cast<float4*>(dst + c0);
 #pragma unroll
                     for (int g = 0; g < 8; ++g) {
-                        // (n_iter == 0: TMEM holds no product; multiply-by-zero of whatever it holds is replaced by
-                        // an explicit zero so that stale NaN bits cannot leak.)
+                        // (n_iter == 0: TMEM holds no product; an explicit zero keeps stale bits out.)
                         d4[g] = n_iter == 0 ? make_float4(0.0f, 0.0f, 0.0f, 0.0f)
                                             : make_float4(__uint_as_float(o[4 * g]) * mul,
                                                           __uint_as_float(o[4 * g + 1]) * mul,
@@ -368,50 +420,6 @@ __global__ void __launch_bounds__(FB_THREADS, 1)
                 }
             }
         }
-    } else if (warp < FB_DQ_WARP0 + 4) {
-        // ------------------------------------------------------------------ dQ drain (one query row per thread)
-        // Each warp stages and reduces its own 32 query rows (two 32x32 f32 boxes), so the four warps never wait for
-        // one another.
-        const int quad = warp & 3;
-        const uint32_t lane_base = static_cast<uint32_t>(quad * 32) << 16;
-        uint8_t* box0 = dq_s + quad * (FbSmem::DQ / 4);   // columns 0-31 of rows 32 quad ..
-        uint8_t* box1 = box0 + FbSmem::DQ / 8;             // columns 32-63
-        for (int32_t n = 0; n < n_iter; ++n) {
-            if (!warp_wait(smem_addr(dq_full), n & 1)) break;
-            tcgen05_fence_after_sync();
-            uint32_t a[32], b[32];
-            tmem_load_32x32b_x32(tmem_base + lane_base + FB_DQ_COL, a);
-            tmem_load_32x32b_x32(tmem_base + lane_base + FB_DQ_COL + 32, b);
-            tmem_load_wait();
-            tcgen05_fence_before_sync();
-            __syncwarp();
-            if (lane == 0) mbar_arrive(smem_addr(dq_empty));
-            // The staging boxes are free once this warp's previous reductions have read them.
-            if (lane == 0) bulk_wait_group_read<0>();
-            __syncwarp();
-            const uint32_t row0 = smem_addr(box0 + lane * 128), row1 = smem_addr(box1 + lane * 128);
-#pragma unroll
-            for (int g = 0; g < 8; ++g) {
-                const uint32_t off = (g ^ (lane & 7)) << 4;
-                st_shared_v4(row0 + off, __float_as_uint(__uint_as_float(a[4 * g]) * p.scale),
-                             __float_as_uint(__uint_as_float(a[4 * g + 1]) * p.scale),
-                             __float_as_uint(__uint_as_float(a[4 * g + 2]) * p.scale),
-                             __float_as_uint(__uint_as_float(a[4 * g + 3]) * p.scale));
-                st_shared_v4(row1 + off, __float_as_uint(__uint_as_float(b[4 * g]) * p.scale),
-                             __float_as_uint(__uint_as_float(b[4 * g + 1]) * p.scale),
-                             __float_as_uint(__uint_as_float(b[4 * g + 2]) * p.scale),
-                             __float_as_uint(__uint_as_float(b[4 * g + 3]) * p.scale));
-            }
-            fence_proxy_async_shared();
-            __syncwarp();
-            if (lane == 0) {
-                const int32_t q0 = (i_first + n) * FB_BQ + 32 * quad;
-                tma_reduce_add_3d(&tm_dq, smem_addr(box0), 0, q0, matrix);
-                tma_reduce_add_3d(&tm_dq, smem_addr(box1), 32, q0, matrix);
-                bulk_commit_group();
-            }
-        }
-        if (lane == 0) bulk_wait_group<0>();
     }
 
     tcgen05_fence_before_sync();
