@@ -14,7 +14,10 @@
 //              time (tcgen05.ld 32x32b.x32), applies scale / bias / GELU / residual, writes a swizzled 32x128-byte
 //              box to shared memory and stores it with a TMA store, or a TMA reduce-add when accumulating into C.
 //              The second accumulator lets the epilogue of one tile overlap the main loop of the next; eight
-//              warps (two per scheduler) hide the latency of TMEM and global loads.
+//              warps (two per scheduler) hide the latency of TMEM and global loads. When a bf16 output reads one
+//              bf16 auxiliary input (GELU input or residual), each warp TMA-loads that input's chunks into its
+//              staging boxes as soon as its previous tile's stores have read them, and the output overwrites the
+//              input in place.
 //
 // Operand layouts: each operand is either K-major (K contiguous) or MN-major (M or N contiguous); both are loaded
 // by TMA in their stored order and described to the tensor core by the major bits of the instruction descriptor,
@@ -67,6 +70,12 @@ struct TcParams {
     const float* row_scale;   // [M] output-row multipliers (one matrix), or nullptr
 };
 
+// Epilogue staging modes (see epilogue_tile); the host picks one per launch.
+constexpr int TC_EPI_ONE_BOX = 1;
+constexpr int TC_EPI_TWO_BOX = 2;
+constexpr int TC_EPI_AUX_BOX = 3;
+constexpr int tc_epi_boxes(int epi) { return epi == TC_EPI_ONE_BOX ? 1 : 2; }
+
 // NBOX = staging boxes per epilogue warp: 2 lets a chunk be staged while the previous chunk's TMA store still reads
 // its box (worth it for GELU epilogues), at the price of one ring stage for BN = 256.
 template <int BN, int NBOX>
@@ -77,7 +86,7 @@ struct TcConfig {
     static constexpr int STAGES = BN == 256 ? (NBOX == 2 ? 3 : 4) : (BN == 128 ? 4 : 6);
     static constexpr int EPI_BYTES = TC_EPI_WARPS * NBOX * TC_EPI_BOX_BYTES;
     static constexpr int TMEM_COLS = 2 * BN;
-    static constexpr int BARRIER_BYTES = 256;
+    static constexpr int BARRIER_BYTES = 512;
     static constexpr int SMEM_BYTES = 1024 + STAGES * STAGE + EPI_BYTES + BARRIER_BYTES;
     static_assert(SMEM_BYTES <= 232448, "shared memory budget of one sm_100 CTA");
     static_assert(TMEM_COLS == 128 || TMEM_COLS == 256 || TMEM_COLS == 512, "TMEM allocation is a power of two");
@@ -250,11 +259,13 @@ __device__ __forceinline__ void stage_half(uint8_t* box, int lane, int h, const 
 //   x = scale * row_scale[row] * acc + bias;  (x staged into pre_box when given);  pre_only: return x;
 //   y = activation(x) (+ residual).
 // The first auxiliary input (GELU input, else residual) is requested before waiting for TMEM so the two latencies
-// overlap; only when both are present is the residual read afterwards.
+// overlap; only when both are present is the residual read afterwards. With `aux_box` the first auxiliary input is
+// already in shared memory (TMA-loaded into the 128B-swizzled staging box this half is staged into) and is read
+// from this lane's row of it.
 template <bool OUT_BF16>
 __device__ __forceinline__ void epilogue_half(const TcParams& p, uint32_t taddr, int32_t col, int32_t row,
                                               int64_t out_base, bool first_split, uint8_t* pre_box, int h,
-                                              float2 (&v)[16], bool pre_only) {
+                                              float2 (&v)[16], bool pre_only, const uint8_t* aux_box = nullptr) {
     uint32_t x[32];
     tmem_load_32x32b_x32(taddr, x);
     const int valid = p.N - col;  // columns of this piece inside the matrix (a multiple of 4 or 8)
@@ -262,8 +273,19 @@ __device__ __forceinline__ void epilogue_half(const TcParams& p, uint32_t taddr,
     const bool want_gin = !pre_only && p.activation == 2;
     const bool want_res = !pre_only && p.residual != nullptr && first_split;
     uint4 raux[8];
-    if (want_gin) load_row_32(p.gelu_input, out_base + col, p.aux_bf16, valid, row_live, raux);
-    else if (want_res) load_row_32(p.residual, out_base + col, OUT_BF16, valid, row_live, raux);
+    if (aux_box != nullptr) {
+        const int lane = threadIdx.x & 31;
+        const uint32_t rowp = smem_addr(aux_box) + lane * 128;
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+            const float4 f = ld_shared_f4(rowp + (((4 * h + j) ^ (lane & 7)) << 4));
+            raux[j] = make_uint4(__float_as_uint(f.x), __float_as_uint(f.y), __float_as_uint(f.z), __float_as_uint(f.w));
+        }
+    } else if (want_gin) {
+        load_row_32(p.gelu_input, out_base + col, p.aux_bf16, valid, row_live, raux);
+    } else if (want_res) {
+        load_row_32(p.residual, out_base + col, OUT_BF16, valid, row_live, raux);
+    }
     tmem_load_wait();
 
 #pragma unroll
@@ -302,23 +324,63 @@ __device__ __forceinline__ void epilogue_half(const TcParams& p, uint32_t taddr,
     }
 }
 
+// Requests, on one lane, the auxiliary input of every column chunk an epilogue warp will stage for tile `u` (the
+// chunks epilogue_tile visits, box j for the j-th): one TMA load of a 32-row box per chunk into staging box j,
+// completing on aux_bar[j]. The boxes must no longer be read by earlier TMA stores.
+template <bool OUT_BF16, int BN>
+__device__ __forceinline__ void request_aux_boxes(const TcParams& p, const CUtensorMap* tm_aux, const TcUnit& u,
+                                                  int32_t row0, int group, uint8_t* boxes, uint64_t* aux_bar) {
+    constexpr int CHUNK = OUT_BF16 ? 64 : 32;
+    int j = 0;
+    for (int c = group * CHUNK; c < BN && row0 < p.M && u.n0 + c < p.N; c += 2 * CHUNK, ++j) {
+        const uint32_t bar = smem_addr(&aux_bar[j]);
+        mbar_arrive_expect_tx(bar, TC_EPI_BOX_BYTES);
+        tma_load_3d(smem_addr(boxes + j * TC_EPI_BOX_BYTES), tm_aux, bar, u.n0 + c, row0, u.batch);
+    }
+}
+
 // One epilogue warp's share of a finished accumulator tile: the column chunks c = group*CHUNK, +2*CHUNK, ... of
-// its 32 rows. Each chunk is staged in a 128-byte-row box and written by a TMA store (or reduce-add). With two boxes
-// they alternate, so staging one chunk overlaps the TMA engine's read of the previous one, and a GELU forward that
-// keeps its pre-activation writes both boxes from one TMEM read; with one box the pre-activation is staged and
-// stored first, then the output from a second TMEM read.
-template <bool OUT_BF16, int BN, int NBOX>
+// its 32 rows. Each chunk is staged in a 128-byte-row box and written by a TMA store (or reduce-add). How the boxes
+// are used is the staging mode EPI (a template parameter, so each kernel carries one path):
+//   TC_EPI_ONE_BOX   one box per warp; a kept pre-activation is staged and stored first, then the output from a
+//                    second TMEM read.
+//   TC_EPI_TWO_BOX   two boxes that alternate, so staging one chunk overlaps the TMA engine's read of the previous
+//                    one; a kept pre-activation fills both boxes from one TMEM read.
+//   TC_EPI_AUX_BOX   two boxes; chunk j's one bf16 auxiliary input (GELU input or residual, map tm_aux) was
+//                    TMA-loaded into box j by request_aux_boxes and its output overwrites it in place.
+template <bool OUT_BF16, int BN, int EPI>
 __device__ __forceinline__ void epilogue_tile(const TcParams& p, const CUtensorMap* tm_c, const CUtensorMap* tm_pre,
                                               const TcUnit& u, int32_t row0, uint32_t t_lane, int group,
-                                              uint8_t* boxes, int& ebox) {
+                                              uint8_t* boxes, int& ebox, uint64_t* aux_bar, uint32_t& aux_phase) {
     constexpr int CHUNK = OUT_BF16 ? 64 : 32;
     const int lane = threadIdx.x & 31;
     const int32_t row = row0 + lane;
     const bool first_split = u.split == 0;
     const int64_t out_base = static_cast<int64_t>(u.batch) * p.out_batch_stride + static_cast<int64_t>(row) * p.N;
-    for (int c = group * CHUNK; c < BN && row0 < p.M && u.n0 + c < p.N; c += 2 * CHUNK) {
+    int j = 0;
+    for (int c = group * CHUNK; c < BN && row0 < p.M && u.n0 + c < p.N; c += 2 * CHUNK, ++j) {
         const int32_t col0 = u.n0 + c;
-        if constexpr (NBOX == 2) {
+        if constexpr (EPI == TC_EPI_AUX_BOX) {
+            uint8_t* box = boxes + j * TC_EPI_BOX_BYTES;
+            // A timed-out wait has already set the device status; the tile is finished with whatever the box holds
+            // so that every barrier still completes.
+            mbar_wait(smem_addr(&aux_bar[j]), (aux_phase >> j) & 1u);
+            __syncwarp();
+            aux_phase ^= 1u << j;
+#pragma unroll
+            for (int h = 0; h < CHUNK / 32; ++h) {
+                float2 v[16];
+                epilogue_half<OUT_BF16>(p, t_lane + c + 32 * h, col0 + 32 * h, row, out_base, first_split, nullptr,
+                                        h, v, false, box);
+                stage_half<OUT_BF16>(box, lane, h, v);
+            }
+            fence_proxy_async_shared();
+            __syncwarp();
+            if (lane == 0) {
+                tma_store_3d(tm_c, smem_addr(box), col0, row0, u.batch);
+                bulk_commit_group();
+            }
+        } else if constexpr (EPI == TC_EPI_TWO_BOX) {
             uint8_t* box = boxes + ebox * TC_EPI_BOX_BYTES;
             uint8_t* pre_box = p.has_pre ? boxes + (ebox ^ 1) * TC_EPI_BOX_BYTES : nullptr;
             if (lane == 0) {
@@ -367,12 +429,13 @@ __device__ __forceinline__ void epilogue_tile(const TcParams& p, const CUtensorM
     }
 }
 
-template <typename E, int BN, bool OUT_BF16, int NBOX>
+template <typename E, int BN, bool OUT_BF16, int EPI>
 __global__ void __launch_bounds__(TC_THREADS, 1)
     tc_gemm_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constant__ CUtensorMap tm_b,
                    const __grid_constant__ CUtensorMap tm_c, const __grid_constant__ CUtensorMap tm_pre,
                    const __grid_constant__ CUtensorMap tm_res, const __grid_constant__ CUtensorMap tm_gin,
-                   const TcParams p) {
+                   const __grid_constant__ CUtensorMap tm_aux, const TcParams p) {
+    constexpr int NBOX = tc_epi_boxes(EPI);
     using Cfg = TcConfig<BN, NBOX>;
     constexpr int ESIZE = sizeof(E);
     constexpr int BK = 128 / ESIZE;      // K elements per ring slot (one 128-byte swizzle row)
@@ -391,7 +454,8 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
     uint64_t* acc_full = bars + 2 * Cfg::STAGES;
     uint64_t* acc_empty = acc_full + 2;
     uint64_t* drain = acc_empty + 2;
-    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
+    uint64_t* aux_bars = drain + 1;  // two per epilogue warp
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(aux_bars + 2 * TC_EPI_WARPS);
 
     const int warp = threadIdx.x >> 5;
     const int lane = threadIdx.x & 31;
@@ -406,6 +470,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
             mbar_init(smem_addr(&acc_empty[a]), TC_EPI_WARPS);  // one arrival per epilogue warp
         }
         mbar_init(smem_addr(drain), 1);
+        for (int b = 0; b < 2 * TC_EPI_WARPS; ++b) mbar_init(smem_addr(&aux_bars[b]), 1);
         fence_mbarrier_init();
         fence_proxy_async_shared();
     }
@@ -531,8 +596,16 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
         const int q = warp & 3;
         const int group = (warp - TC_EPI_WARP0) >> 2;
         uint8_t* boxes = epi + (warp - TC_EPI_WARP0) * NBOX * TC_EPI_BOX_BYTES;
+        uint64_t* aux_bar = aux_bars + 2 * (warp - TC_EPI_WARP0);
+        // The host picks TC_EPI_AUX_BOX only for bf16 outputs of products without causal skipping.
+        constexpr bool box_aux = EPI == TC_EPI_AUX_BOX;
+        uint32_t aux_phase = 0;
         int ebox = 0;
         int iter = 0;
+        if (box_aux && lane == 0 && static_cast<int32_t>(blockIdx.x) < p.num_units) {
+            const TcUnit u0 = tc_decode_unit(p, blockIdx.x, BN, BK);
+            request_aux_boxes<OUT_BF16, BN>(p, &tm_aux, u0, u0.m0 + q * 32, group, boxes, aux_bar);
+        }
         for (int32_t unit = blockIdx.x; unit < p.num_units; unit += gridDim.x) {
             const TcUnit u = tc_decode_unit(p, unit, BN, BK);
             if (u.skip) continue;
@@ -543,11 +616,21 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
             const int32_t row0 = u.m0 + q * 32;
             const uint32_t t_lane = tmem_base + (static_cast<uint32_t>(q * 32) << 16) + acc * BN;
 
-            epilogue_tile<OUT_BF16, BN, NBOX>(p, &tm_c, &tm_pre, u, row0, t_lane, group, boxes, ebox);
+            epilogue_tile<OUT_BF16, BN, EPI>(p, &tm_c, &tm_pre, u, row0, t_lane, group, boxes, ebox, aux_bar,
+                                             aux_phase);
             tcgen05_fence_before_sync();
             __syncwarp();
             if (lane == 0) mbar_arrive(smem_addr(&acc_empty[acc]));
             ++iter;
+            // The next tile's auxiliary input is requested as soon as this tile's stores have read the boxes, so
+            // its loads overlap the next main loop.
+            const int32_t next = unit + static_cast<int32_t>(gridDim.x);
+            if (box_aux && lane == 0 && next < p.num_units) {
+                bulk_wait_group_read<0>();
+                const TcUnit un = tc_decode_unit(p, next, BN, BK);
+                request_aux_boxes<OUT_BF16, BN>(p, &tm_aux, un, un.m0 + q * 32, group, boxes, aux_bar);
+            }
+            __syncwarp();
         }
         if (lane == 0) bulk_wait_group<0>();
         __syncwarp();

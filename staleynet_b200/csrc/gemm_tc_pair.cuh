@@ -20,25 +20,29 @@ namespace snb {
 constexpr int TC2_BM = 256;  // rows per CTA pair (128 per CTA)
 constexpr int TC2_BN = 256;  // columns per pair tile (128 staged per CTA)
 
+// NBOX = staging boxes per epilogue warp, as in the single-CTA kernel: two boxes (GELU epilogues) cost one ring
+// stage.
+template <int NBOX>
 struct Tc2Config {
     static constexpr int STAGE_A = 128 * 128;
     static constexpr int STAGE_B = (TC2_BN / 2) * 128;
     static constexpr int STAGE = STAGE_A + STAGE_B;
-    static constexpr int STAGES = 6;
-    static constexpr int EPI_BYTES = TC_EPI_WARPS * TC_EPI_BOX_BYTES;  // one staging box per epilogue warp
+    static constexpr int STAGES = NBOX == 2 ? 5 : 6;
+    static constexpr int EPI_BYTES = TC_EPI_WARPS * NBOX * TC_EPI_BOX_BYTES;
     static constexpr int TMEM_COLS = 2 * TC2_BN;
-    static constexpr int BARRIER_BYTES = 256;
+    static constexpr int BARRIER_BYTES = 512;
     static constexpr int SMEM_BYTES = 1024 + STAGES * STAGE + EPI_BYTES + BARRIER_BYTES;
     static_assert(SMEM_BYTES <= 232448, "shared memory budget of one sm_100 CTA");
 };
 
-template <typename E, bool OUT_BF16>
+template <typename E, bool OUT_BF16, int EPI>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(TC_THREADS, 1)
     tc_gemm_pair_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constant__ CUtensorMap tm_b,
                         const __grid_constant__ CUtensorMap tm_c, const __grid_constant__ CUtensorMap tm_pre,
                         const __grid_constant__ CUtensorMap tm_res, const __grid_constant__ CUtensorMap tm_gin,
-                        const TcParams p) {
-    using Cfg = Tc2Config;
+                        const __grid_constant__ CUtensorMap tm_aux, const TcParams p) {
+    constexpr int NBOX = tc_epi_boxes(EPI);
+    using Cfg = Tc2Config<NBOX>;
     constexpr int BN = TC2_BN;
     constexpr int ESIZE = sizeof(E);
     constexpr int BK = 128 / ESIZE;
@@ -57,7 +61,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(TC_THREADS, 1)
     uint64_t* acc_full = bars + 2 * Cfg::STAGES;
     uint64_t* acc_empty = acc_full + 2;
     uint64_t* drain = acc_empty + 2;
-    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
+    uint64_t* aux_bars = drain + 1;  // two per epilogue warp
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(aux_bars + 2 * TC_EPI_WARPS);
 
     const int warp = threadIdx.x >> 5;
     const int lane = threadIdx.x & 31;
@@ -76,6 +81,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(TC_THREADS, 1)
             mbar_init(smem_addr(&acc_empty[a]), 2 * TC_EPI_WARPS);  // every epilogue warp of both CTAs
         }
         mbar_init(smem_addr(drain), 1);
+        for (int b = 0; b < 2 * TC_EPI_WARPS; ++b) mbar_init(smem_addr(&aux_bars[b]), 1);
         fence_mbarrier_init();
         fence_proxy_async_shared();
     }
@@ -197,23 +203,39 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(TC_THREADS, 1)
         // ------------------------------------------------------------------ epilogue (both CTAs)
         const int q = warp & 3;
         const int group = (warp - TC_EPI_WARP0) >> 2;
-        uint8_t* boxes = epi + (warp - TC_EPI_WARP0) * TC_EPI_BOX_BYTES;
+        uint8_t* boxes = epi + (warp - TC_EPI_WARP0) * NBOX * TC_EPI_BOX_BYTES;
+        uint64_t* aux_bar = aux_bars + 2 * (warp - TC_EPI_WARP0);
+        constexpr bool box_aux = EPI == TC_EPI_AUX_BOX;
+        const int32_t row_off = 128 * static_cast<int32_t>(rank) + q * 32;  // this warp's rows within a pair tile
+        uint32_t aux_phase = 0;
         int ebox = 0;
         int iter = 0;
+        if (box_aux && lane == 0 && first_unit < p.num_units) {
+            const TcUnit u0 = tc_decode_unit(p, first_unit, BN, BK, TC2_BM);
+            request_aux_boxes<OUT_BF16, BN>(p, &tm_aux, u0, u0.m0 + row_off, group, boxes, aux_bar);
+        }
         for (int32_t unit = first_unit; unit < p.num_units; unit += unit_step) {
             const TcUnit u = tc_decode_unit(p, unit, BN, BK, TC2_BM);
             const int acc = iter & 1;
             const uint32_t acc_phase = (iter >> 1) & 1;
             if (!mbar_wait_cluster(smem_addr(&acc_full[acc]), acc_phase)) break;
             tcgen05_fence_after_sync();
-            const int32_t row0 = u.m0 + 128 * static_cast<int32_t>(rank) + q * 32;
+            const int32_t row0 = u.m0 + row_off;
             const uint32_t t_lane = tmem_base + (static_cast<uint32_t>(q * 32) << 16) + acc * BN;
 
-            epilogue_tile<OUT_BF16, BN, 1>(p, &tm_c, &tm_pre, u, row0, t_lane, group, boxes, ebox);
+            epilogue_tile<OUT_BF16, BN, EPI>(p, &tm_c, &tm_pre, u, row0, t_lane, group, boxes, ebox, aux_bar,
+                                             aux_phase);
             tcgen05_fence_before_sync();
             __syncwarp();
             if (lane == 0) mbar_arrive_cluster(map_to_cta(smem_addr(&acc_empty[acc]), 0));
             ++iter;
+            const int32_t next = unit + unit_step;
+            if (box_aux && lane == 0 && next < p.num_units) {
+                bulk_wait_group_read<0>();
+                const TcUnit un = tc_decode_unit(p, next, BN, BK, TC2_BM);
+                request_aux_boxes<OUT_BF16, BN>(p, &tm_aux, un, un.m0 + row_off, group, boxes, aux_bar);
+            }
+            __syncwarp();
         }
         if (lane == 0) bulk_wait_group<0>();
         __syncwarp();

@@ -287,6 +287,43 @@ def test_fused_gelu_backward_epilogue(gpu):
     assert o.relative_error(expected, out.cpu().numpy()) < 1e-4
 
 
+@pytest.mark.parametrize("kind", ["gelu_grad", "bias_residual"])
+@pytest.mark.parametrize("rows,cols,inner,batch", [(384, 520, 256, 1), (384, 520, 2048, 1), (200, 136, 96, 1),
+                                                   (130, 72, 64, 1), (260, 264, 128, 2)])
+def test_bf16_auxiliary_input_staged_by_tma(gpu, kind, rows, cols, inner, batch):
+    """bf16 outputs whose one bf16 auxiliary input (the GELU input of project.backward's dX product, or a block's
+    residual) is TMA-loaded into the epilogue's staging boxes: single-CTA and CTA-pair tiles, ragged tile edges
+    (rows, and columns not a multiple of the 64-column chunk), and a batch of two."""
+    T, n, k = rows, cols, inner
+    x = o.lcg_values(batch * T * k, 81)
+    w = o.lcg_values(batch * k * n, 82) * 0.05
+    b = o.lcg_values(n, 83)
+    aux = o.lcg_values(batch * T * n, 84) * 2
+    xb, _ = o.round_bf16(x)
+    wb, _ = o.round_bf16(w)
+    auxb, _ = o.round_bf16(aux)
+    spec = MatmulSpec.new(T, n, k)
+    if batch > 1:
+        spec = spec.batched(BatchStrides(count=batch, left=T * k, right=k * n, output=T * n))
+    acc = np.zeros(batch * T * n, np.float32)
+    o.matmul(to_oracle(spec), batch, xb, wb, acc)
+    xt, wt = torch.from_numpy(x).cuda().bfloat16(), torch.from_numpy(w).cuda().bfloat16()
+    at = torch.from_numpy(aux).cuda().bfloat16()
+    out = torch.empty(batch * T * n, device="cuda", dtype=torch.bfloat16)
+    if kind == "gelu_grad":
+        gpu.gemm(spec, xt, wt, out, activation=_ffi.ACTIVATION_GELU_GRAD, gelu_input=at)
+        expected = acc * o.gelu_derivative(auxb)
+    else:
+        gpu.gemm(spec, xt, wt, out, bias=torch.from_numpy(b).cuda(), residual=at)
+        expected = acc + np.tile(b, batch * T) + auxb
+    assert _ffi.last_path() in _ffi.TENSOR_CORE_PATHS
+    if k >= 2048:
+        assert _ffi.last_path() == _ffi.PATH_TENSOR_CORE_PAIR
+    torch.cuda.synchronize()
+    assert o.relative_error(expected, out.float().cpu().numpy()) < 1e-2
+    gpu.device_status()
+
+
 def test_undersized_operands_raise_like_the_reference(gpu):
     gpu.matmul_kernel = MatmulKernel.TENSOR_CORE
     a = torch.zeros(23, device="cuda")
