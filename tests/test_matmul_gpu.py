@@ -324,6 +324,34 @@ def test_bf16_auxiliary_input_staged_by_tma(gpu, kind, rows, cols, inner, batch)
     gpu.device_status()
 
 
+@pytest.mark.parametrize("out_dtype", ["f32", "bf16"])
+@pytest.mark.parametrize("rows,cols,inner,batch", [(130, 264, 104, 1), (257, 520, 256, 3), (300, 392, 2048, 1)])
+def test_overwritten_outputs_at_ragged_tile_edges(gpu, out_dtype, rows, cols, inner, batch):
+    """Products that overwrite C (no accumulation) on 256-column tiles, whose epilogue warps write the staged boxes
+    to global memory themselves: ragged rows and columns, batches, single-CTA and CTA-pair tiles; C's other
+    elements (past each matrix's end in the batch stride) stay untouched."""
+    T, n, k = rows, cols, inner
+    gap = 48  # output batch stride = T * n + gap
+    x = o.lcg_values(batch * T * k, 91)
+    w = o.lcg_values(batch * k * n, 92) * 0.05
+    xb, _ = o.round_bf16(x)
+    wb, _ = o.round_bf16(w)
+    spec = MatmulSpec.new(T, n, k).batched(BatchStrides(count=batch, left=T * k, right=k * n, output=T * n + gap))
+    odt = torch.bfloat16 if out_dtype == "bf16" else torch.float32
+    out = torch.full((batch * (T * n + gap),), 7.0, device="cuda", dtype=odt)
+    expected = np.full(batch * (T * n + gap), 7.0, np.float32)
+    o.matmul(to_oracle(spec), batch, xb, wb, expected)
+    gpu.gemm(spec, torch.from_numpy(x).cuda().bfloat16(), torch.from_numpy(w).cuda().bfloat16(), out)
+    assert _ffi.last_path() in _ffi.TENSOR_CORE_PATHS
+    torch.cuda.synchronize()
+    got = out.float().cpu().numpy()
+    tol = 1e-2 if out_dtype == "bf16" else 1e-5
+    assert o.relative_error(expected, got) < tol
+    for b in range(batch):  # the gaps between matrices keep their initial value exactly
+        assert np.all(got[b * (T * n + gap) + T * n:(b + 1) * (T * n + gap)] == 7.0)
+    gpu.device_status()
+
+
 def test_undersized_operands_raise_like_the_reference(gpu):
     gpu.matmul_kernel = MatmulKernel.TENSOR_CORE
     a = torch.zeros(23, device="cuda")
