@@ -34,6 +34,7 @@ sys.path.insert(0, str(ROOT))
 METRIC = "GEMM TFLOP/s (fwd+bwd) & % bf16 tensor peak at 1/2/4/8 B200 vs host-CPU ref"
 UNIT = "TFLOP/s"
 FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}
+GENERATOR = "the reference's generator (SplitMix64 + Box-Muller, random.rs:27-70, seed = rank) drawn on the device"
 
 
 def load_peaks():
@@ -364,8 +365,8 @@ def run_ours(args, shape, rank: int, world: int, local_rank: int) -> int:
         line = {
             "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": ms_step, "higher_is_better": True, "scaling": "weak",
-            "vs_baseline": None, "dtype": "bf16", "data": "synthetic (seeded N(0,1) activations, N(0,1/sqrt(768)) "
-                                                           "weights, torch generator)",
+            "vs_baseline": None, "dtype": "bf16", "data": "synthetic: " + GENERATOR + "; activations "
+                                                           "N(0,1), weights N(0,1/sqrt(768))",
             "config": workload_config(shape, world),
             "pct_bf16_peak_sustained": 100.0 * (value / world) / peak_sus,
             "pct_bf16_peak_burst": 100.0 * (value / world) / peak_burst,
@@ -464,22 +465,20 @@ def run_head(args, rank: int, world: int, local_rank: int) -> int:
     losses summed on the host. `value` counts the head GEMM's FLOPs either way."""
     import torch
 
-    from staleynet_b200 import _ffi
-    from staleynet_b200.matmul import CrossEntropyHead, Gpu, MatmulSpec
+    from staleynet_b200.matmul import CrossEntropyHead, DeviceRandom, Gpu, MatmulSpec
 
     torch.cuda.set_device(local_rank)
     device = torch.device("cuda", local_rank)
     stream = torch.cuda.current_stream(device)
     tokens, width, books, size = args.tokens, 768, 16, 1024
     cols = books * size
-    g = torch.Generator(device=device)
-    g.manual_seed(rank)
-    x = torch.randn(tokens, width, device=device, generator=g).bfloat16()
-    w = (torch.randn(width, cols, device=device, generator=g) / width ** 0.5).bfloat16()
-    bias = torch.zeros(cols, device=device)
-    targets = torch.randint(0, size, (tokens, books), device=device, generator=g, dtype=torch.int32)
-    scales = torch.full((books,), 1.0 / (tokens * books), device=device)
     gpu = Gpu(local_rank)
+    rng = DeviceRandom(gpu, rank)
+    x = rng.normal_(torch.empty(tokens, width, device=device, dtype=torch.bfloat16))
+    w = rng.normal_(torch.empty(width, cols, device=device, dtype=torch.bfloat16), 1.0 / width ** 0.5)
+    bias = torch.zeros(cols, device=device)
+    targets = rng.below_(torch.empty(tokens, books, device=device, dtype=torch.int32), size)
+    scales = torch.full((books,), 1.0 / (tokens * books), device=device)
     spec = MatmulSpec.new(tokens, cols, width)
     fused = args.head_path == "fused"
     host_sums = torch.empty(books, dtype=torch.float32, pin_memory=True)
@@ -541,7 +540,7 @@ def run_head(args, rank: int, world: int, local_rank: int) -> int:
     line = {
         "metric": METRIC, "value": flops / (ms / 1e3) / 1e12, "unit": UNIT, "n_gpus": 1, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
-        "dtype": "bf16", "data": "synthetic (seeded N(0,1) activations, N(0, 1/768) weights, uniform targets)",
+        "dtype": "bf16", "data": "synthetic: " + GENERATOR + "; activations N(0,1), weights N(0,1/sqrt(768)), targets below(1024)",
         "config": {"workload": "cfg3 output layer forward + loss: 65,536 tokens x 768 -> 16 codebooks x 1024, "
                                "softmax cross-entropy with gradient, loss on the host",
                    "head_path": args.head_path, "tokens": tokens, "width": width, "codebooks": books,
@@ -593,22 +592,21 @@ def run_optimizer(args, rank: int, world: int, local_rank: int) -> int:
     tensor snb_sum_of_squares and a host read of it, then per tensor the gradient scaled and snb_adamw_step."""
     import torch
 
-    from staleynet_b200.matmul import AdamWHyperparameters, Gpu
+    from staleynet_b200.matmul import AdamWHyperparameters, DeviceRandom, Gpu
     from staleynet_b200.step import ModelShape
 
     torch.cuda.set_device(local_rank)
     device = torch.device("cuda", local_rank)
     stream = torch.cuda.current_stream(device)
     shapes = model_parameter_shapes(ModelShape())
-    g = torch.Generator(device=device)
-    g.manual_seed(rank)
+    gpu = Gpu(local_rank)
+    rng = DeviceRandom(gpu, rank)
     tensors = []
     for _, n, decayed in shapes:
-        p = torch.randn(n, device=device, generator=g) * 0.02
-        grad = torch.randn(n, device=device, generator=g) * 1e-3
+        p = rng.normal_(torch.empty(n, device=device), 0.02)
+        grad = rng.normal_(torch.empty(n, device=device), 1e-3)
         tensors.append((p, grad, torch.zeros(n, device=device), torch.zeros(n, device=device), 0.1 if decayed else 0.0))
     elements = sum(n for _, n, _ in shapes)
-    gpu = Gpu(local_rank)
     multi = args.optimizer_path == "multi"
     square_sum = torch.zeros(1, device=device, dtype=torch.float64)
     host = torch.empty(1, dtype=torch.float64, pin_memory=True)
@@ -654,7 +652,7 @@ def run_optimizer(args, rank: int, world: int, local_rank: int) -> int:
     line = {
         "metric": "optimizer step (global norm + clip + AdamW) time", "value": ms, "unit": "ms",
         "n_gpus": 1, "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": False,
-        "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic (seeded parameters and gradients)",
+        "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic: " + GENERATOR + "; parameters N(0,0.02), gradients N(0,1e-3)",
         "config": {"workload": "cfg3 model optimizer step: 111.5 M f32 parameters in "
                                f"{len(shapes)} tensors, gradient-norm clip at 1.0, AdamW", "optimizer_path":
                    args.optimizer_path, "parameters": elements, "tensors": len(shapes),
@@ -677,21 +675,20 @@ def run_norm(args, rank: int, world: int, local_rank: int) -> int:
     gain folded into the weights; --norm-path unfused: the normalised rows written as bf16, then the GEMM."""
     import torch
 
-    from staleynet_b200.matmul import Gpu, MatmulSpec
+    from staleynet_b200.matmul import DeviceRandom, Gpu, MatmulSpec
 
     torch.cuda.set_device(local_rank)
     device = torch.device("cuda", local_rank)
     stream = torch.cuda.current_stream(device)
     tokens, width, cols, eps = args.tokens, 768, 2304, 1e-5
-    g = torch.Generator(device=device)
-    g.manual_seed(rank)
-    x = torch.randn(tokens, width, device=device, generator=g).bfloat16()
-    gain = 1.0 + 0.1 * torch.randn(width, device=device, generator=g)
-    w = (torch.randn(width, cols, device=device, generator=g) / width ** 0.5).bfloat16()
+    gpu = Gpu(local_rank)
+    rng = DeviceRandom(gpu, rank)
+    x = rng.normal_(torch.empty(tokens, width, device=device, dtype=torch.bfloat16))
+    gain = 1.0 + rng.normal_(torch.empty(width, device=device), 0.1)
+    w = rng.normal_(torch.empty(width, cols, device=device, dtype=torch.bfloat16), 1.0 / width ** 0.5)
     bias = torch.zeros(cols, device=device)
     y = torch.empty(tokens, cols, device=device, dtype=torch.bfloat16)
     inv = torch.empty(tokens, device=device)
-    gpu = Gpu(local_rank)
     spec = MatmulSpec.new(tokens, cols, width)
     fused = args.norm_path == "fused"
     wg = torch.empty_like(w)
@@ -727,7 +724,7 @@ def run_norm(args, rank: int, world: int, local_rank: int) -> int:
     line = {
         "metric": METRIC, "value": flops / (ms / 1e3) / 1e12, "unit": UNIT, "n_gpus": 1, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
-        "dtype": "bf16", "data": "synthetic (seeded N(0,1) rows, gains near 1)",
+        "dtype": "bf16", "data": "synthetic: " + GENERATOR + "; rows N(0,1), gains 1 + N(0,0.1), weights N(0,1/sqrt(768))",
         "config": {"workload": "cfg3 RMSNorm + QKV product: 65,536 x 768 -> 2304", "norm_path": args.norm_path,
                    "tokens": tokens, "l2": "inputs larger than L2 (y: 302 MB bf16)"},
         "roofline": {"bound": "tensor", "kernel": "tc_gemm_kernel with row_scale (+ rms statistics)",
@@ -826,7 +823,7 @@ def run_attention(args, rank: int, world: int, local_rank: int) -> int:
     line = {
         "metric": METRIC, "value": att.flops / sec / 1e12, "unit": UNIT, "n_gpus": 1, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": ms / args.steps, "higher_is_better": True, "scaling": "weak",
-        "vs_baseline": None, "dtype": "bf16", "data": "synthetic (seeded N(0,1) bf16 Q/K/V/dO)",
+        "vs_baseline": None, "dtype": "bf16", "data": "synthetic: " + GENERATOR + "; Q, K, V, dO N(0,1) in bf16",
         "config": {"workload": workload, "attention_path": args.attention_path,
                    "batch": shape.batch, "heads": shape.heads, "head_dim": shape.head_dim, "seq_len": shape.time,
                    "flops": "causal (visible query-key pairs) count of the six products", "l2": l2},

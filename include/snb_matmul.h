@@ -344,6 +344,20 @@ SNB_API int snb_sum_of_squares(void* stream, const float* values, uint64_t count
 SNB_API int snb_adamw_step_multi(void* stream, const snb_adamw_tensor* tensors, uint64_t tensor_count,
                                  const snb_adamw_hyper* hyper, float max_gradient_norm, double* gradient_square_sum);
 
+/* Seeded inputs on the device, the reference's generator (`Random`, crates/staleynet-model/src/random.rs:27-70):
+ * SplitMix64 whose k-th draw (k = 1, 2, ...) from Random::new(seed) is its output for state seed + k * 0x9E3779B97F4A7C15.
+ * output[i] = std * normal() computed from draws first_draw + 2i + 1 and + 2 (random.rs:64-68, two draws per value),
+ * i.e. what `Init::Normal(std)` (parameter.rs:54) writes from a Random that has already made first_draw draws; a
+ * following fill continues at first_draw + 2 * count. output_type SNB_TYPE_F32, or SNB_TYPE_BF16 (the f32 value
+ * rounded to nearest even). The device's logf / cosf may differ from the host libm's in an f32's last bit. No
+ * reference counterpart as a device call. */
+SNB_API int snb_random_normal(void* stream, void* output, int32_t output_type, uint64_t count, uint64_t seed,
+                              uint64_t first_draw, float std);
+
+/* output[i] = `Random::below(bound)` (random.rs:54-56) from draw first_draw + i + 1 (one draw per value). */
+SNB_API int snb_random_below(void* stream, uint32_t* output, uint64_t count, uint64_t seed, uint64_t first_draw,
+                             uint64_t bound);
+
 /* Failure-detection self-test: launches a one-thread kernel that waits on an mbarrier nothing completes, through
  * the bounded wait every tensor-core pipeline wait uses. The wait gives up after limit_ns (at most 1 s), records a
  * timeout in the device status word and the kernel returns normally; a following snb_device_status() reports

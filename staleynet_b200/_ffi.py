@@ -68,6 +68,8 @@ EXPORTED_SYMBOLS = (
     "snb_adamw_step",
     "snb_sum_of_squares",
     "snb_adamw_step_multi",
+    "snb_random_normal",
+    "snb_random_below",
     "snb_selftest_bounded_wait",
     "snb_abi_version",
 )
@@ -205,8 +207,11 @@ def load() -> ctypes.CDLL:
         lib.snb_sum_of_squares.argtypes = [c_void_p, c_void_p, c_uint64, c_void_p]
         lib.snb_adamw_step_multi.argtypes = [c_void_p, POINTER(AdamWTensor), c_uint64, POINTER(AdamWHyper), c_float,
                                              c_void_p]
+        lib.snb_random_normal.argtypes = [c_void_p, c_void_p, c_int32, c_uint64, c_uint64, c_uint64, c_float]
+        lib.snb_random_below.argtypes = [c_void_p, c_void_p, c_uint64, c_uint64, c_uint64, c_uint64]
         for name in ("snb_rms_norm_forward", "snb_rms_norm_backward", "snb_rms_norm_stats", "snb_scale_rows",
-                     "snb_adamw_step", "snb_sum_of_squares", "snb_adamw_step_multi"):
+                     "snb_adamw_step", "snb_sum_of_squares", "snb_adamw_step_multi", "snb_random_normal",
+                     "snb_random_below"):
             getattr(lib, name).restype = c_int
         lib.snb_selftest_bounded_wait.argtypes = [c_void_p, c_uint64]
         lib.snb_selftest_bounded_wait.restype = c_int

@@ -21,7 +21,7 @@ import ctypes
 from dataclasses import dataclass
 
 from . import _ffi
-from .matmul import BatchStrides, MatmulSpec, check
+from .matmul import BatchStrides, DeviceRandom, Gpu, MatmulSpec, check
 
 
 @dataclass(frozen=True)
@@ -78,11 +78,11 @@ class AttentionProducts:
         self.shape = s
         self.lib = _ffi.load()
         n, S, d = s.count, s.time, s.head_dim
-        gen = torch.Generator(device=device)
-        gen.manual_seed(seed)
+        # Q, K, V and dO from the reference's generator (Random::new(seed), random.rs:27-70), drawn on the device.
+        rng = DeviceRandom(Gpu(device.index if device.index is not None else 0), seed)
 
         def normal(numel):
-            return torch.randn(numel, generator=gen, device=device, dtype=torch.float32).to(torch.bfloat16)
+            return rng.normal_(torch.empty(numel, device=device, dtype=torch.bfloat16))
 
         bf16, f32 = torch.bfloat16, torch.float32
         self.q, self.k, self.v, self.d_out = (normal(n * S * d) for _ in range(4))
@@ -176,16 +176,14 @@ class FusedAttention:
     def __init__(self, shape: AttentionShape, device, seed: int = 0):
         import torch
 
-        from .matmul import Gpu
-
         s = shape
         self.shape = s
         n, S, d = s.count, s.time, s.head_dim
-        gen = torch.Generator(device=device)
-        gen.manual_seed(seed)
+        # Q, K, V and dO from the reference's generator (Random::new(seed), random.rs:27-70), drawn on the device.
+        rng = DeviceRandom(Gpu(device.index if device.index is not None else 0), seed)
 
         def normal():
-            return torch.randn(n, S, d, generator=gen, device=device, dtype=torch.float32).to(torch.bfloat16)
+            return rng.normal_(torch.empty(n, S, d, device=device, dtype=torch.bfloat16))
 
         self.q, self.k, self.v, self.d_out = (normal() for _ in range(4))
         self.out = torch.empty(n, S, d, device=device, dtype=torch.float32)

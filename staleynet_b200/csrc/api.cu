@@ -110,7 +110,7 @@ using namespace snb;
 
 extern "C" {
 
-int snb_abi_version(void) { return 101; }
+int snb_abi_version(void) { return 102; }
 
 const char* snb_last_error(void) { return t_last_error.c_str(); }
 
@@ -425,6 +425,32 @@ int snb_adamw_step(void* stream, float* parameter, const float* gradient, float*
     std::string err;
     int rc = adamw_launch(static_cast<cudaStream_t>(stream), parameter, gradient, first_moment, second_moment, count,
                           *hyper, &err);
+    if (rc != SNB_OK) return fail(rc, err);
+    t_last_path = SNB_PATH_SIMT;
+    return SNB_OK;
+}
+
+int snb_random_normal(void* stream, void* output, int32_t output_type, uint64_t count, uint64_t seed,
+                      uint64_t first_draw, float std) {
+    t_last_path = SNB_PATH_NONE;
+    if (count > 0 && output == nullptr) return fail(SNB_ERR_INVALID_ARGUMENT, "random_normal: null output");
+    if (output_type != SNB_TYPE_F32 && output_type != SNB_TYPE_BF16)
+        return fail(SNB_ERR_INVALID_ARGUMENT, "random_normal: output_type must be SNB_TYPE_F32 or SNB_TYPE_BF16");
+    std::string err;
+    int rc = random_normal_launch(static_cast<cudaStream_t>(stream), output, output_type, count, seed, first_draw, std,
+                                  &err);
+    if (rc != SNB_OK) return fail(rc, err);
+    t_last_path = SNB_PATH_SIMT;
+    return SNB_OK;
+}
+
+int snb_random_below(void* stream, uint32_t* output, uint64_t count, uint64_t seed, uint64_t first_draw,
+                     uint64_t bound) {
+    t_last_path = SNB_PATH_NONE;
+    if (count > 0 && output == nullptr) return fail(SNB_ERR_INVALID_ARGUMENT, "random_below: null output");
+    if (bound == 0) return fail(SNB_ERR_INVALID_ARGUMENT, "random_below: bound must be positive");
+    std::string err;
+    int rc = random_below_launch(static_cast<cudaStream_t>(stream), output, count, seed, first_draw, bound, &err);
     if (rc != SNB_OK) return fail(rc, err);
     t_last_path = SNB_PATH_SIMT;
     return SNB_OK;

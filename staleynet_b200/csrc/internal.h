@@ -98,4 +98,11 @@ int read_and_clear_device_status(unsigned int* status, std::string* err);
 
 std::string cuda_message(const char* what, cudaError_t e);
 
+// The reference's seeded stream on the device (random.cu): normal values (f32 or bf16 output) and below(bound)
+// integers from draw first_draw + 1 on.
+int random_normal_launch(cudaStream_t s, void* out, int out_type, uint64_t count, uint64_t seed, uint64_t first_draw,
+                         float stddev, std::string* err);
+int random_below_launch(cudaStream_t s, uint32_t* out, uint64_t count, uint64_t seed, uint64_t first_draw,
+                        uint64_t bound, std::string* err);
+
 }  // namespace snb

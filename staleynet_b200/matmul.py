@@ -339,6 +339,31 @@ class Gpu:
         check(self.lib.snb_adamw_step(self._stream_handle(), _ptr(parameter), _ptr(gradient), _ptr(first_moment),
                                       _ptr(second_moment), parameter.numel(), ctypes.byref(h)))
 
+    def random_normal(self, output, seed: int, first_draw: int = 0, std: float = 1.0) -> int:
+        """snb_random_normal: `output` (f32 or bf16) = std * normal() of the reference's `Random::new(seed)` after
+        `first_draw` draws (random.rs:27-70, two draws per value). Returns the draw count after the fill."""
+        import torch
+
+        _require_cuda(output)
+        if output.dtype not in (torch.float32, torch.bfloat16):
+            raise SnbError(_ffi.ERR_INVALID_ARGUMENT, "random_normal: output must be float32 or bfloat16")
+        out_type = _ffi.TYPE_BF16 if output.dtype == torch.bfloat16 else _ffi.TYPE_F32
+        check(self.lib.snb_random_normal(self._stream_handle(), _ptr(output), out_type, output.numel(),
+                                         seed & 0xFFFFFFFFFFFFFFFF, first_draw, std))
+        return first_draw + 2 * output.numel()
+
+    def random_below(self, output, bound: int, seed: int, first_draw: int = 0) -> int:
+        """snb_random_below: `output` (int32, read as uint32) = `Random::below(bound)` of `Random::new(seed)` after
+        `first_draw` draws (random.rs:54-56). Returns the draw count after the fill."""
+        import torch
+
+        _require_cuda(output)
+        if output.dtype != torch.int32:
+            raise SnbError(_ffi.ERR_INVALID_ARGUMENT, "random_below: output must be int32")
+        check(self.lib.snb_random_below(self._stream_handle(), _ptr(output), output.numel(),
+                                        seed & 0xFFFFFFFFFFFFFFFF, first_draw, bound))
+        return first_draw + output.numel()
+
     def sum_of_squares(self, values, result) -> None:
         """snb_sum_of_squares into a one-element float64 device tensor."""
         _require_cuda(values, result)
@@ -441,3 +466,22 @@ class Gpu:
 
 def last_path() -> int:
     return _ffi.last_path()
+
+
+class DeviceRandom:
+    """The reference's `Random::new(seed)` (crates/staleynet-model/src/random.rs:27-70) as a draw counter over the
+    device fills: `normal_` and `below_` write what the same sequence of `Init::Normal(std)` / `below(bound)` calls
+    would produce on the host, and advance the counter by the draws they consume."""
+
+    def __init__(self, gpu: "Gpu", seed: int):
+        self.gpu = gpu
+        self.seed = seed
+        self.draws = 0
+
+    def normal_(self, output, std: float = 1.0):
+        self.draws = self.gpu.random_normal(output, self.seed, self.draws, std)
+        return output
+
+    def below_(self, output, bound: int):
+        self.draws = self.gpu.random_below(output, bound, self.seed, self.draws)
+        return output

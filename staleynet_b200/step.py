@@ -25,7 +25,7 @@ from dataclasses import dataclass
 
 from . import _ffi
 from .data_parallel import GradientBuckets
-from .matmul import MatmulSpec, check
+from .matmul import DeviceRandom, Gpu, MatmulSpec, check
 
 
 @dataclass(frozen=True)
@@ -69,12 +69,13 @@ class TrainingStepGemms:
         self.lib = _ffi.load()
         s = shape
         T, w, f, V = s.tokens, s.width, s.ffn, s.head_width
-        gen = torch.Generator(device=device)
-        gen.manual_seed(seed)
         bf16, f32 = torch.bfloat16, torch.float32
+        # Inputs and weights come from the reference's generator (Random::new(seed), random.rs:27-70), drawn on the
+        # device in the order they are created here.
+        rng = DeviceRandom(Gpu(device.index if device.index is not None else 0), seed)
 
         def normal(n, std, dtype=bf16):
-            return (torch.randn(n, generator=gen, device=device, dtype=f32) * std).to(dtype)
+            return rng.normal_(torch.empty(n, device=device, dtype=dtype), std)
 
         wstd = 1.0 / (w ** 0.5)
         self.weights = []

@@ -71,7 +71,7 @@ def test_library_loads_and_exports_every_declared_symbol():
     for name in declared:
         assert hasattr(lib, name), f"{name} declared in the header but not exported"
     assert sorted(_ffi.EXPORTED_SYMBOLS) == declared
-    assert lib.snb_abi_version() == 101
+    assert lib.snb_abi_version() == 102
 
 
 def call_matmul(rows, cols, inner, left_len, right_len, output_len, count=1, precision=_ffi.PRECISION_F32):
