@@ -203,6 +203,12 @@ def cpu_baseline(shape, budget_flops: float = 20e9, threads: int = 0) -> dict:
             "seconds_per_step_extrapolated": seconds_full}
 
 
+def single_thread_baseline(shape, budget_flops: float) -> dict:
+    """The reference-faithful form of the CPU baseline: the same loop on one thread, as reference::matmul runs."""
+    r = cpu_baseline(shape, budget_flops=budget_flops, threads=1)
+    return {"value": r["value"], "unit": r["unit"], "cores": r["cores"], "sample": r["sample"]}
+
+
 # ------------------------------------------------------------------------------------------------ main paths
 def run_reference(args, shape, rank: int, world: int) -> int:
     if rank != 0:
@@ -223,7 +229,8 @@ def run_reference(args, shape, rank: int, world: int) -> int:
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": statistics.median(secs) * 1e3,
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
         "config": workload_config(shape, args.gpus),
-        "cpu_baseline": {"value": value, "unit": UNIT, "cores": r["cores"], "kind": "port", "sample": r["sample"]},
+        "cpu_baseline": {"value": value, "unit": UNIT, "cores": r["cores"], "kind": "port", "sample": r["sample"],
+                         "single_thread": single_thread_baseline(shape, args.cpu_sample_flops / 20)},
         "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
         "note": "CPU restatement of reference::matmul (crates/staleynet-cuda/src/reference.rs:18-38); the "
                 "reference's Rust CPU path cannot be built here (no Rust toolchain)",
@@ -351,6 +358,7 @@ def run_ours(args, shape, rank: int, world: int, local_rank: int) -> int:
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         cpu = cpu_baseline(shape, budget_flops=args.cpu_sample_flops)
+        cpu["single_thread"] = single_thread_baseline(shape, args.cpu_sample_flops / 20)
 
     if rank == 0:
         peaks, source = load_peaks()
