@@ -113,10 +113,25 @@ class OverlappedAllReduce:
             self.side.wait_event(ready)
             self.works.append(dist.all_reduce(tensor, group=self.group, async_op=True))
 
-    def wait(self) -> None:
-        for w in self.works:
-            w.wait()
-        self.works = []
+    def wait(self, timeout_s: float | None = None) -> None:
+        """Waits for every submitted all-reduce. With `timeout_s`, one that has not completed by then (a peer
+        stopped taking part) raises CollectiveFailed instead of blocking: the caller then tears the process group
+        down, since its communicator may still hold the collective."""
+        import datetime
+
+        works, self.works = self.works, []
+        try:
+            for w in works:
+                if timeout_s is None:
+                    w.wait()
+                else:
+                    w.wait(datetime.timedelta(seconds=timeout_s))
+        except Exception as e:  # the backend raises its own error types for a timed-out or aborted collective
+            raise CollectiveFailed(f"gradient all-reduce not complete within {timeout_s} s: {e}") from e
+
+
+class CollectiveFailed(RuntimeError):
+    """A gradient all-reduce did not complete within its deadline."""
 
 
 class PeerLost(RuntimeError):

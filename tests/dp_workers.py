@@ -88,3 +88,38 @@ def heartbeat_detects_a_departed_rank(rank, world, port, result_queue):
         result_queue.put(("peer lost", str(e)))
     result_queue.close()
     result_queue.join_thread()  # deliver the result before this process ends
+
+
+def collective_deadline_is_an_error(rank, world, port, result_queue):
+    """Step 0's all-reduce completes on both ranks; in step 1 rank 1 takes no part, and rank 0's bounded wait turns
+    the missing peer into CollectiveFailed after its deadline instead of blocking."""
+    import time
+
+    import torch
+    import torch.distributed as dist
+
+    from staleynet_b200.data_parallel import CollectiveFailed, OverlappedAllReduce
+
+    _init(rank, world, port)
+    store = dist.distributed_c10d._get_default_store()
+    try:
+        reducer = OverlappedAllReduce()
+        t = torch.full((1024,), float(rank + 1))
+        reducer.submit(t)
+        reducer.wait(timeout_s=20.0)
+        assert float(t[0]) == 3.0
+        if rank == 1:
+            store.wait(["snb/test/done"], datetime.timedelta(seconds=60))   # stays alive, joins nothing
+            return
+        reducer.submit(torch.ones(1024))
+        t0 = time.time()
+        try:
+            reducer.wait(timeout_s=2.0)
+            result_queue.put(("no error", time.time() - t0))
+        except CollectiveFailed as e:
+            result_queue.put(("collective failed", time.time() - t0, str(e)[:80]))
+        finally:
+            store.set("snb/test/done", "1")
+    except Exception as e:  # noqa: BLE001
+        result_queue.put(("error", repr(e)))
+        raise

@@ -61,3 +61,9 @@ def test_the_heartbeat_reports_a_rank_that_left_between_steps():
     (status, detail), = run_ranks(dp_workers.heartbeat_detects_a_departed_rank, timeout=60)
     assert status == "peer lost", detail
     assert "snb/ready/1/1" in detail
+
+
+def test_a_collective_past_its_deadline_is_an_error_not_a_hang():
+    (status, seconds, *detail), = run_ranks(dp_workers.collective_deadline_is_an_error, timeout=90)
+    assert status == "collective failed", (status, detail)
+    assert seconds < 30, seconds
