@@ -66,6 +66,13 @@ def load_profile_traffic(summary: str, kernel: str):
     return None if entry is None else entry.get("dram_bytes")
 
 
+def profile_traffic_sum(summary: str, kernels) -> float | None:
+    """Sum of the per-launch DRAM bytes of `kernels` in profiles/<summary> (one launch of each per step); None when
+    any is missing."""
+    parts = [load_profile_traffic(summary, k) for k in kernels]
+    return None if any(x is None for x in parts) else float(sum(parts))
+
+
 def load_kernel_traffic(kernel: str):
     """A fused-attention kernel's DRAM bytes per launch at BASELINE config 4."""
     return load_profile_traffic("fused_attention_cfg4_kernels.json", kernel)
@@ -668,7 +675,10 @@ def run_optimizer(args, rank: int, world: int, local_rank: int) -> int:
         "roofline": {"bound": "hbm", "kernel": "multi_adamw_kernel + multi_sum_of_squares_kernel" if multi else
                      "sum_of_squares_kernel + adamw_kernel per tensor",
                      "achieved": algorithmic / (ms / 1e3) / 1e9, "peak": hbm, "unit": "GB/s",
-                     "frac": algorithmic / (ms / 1e3) / 1e9 / hbm, "traffic": None,
+                     "frac": algorithmic / (ms / 1e3) / 1e9 / hbm,
+                     "traffic": profile_traffic_sum("norm_optim_cfg3_kernels.json",
+                                                    ("multi_adamw_kernel", "multi_sum_of_squares_kernel"))
+                     if multi else None, "traffic_unit": "DRAM bytes per step (ncu, profiles/norm_optim_cfg3_kernels.md)",
                      "algorithmic_bytes_per_step": algorithmic, "peak_source": f"{source} hbm_gbs"},
         "e2e": {"value": ms, "unit": "ms", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0 if multi else 8 * len(shapes)},
         "gpu_launches": (2 if multi else 2 * len(shapes)) * args.steps, "clocks": clock_info,
@@ -737,7 +747,12 @@ def run_norm(args, rank: int, world: int, local_rank: int) -> int:
                    "tokens": tokens, "l2": "inputs larger than L2 (y: 302 MB bf16)"},
         "roofline": {"bound": "tensor", "kernel": "tc_gemm_kernel with row_scale (+ rms statistics)",
                      "achieved": flops / (ms / 1e3) / 1e12, "peak": peak, "unit": "TFLOP/s",
-                     "frac": flops / (ms / 1e3) / 1e12 / peak, "traffic": None, "peak_source": f"{source} bf16_tflops"},
+                     "frac": flops / (ms / 1e3) / 1e12 / peak,
+                     "traffic": profile_traffic_sum("norm_optim_cfg3_kernels.json",
+                                                    ("tc_gemm_kernel", "rms_norm_forward_kernel"))
+                     if args.norm_path == "fused" and tokens == 65536 else None,
+                     "traffic_unit": "DRAM bytes per step (ncu, profiles/norm_optim_cfg3_kernels.md)",
+                     "peak_source": f"{source} bf16_tflops"},
         "e2e": {"value": flops / (ms / 1e3) / 1e12, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
         "gpu_launches": 2 * args.steps, "clocks": clock_info,
     }
