@@ -104,25 +104,59 @@ struct AdamWArgs {
     float first_correction, second_correction;
 };
 
-// The reference's per-element update (kernels/optimizer.rs:57-70), on the gradient times `clip`.
-__device__ __forceinline__ void adamw_element(float* parameter, const float* gradient, float* first, float* second,
-                                              int64_t i, const AdamWArgs& a, float weight_decay, float clip) {
-    const float grad = gradient[i] * clip;
-    const float mean = a.beta1 * first[i] + (1.0f - a.beta1) * grad;
-    const float variance = a.beta2 * second[i] + (1.0f - a.beta2) * grad * grad;
-    first[i] = mean;
-    second[i] = variance;
+// The reference's per-element update (kernels/optimizer.rs:57-70), on the gradient times `clip`, in registers.
+__device__ __forceinline__ void adamw_value(float& weight, float gradient, float& first, float& second,
+                                            const AdamWArgs& a, float weight_decay, float clip) {
+    const float grad = gradient * clip;
+    const float mean = a.beta1 * first + (1.0f - a.beta1) * grad;
+    const float variance = a.beta2 * second + (1.0f - a.beta2) * grad * grad;
+    first = mean;
+    second = variance;
     const float mean_hat = mean / a.first_correction;
     const float variance_hat = variance / a.second_correction;
-    const float weight = parameter[i];
     const float update = mean_hat / (sqrtf(variance_hat) + a.epsilon) + weight_decay * weight;
-    parameter[i] = weight - a.learning_rate * update;
+    weight = weight - a.learning_rate * update;
+}
+
+__device__ __forceinline__ void adamw_element(float* parameter, const float* gradient, float* first, float* second,
+                                              int64_t i, const AdamWArgs& a, float weight_decay, float clip) {
+    float w = parameter[i], m = first[i], v = second[i];
+    adamw_value(w, gradient[i], m, v, a, weight_decay, clip);
+    first[i] = m;
+    second[i] = v;
+    parameter[i] = w;
+}
+
+// Arrays that start on 16-byte boundaries are read and written as float4 vectors, four elements per access, which
+// keeps four times as many bytes in flight per thread (the streaming kernels here are bound by HBM latency times
+// bandwidth, not arithmetic).
+__device__ __forceinline__ bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; }
+
+__device__ __forceinline__ void adamw_vector(float* parameter, const float* gradient, float* first, float* second,
+                                             int64_t j, const AdamWArgs& a, float weight_decay, float clip) {
+    float4 pv = reinterpret_cast<float4*>(parameter)[j], mv = reinterpret_cast<float4*>(first)[j];
+    float4 vv = reinterpret_cast<float4*>(second)[j];
+    const float4 gv = reinterpret_cast<const float4*>(gradient)[j];
+    adamw_value(pv.x, gv.x, mv.x, vv.x, a, weight_decay, clip);
+    adamw_value(pv.y, gv.y, mv.y, vv.y, a, weight_decay, clip);
+    adamw_value(pv.z, gv.z, mv.z, vv.z, a, weight_decay, clip);
+    adamw_value(pv.w, gv.w, mv.w, vv.w, a, weight_decay, clip);
+    reinterpret_cast<float4*>(parameter)[j] = pv;
+    reinterpret_cast<float4*>(first)[j] = mv;
+    reinterpret_cast<float4*>(second)[j] = vv;
 }
 
 __global__ void adamw_kernel(float* parameter, const float* gradient, float* first, float* second, int64_t count,
                              AdamWArgs a, float weight_decay) {
-    for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < count;
-         i += static_cast<int64_t>(gridDim.x) * blockDim.x)
+    const int64_t stride = static_cast<int64_t>(gridDim.x) * blockDim.x;
+    const int64_t tid = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+    int64_t scalar_begin = 0;
+    if (aligned16(parameter) && aligned16(gradient) && aligned16(first) && aligned16(second)) {
+        for (int64_t j = tid; j < count / 4; j += stride) adamw_vector(parameter, gradient, first, second, j, a,
+                                                                      weight_decay, 1.0f);
+        scalar_begin = count / 4 * 4;
+    }
+    for (int64_t i = scalar_begin + tid; i < count; i += stride)
         adamw_element(parameter, gradient, first, second, i, a, weight_decay, 1.0f);
 }
 
@@ -140,10 +174,19 @@ __device__ __forceinline__ void add_block_sum(float v, double* total) {
 }
 
 __global__ void __launch_bounds__(256) sum_of_squares_kernel(const float* values, int64_t count, double* total) {
+    const int64_t stride = static_cast<int64_t>(gridDim.x) * blockDim.x;
+    const int64_t tid = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
     float sum = 0.0f;
-    for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < count;
-         i += static_cast<int64_t>(gridDim.x) * blockDim.x)
-        sum += values[i] * values[i];
+    int64_t scalar_begin = 0;
+    if (aligned16(values)) {
+        const float4* v4 = reinterpret_cast<const float4*>(values);
+        for (int64_t j = tid; j < count / 4; j += stride) {
+            const float4 v = v4[j];
+            sum += v.x * v.x + v.y * v.y + v.z * v.z + v.w * v.w;
+        }
+        scalar_begin = count / 4 * 4;
+    }
+    for (int64_t i = scalar_begin + tid; i < count; i += stride) sum += values[i] * values[i];
     add_block_sum(sum, total);
 }
 
@@ -168,6 +211,10 @@ __device__ __forceinline__ int tensor_of_chunk(const MultiTensors& m, int64_t ch
     return lo;
 }
 
+// Chunks start at multiples of kMultiChunk (a multiple of 4), so a tensor whose arrays are 16-byte aligned is
+// read and written in float4 vectors (see aligned16); the last count % 4 elements and unaligned tensors take the
+// scalar path.
+
 __global__ void __launch_bounds__(256) multi_sum_of_squares_kernel(const __grid_constant__ MultiTensors m,
                                                                    double* total) {
     const int64_t chunk = blockIdx.x;
@@ -175,11 +222,19 @@ __global__ void __launch_bounds__(256) multi_sum_of_squares_kernel(const __grid_
     const int64_t begin = (chunk - m.chunk_start[t]) * kMultiChunk;
     const int64_t end = begin + kMultiChunk < static_cast<int64_t>(m.t[t].count) ? begin + kMultiChunk
                                                                                    : static_cast<int64_t>(m.t[t].count);
+    const float* g = m.t[t].gradient;
     float sum = 0.0f;
-    for (int64_t i = begin + threadIdx.x; i < end; i += blockDim.x) {
-        const float g = m.t[t].gradient[i];
-        sum += g * g;
+    int64_t scalar_begin = begin;
+    if (aligned16(g)) {
+        const int64_t n4 = (end - begin) >> 2;
+        const float4* g4 = reinterpret_cast<const float4*>(g + begin);
+        for (int64_t j = threadIdx.x; j < n4; j += blockDim.x) {
+            const float4 v = g4[j];
+            sum += v.x * v.x + v.y * v.y + v.z * v.z + v.w * v.w;
+        }
+        scalar_begin = begin + 4 * n4;
     }
+    for (int64_t i = scalar_begin + threadIdx.x; i < end; i += blockDim.x) sum += g[i] * g[i];
     add_block_sum(sum, total);
 }
 
@@ -192,9 +247,17 @@ __global__ void __launch_bounds__(256) multi_adamw_kernel(const __grid_constant_
     const int64_t begin = (chunk - m.chunk_start[t]) * kMultiChunk;
     const int64_t end = begin + kMultiChunk < static_cast<int64_t>(m.t[t].count) ? begin + kMultiChunk
                                                                                    : static_cast<int64_t>(m.t[t].count);
-    for (int64_t i = begin + threadIdx.x; i < end; i += blockDim.x)
-        adamw_element(m.t[t].parameter, m.t[t].gradient, m.t[t].first_moment, m.t[t].second_moment, i, a,
-                      m.t[t].weight_decay, clip);
+    const snb_adamw_tensor& x = m.t[t];
+    int64_t scalar_begin = begin;
+    if (aligned16(x.parameter) && aligned16(x.gradient) && aligned16(x.first_moment) && aligned16(x.second_moment)) {
+        const int64_t n4 = (end - begin) >> 2;
+        for (int64_t j = threadIdx.x; j < n4; j += blockDim.x)
+            adamw_vector(x.parameter + begin, x.gradient + begin, x.first_moment + begin, x.second_moment + begin, j,
+                         a, x.weight_decay, clip);
+        scalar_begin = begin + 4 * n4;
+    }
+    for (int64_t i = scalar_begin + threadIdx.x; i < end; i += blockDim.x)
+        adamw_element(x.parameter, x.gradient, x.first_moment, x.second_moment, i, a, x.weight_decay, clip);
 }
 
 AdamWArgs adamw_args(const snb_adamw_hyper& h) {

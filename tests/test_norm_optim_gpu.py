@@ -132,6 +132,34 @@ def test_sum_of_squares_and_multi_tensor_adamw_with_clipping():
         assert o.relative_error(em, mt.cpu().numpy()) < 1e-5 and o.relative_error(ev, vt.cpu().numpy()) < 1e-5
 
 
+def test_multi_tensor_adamw_on_views_that_are_not_16_byte_aligned():
+    """Tensors whose arrays start one element into an allocation take the kernel's scalar path, aligned ones the
+    float4 path; both give the reference's per-element update."""
+    rng = np.random.default_rng(5)
+    sizes, offsets = [1001, 4096, 16384 + 6], [1, 0, 3]
+    host = [tuple(rng.standard_normal(n).astype(np.float32) * s for s in (1.0, 1.0, 0.01)) +
+            ((rng.random(n) * 0.02).astype(np.float32),) for n in sizes]
+    dev = []
+    for arrays, off in zip(host, offsets):
+        views = []
+        for a in arrays:
+            buf = torch.zeros(a.size + off, device="cuda")
+            buf[off:] = torch.from_numpy(a).cuda()
+            views.append(buf[off:])
+        dev.append(tuple(views))
+    gpu = Gpu(0)
+    total = torch.zeros(1, device="cuda", dtype=torch.float64)
+    hyper = AdamWHyperparameters(1e-3, 0.9, 0.999, 1e-8, 0.0, 3)
+    gpu.adamw_step_multi([(p, g, m, v, 0.01) for p, g, m, v in dev], hyper, 1e9, total)
+    torch.cuda.synchronize()
+    assert abs(total.item() - sum(o.sum_of_squares(h[1]) for h in host)) <= 1e-5 * total.item()
+    for (w, g, m, v), (pt, _, mt, vt) in zip(host, dev):
+        e, em, ev = w.copy(), m.copy(), v.copy()
+        o.adamw_step(e, g, em, ev, hyper.learning_rate, hyper.beta1, hyper.beta2, hyper.epsilon, 0.01, hyper.step)
+        assert o.relative_error(e, pt.cpu().numpy()) < 1e-5
+        assert o.relative_error(em, mt.cpu().numpy()) < 1e-5 and o.relative_error(ev, vt.cpu().numpy()) < 1e-5
+
+
 @pytest.mark.parametrize("rows,cols", [(300, 2304), (200, 513)])
 def test_fused_rms_norm_prologue_equals_norm_then_gemm(rows, cols):
     """rms_norm(x) W computed as diag(1/rms) x (diag(g) W): snb_rms_norm_stats + snb_scale_rows + snb_gemm with
