@@ -97,26 +97,13 @@ struct TcUnit {
     bool skip;  // every output of the tile is a masked score (SNB_CAUSAL_SKIP_MASKED_OUTPUT): no work at all
 };
 
-// Work-unit order: K split outermost (the tiles of one split run side by side, so concurrent CTAs share operand
-// slices in L2 and the splits of one tile never reduce into C at the same time), then the batch, then output tiles
-// with the M or the N tile index fastest, whichever keeps the larger operand streaming through DRAM once.
-__device__ __forceinline__ TcUnit tc_decode_unit(const TcParams& p, int32_t unit, int BN, int BK, int BM = TC_BM) {
+// The unit at output tile (mt, nt) of matrix `batch` in K split `split`: its output origin and K-slice range, cut
+// by the causal hints of a batched attention product.
+__device__ __forceinline__ TcUnit tc_make_unit(const TcParams& p, int32_t split, int32_t batch, int32_t mt, int32_t nt,
+                                               int BN, int BK, int BM) {
     TcUnit u;
-    const int32_t tiles = p.count * p.m_tiles * p.n_tiles;
-    u.split = unit / tiles;
-    const int32_t tile = unit - u.split * tiles;
-    int32_t mt, nt, rest;
-    if (p.m_fastest) {
-        mt = tile % p.m_tiles;
-        rest = tile / p.m_tiles;
-        nt = rest % p.n_tiles;
-        u.batch = rest / p.n_tiles;
-    } else {
-        nt = tile % p.n_tiles;
-        rest = tile / p.n_tiles;
-        mt = rest % p.m_tiles;
-        u.batch = rest / p.m_tiles;
-    }
+    u.split = split;
+    u.batch = batch;
     u.m0 = mt * BM;
     u.n0 = nt * BN;
     u.kb_begin = u.split * p.k_blocks_per_split;
@@ -139,6 +126,61 @@ __device__ __forceinline__ TcUnit tc_decode_unit(const TcParams& p, int32_t unit
     // Keep at least one K slice (its masked contributions are zero) so the accumulator is always written.
     if (u.kb_begin >= u.kb_end) u.kb_begin = u.kb_end - 1;
     return u;
+}
+
+// Work-unit order: K split outermost (the tiles of one split run side by side, so concurrent CTAs share operand
+// slices in L2 and the splits of one tile never reduce into C at the same time), then the batch, then output tiles
+// with the M or the N tile index fastest, whichever keeps the larger operand streaming through DRAM once: unit
+// = ((split * count + batch) * n_slow + slow) * n_fast + fast, with (fast, slow) = (mt, nt) when p.m_fastest, else
+// (nt, mt). A CTA walks units first, first + step, ... with a TcCursor, which keeps these digits
+// and adds the step's digits with carries: the integer divisions happen once per CTA, not once per tile, where
+// they kept the single MMA-issuing thread busy for about a thousand cycles between tiles while the tensor pipe ran
+// dry (measured on K=768 products: ~1,100 idle cycles per 6,144-cycle tile).
+struct TcCursor {
+    int32_t unit, step;
+    int32_t split, batch, slow, fast;
+    int32_t d_split, d_batch, d_slow, d_fast;
+    int32_t n_slow, n_fast;
+};
+
+__device__ __forceinline__ void tc_digits(const TcParams& p, int32_t x, int32_t n_slow, int32_t n_fast, int32_t& split,
+                                          int32_t& batch, int32_t& slow, int32_t& fast) {
+    fast = x % n_fast;
+    x /= n_fast;
+    slow = x % n_slow;
+    x /= n_slow;
+    batch = x % p.count;
+    split = x / p.count;
+}
+
+__device__ __forceinline__ TcCursor tc_cursor(const TcParams& p, int32_t first, int32_t step) {
+    TcCursor c;
+    c.unit = first;
+    c.step = step;
+    c.n_fast = p.m_fastest ? p.m_tiles : p.n_tiles;
+    c.n_slow = p.m_fastest ? p.n_tiles : p.m_tiles;
+    tc_digits(p, first, c.n_slow, c.n_fast, c.split, c.batch, c.slow, c.fast);
+    tc_digits(p, step, c.n_slow, c.n_fast, c.d_split, c.d_batch, c.d_slow, c.d_fast);
+    return c;
+}
+
+__device__ __forceinline__ void tc_advance(const TcParams& p, TcCursor& c) {
+    c.unit += c.step;
+    c.fast += c.d_fast;
+    int32_t carry = c.fast >= c.n_fast ? 1 : 0;
+    c.fast -= carry * c.n_fast;
+    c.slow += c.d_slow + carry;
+    carry = c.slow >= c.n_slow ? 1 : 0;
+    c.slow -= carry * c.n_slow;
+    c.batch += c.d_batch + carry;
+    carry = c.batch >= p.count ? 1 : 0;
+    c.batch -= carry * p.count;
+    c.split += c.d_split + carry;
+}
+
+__device__ __forceinline__ TcUnit tc_cursor_unit(const TcParams& p, const TcCursor& c, int BN, int BK, int BM = TC_BM) {
+    return p.m_fastest ? tc_make_unit(p, c.split, c.batch, c.fast, c.slow, BN, BK, BM)
+                       : tc_make_unit(p, c.split, c.batch, c.slow, c.fast, BN, BK, BM);
 }
 
 __device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
@@ -494,8 +536,8 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
             int stage = 0;
             uint32_t phase = 0;
             bool ok = true;
-            for (int32_t unit = blockIdx.x; unit < p.num_units && ok; unit += gridDim.x) {
-                const TcUnit u = tc_decode_unit(p, unit, BN, BK);
+            for (TcCursor cur = tc_cursor(p, blockIdx.x, gridDim.x); cur.unit < p.num_units && ok; tc_advance(p, cur)) {
+                const TcUnit u = tc_cursor_unit(p, cur, BN, BK);
                 if (u.skip) continue;
                 const int32_t ba = p.a_batched ? u.batch : 0;
                 const int32_t bb = p.b_batched ? u.batch : 0;
@@ -553,8 +595,8 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
             int iter = 0;
             bool ok = true;
             bool issued = false;
-            for (int32_t unit = blockIdx.x; unit < p.num_units && ok; unit += gridDim.x) {
-                const TcUnit u = tc_decode_unit(p, unit, BN, BK);
+            for (TcCursor cur = tc_cursor(p, blockIdx.x, gridDim.x); cur.unit < p.num_units && ok; tc_advance(p, cur)) {
+                const TcUnit u = tc_cursor_unit(p, cur, BN, BK);
                 if (u.skip) continue;
                 const int acc = iter & 1;
                 const uint32_t acc_phase = (iter >> 1) & 1;
@@ -602,12 +644,13 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
         uint32_t aux_phase = 0;
         int ebox = 0;
         int iter = 0;
-        if (box_aux && lane == 0 && static_cast<int32_t>(blockIdx.x) < p.num_units) {
-            const TcUnit u0 = tc_decode_unit(p, blockIdx.x, BN, BK);
+        TcCursor cur = tc_cursor(p, blockIdx.x, gridDim.x);
+        if (box_aux && lane == 0 && cur.unit < p.num_units) {
+            const TcUnit u0 = tc_cursor_unit(p, cur, BN, BK);
             request_aux_boxes<OUT_BF16, BN>(p, &tm_aux, u0, u0.m0 + q * 32, group, boxes, aux_bar);
         }
-        for (int32_t unit = blockIdx.x; unit < p.num_units; unit += gridDim.x) {
-            const TcUnit u = tc_decode_unit(p, unit, BN, BK);
+        for (; cur.unit < p.num_units; tc_advance(p, cur)) {
+            const TcUnit u = tc_cursor_unit(p, cur, BN, BK);
             if (u.skip) continue;
             const int acc = iter & 1;
             const uint32_t acc_phase = (iter >> 1) & 1;
@@ -624,10 +667,11 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
             ++iter;
             // The next tile's auxiliary input is requested as soon as this tile's stores have read the boxes, so
             // its loads overlap the next main loop.
-            const int32_t next = unit + static_cast<int32_t>(gridDim.x);
-            if (box_aux && lane == 0 && next < p.num_units) {
+            TcCursor next = cur;
+            tc_advance(p, next);
+            if (box_aux && lane == 0 && next.unit < p.num_units) {
                 bulk_wait_group_read<0>();
-                const TcUnit un = tc_decode_unit(p, next, BN, BK);
+                const TcUnit un = tc_cursor_unit(p, next, BN, BK);
                 request_aux_boxes<OUT_BF16, BN>(p, &tm_aux, un, un.m0 + q * 32, group, boxes, aux_bar);
             }
             __syncwarp();

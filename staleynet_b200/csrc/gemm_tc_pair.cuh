@@ -105,8 +105,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(TC_THREADS, 1)
             int stage = 0;
             uint32_t phase = 0;
             bool ok = true;
-            for (int32_t unit = first_unit; unit < p.num_units && ok; unit += unit_step) {
-                const TcUnit u = tc_decode_unit(p, unit, BN, BK, TC2_BM);
+            for (TcCursor cur = tc_cursor(p, first_unit, unit_step); cur.unit < p.num_units && ok; tc_advance(p, cur)) {
+                const TcUnit u = tc_cursor_unit(p, cur, BN, BK, TC2_BM);
                 const int32_t ba = p.a_batched ? u.batch : 0;
                 const int32_t bb = p.b_batched ? u.batch : 0;
                 const int32_t m0 = u.m0 + 128 * static_cast<int32_t>(rank);  // this CTA's rows
@@ -161,8 +161,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(TC_THREADS, 1)
             int iter = 0;
             bool ok = true;
             bool issued = false;
-            for (int32_t unit = first_unit; unit < p.num_units && ok; unit += unit_step) {
-                const TcUnit u = tc_decode_unit(p, unit, BN, BK, TC2_BM);
+            for (TcCursor cur = tc_cursor(p, first_unit, unit_step); cur.unit < p.num_units && ok; tc_advance(p, cur)) {
+                const TcUnit u = tc_cursor_unit(p, cur, BN, BK, TC2_BM);
                 const int acc = iter & 1;
                 const uint32_t acc_phase = (iter >> 1) & 1;
                 if (!mbar_wait_cluster(smem_addr(&acc_empty[acc]), acc_phase ^ 1u)) { ok = false; break; }
@@ -210,12 +210,13 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(TC_THREADS, 1)
         uint32_t aux_phase = 0;
         int ebox = 0;
         int iter = 0;
-        if (box_aux && lane == 0 && first_unit < p.num_units) {
-            const TcUnit u0 = tc_decode_unit(p, first_unit, BN, BK, TC2_BM);
+        TcCursor cur = tc_cursor(p, first_unit, unit_step);
+        if (box_aux && lane == 0 && cur.unit < p.num_units) {
+            const TcUnit u0 = tc_cursor_unit(p, cur, BN, BK, TC2_BM);
             request_aux_boxes<OUT_BF16, BN>(p, &tm_aux, u0, u0.m0 + row_off, group, boxes, aux_bar);
         }
-        for (int32_t unit = first_unit; unit < p.num_units; unit += unit_step) {
-            const TcUnit u = tc_decode_unit(p, unit, BN, BK, TC2_BM);
+        for (; cur.unit < p.num_units; tc_advance(p, cur)) {
+            const TcUnit u = tc_cursor_unit(p, cur, BN, BK, TC2_BM);
             const int acc = iter & 1;
             const uint32_t acc_phase = (iter >> 1) & 1;
             if (!mbar_wait_cluster(smem_addr(&acc_full[acc]), acc_phase)) break;
@@ -229,10 +230,11 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(TC_THREADS, 1)
             __syncwarp();
             if (lane == 0) mbar_arrive_cluster(map_to_cta(smem_addr(&acc_empty[acc]), 0));
             ++iter;
-            const int32_t next = unit + unit_step;
-            if (box_aux && lane == 0 && next < p.num_units) {
+            TcCursor next = cur;
+            tc_advance(p, next);
+            if (box_aux && lane == 0 && next.unit < p.num_units) {
                 bulk_wait_group_read<0>();
-                const TcUnit un = tc_decode_unit(p, next, BN, BK, TC2_BM);
+                const TcUnit un = tc_cursor_unit(p, next, BN, BK, TC2_BM);
                 request_aux_boxes<OUT_BF16, BN>(p, &tm_aux, un, un.m0 + row_off, group, boxes, aux_bar);
             }
             __syncwarp();
