@@ -405,7 +405,7 @@ def run_ours(args, shape, rank: int, world: int, local_rank: int) -> int:
             "clocks": clock_info,
         }
         if cpu is not None:
-            line["cpu_baseline"] = {k: cpu[k] for k in ("value", "unit", "cores", "kind", "sample")}
+            line["cpu_baseline"] = {k: cpu[k] for k in ("value", "unit", "cores", "kind", "sample", "single_thread")}
         print(json.dumps(line), flush=True)
     del step
     return 0
