@@ -80,22 +80,10 @@ __device__ __forceinline__ void rms_norm_row(const void* input, int in_bf16, con
         }
     }
     const float inverse = 1.0f / sqrtf(warp_sum_f(square_sum) / static_cast<float>(cols) + epsilon);
+    // The normalised output, one element per lane so that a warp's stores are contiguous.
     if (output != nullptr) {
-        if (vec) {
-            const uint4* src = reinterpret_cast<const uint4*>(
-                reinterpret_cast<const uint8_t*>(input) + base * (in_bf16 ? 2 : 4));
-            for (int64_t k = lane; k < cols / per; k += 32) {
-                float v[8];
-                unpack16(__ldg(src + k), in_bf16, v);
-                const int64_t c0 = k * per;
-#pragma unroll
-                for (int e = 0; e < 8; ++e)
-                    if (e < per) store_elem(output, base + c0 + e, v[e] * inverse * __ldg(gain + c0 + e), out_bf16);
-            }
-        } else {
-            for (int64_t c = lane; c < cols; c += 32)
-                store_elem(output, base + c, load_elem(input, base + c, in_bf16) * inverse * gain[c], out_bf16);
-        }
+        for (int64_t c = lane; c < cols; c += 32)
+            store_elem(output, base + c, load_elem(input, base + c, in_bf16) * inverse * gain[c], out_bf16);
     }
     if (lane == 0) inv_rms[row] = inverse;
 }
@@ -103,9 +91,8 @@ __device__ __forceinline__ void rms_norm_row(const void* input, int in_bf16, con
 // One warp per row (the launch gives every row its own warp: a grid of fewer, row-looping warps measured slower,
 // since a warp reduces one row before it loads the next): inv_rms[row] = s and, when `output` is given,
 // output = x s g (of out_bf16's type). With `vec`
-// (every row of the input starts on a 16-byte boundary) each lane reads 16-byte pieces of the row, so a warp keeps
-// several times the bytes in flight of one element per lane; the sums are the same f32 values added in a different
-// order.
+// (every row of the input starts on a 16-byte boundary) each lane reads 16-byte pieces of the row for the sum of
+// squares (the same f32 values added in a different order).
 __global__ void rms_norm_forward_kernel(const void* input, int in_bf16, const float* gain, void* output, int out_bf16,
                                         float* inv_rms, int64_t rows, int64_t cols, float epsilon, int vec) {
     const int lane = threadIdx.x & 31;
