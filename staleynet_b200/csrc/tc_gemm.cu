@@ -597,9 +597,15 @@ int fused_attention_backward(cudaStream_t stream, const void* q, const void* k, 
         if (!static_scratch_only) cudaFreeAsync(stats, stream);
     };
     const uint64_t rows = count * queries;
-    fb_rowstats_kernel<<<static_cast<unsigned>((rows + 7) / 8), 256, 0, stream>>>(
-        out, out_type == SNB_TYPE_BF16 ? 1 : 0, static_cast<const uint16_t*>(d_out), lse, stats,
-        static_cast<int64_t>(rows), static_cast<int32_t>(queries), static_cast<int64_t>(stride));
+    if (reinterpret_cast<uintptr_t>(out) % 16 == 0 && reinterpret_cast<uintptr_t>(d_out) % 16 == 0) {
+        fb_rowstats_vec_kernel<<<static_cast<unsigned>((rows + 31) / 32), 256, 0, stream>>>(
+            out, out_type == SNB_TYPE_BF16 ? 1 : 0, static_cast<const uint16_t*>(d_out), lse, stats,
+            static_cast<int64_t>(rows), static_cast<int32_t>(queries), static_cast<int64_t>(stride));
+    } else {
+        fb_rowstats_kernel<<<static_cast<unsigned>((rows + 7) / 8), 256, 0, stream>>>(
+            out, out_type == SNB_TYPE_BF16 ? 1 : 0, static_cast<const uint16_t*>(d_out), lse, stats,
+            static_cast<int64_t>(rows), static_cast<int32_t>(queries), static_cast<int64_t>(stride));
+    }
     e = cudaGetLastError();
     if (e != cudaSuccess) {
         release();
