@@ -241,13 +241,17 @@ int tc_gemm_try(cudaStream_t stream, const GemmRequest& r, bool* launched, int* 
 
     const int bn = p.cols <= 64 ? 64 : (p.cols <= 128 ? 128 : 256);
     const int bk = 128 / esize;
-    // Wide, tall products with long K run on CTA pairs (256 x 256 tiles, a third less L2 traffic per FLOP). With
-    // short K (K=768: 12 slices per tile) a pair's main loop must wait for the slower of its two CTAs' epilogues,
-    // which costs more than the pair saves (measured on the training step's shapes), so those stay on single
-    // CTAs. The causal attention hints are implemented by the single-CTA kernel only.
+    // Tall products wider than 128 columns run on CTA pairs (256 x 256 tiles, a third less L2 traffic per FLOP, and a
+    // 6-stage ring that covers the longer load latency while output stores are in flight) when K is long, and for
+    // bf16 products also when they are at most 1,024 columns wide. Measured on the training step's K=768 shapes:
+    // pairs are 3-7 % faster at 768 columns (output.fwd, output.dX) but 3-7 % slower at 2,304 and 3,072 (qkv.fwd,
+    // expand.fwd, project.dX), where the pair's main loop waits for the slower of two epilogues. The causal attention
+    // hints are implemented by the single-CTA kernel only.
     constexpr int64_t kPairMinKBytes = 4096;  // K >= 2048 bf16 / 1024 f32
+    constexpr int64_t kPairMaxNarrowCols = 1024;
     const bool pair = bn == 256 && p.rows > TC_BM && r.causal == SNB_CAUSAL_NONE && dev.sm_count >= 2 &&
-                      static_cast<int64_t>(p.inner) * esize >= kPairMinKBytes;
+                      (static_cast<int64_t>(p.inner) * esize >= kPairMinKBytes ||
+                       (bf16_in && static_cast<int64_t>(p.cols) <= kPairMaxNarrowCols));
     const int bm = pair ? TC2_BM : TC_BM;
     const int workers = pair ? dev.sm_count / 2 : dev.sm_count;
     const int64_t m_tiles = (p.rows + bm - 1) / bm;
