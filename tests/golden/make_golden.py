@@ -3,19 +3,20 @@ path and its neighbours, each with the file:line it comes from.
 
     python tests/golden/make_golden.py [--reference /path/to/staleynet]
 
-The vectors are transcribed below; when the reference checkout is given (or found at the default path), every
-literal is checked to occur verbatim at the cited lines before the fixture is written, so the fixture cannot drift
-from the reference's tests. The GPU box never runs this script; tests read only the JSON.
+The vectors are transcribed below; when the reference checkout is given (by --reference or the STALEYNET_REFERENCE
+environment variable), every literal is checked to occur verbatim at the cited lines before the fixture is written,
+so the fixture cannot drift from the reference's tests. The GPU box never runs this script; tests read only the JSON.
 """
 from __future__ import annotations
 
 import argparse
 import json
+import os
 import sys
 from pathlib import Path
 
 HERE = Path(__file__).resolve().parent
-DEFAULT_REFERENCE = Path("/root/reference")
+DEFAULT_REFERENCE = Path(os.environ["STALEYNET_REFERENCE"]) if os.environ.get("STALEYNET_REFERENCE") else None
 REF_FILE = "crates/staleynet-cuda/src/reference.rs"
 
 # (name, source lines, literal snippets that must appear in those lines, case data)
@@ -206,7 +207,7 @@ def main(argv=None) -> int:
     ap.add_argument("--reference", type=Path, default=DEFAULT_REFERENCE)
     args = ap.parse_args(argv)
     checked = False
-    if (args.reference / REF_FILE).exists():
+    if args.reference is not None and (args.reference / REF_FILE).exists():
         check_against_reference(args.reference)
         checked = True
     out = {
