@@ -900,6 +900,11 @@ def main(argv=None) -> int:
         import torch
         import torch.distributed as dist
 
+        # NCCL writes its version banner and warnings to the C stdout (fd 1) when NCCL_DEBUG is set. Rank 0's
+        # stdout carries only the result line: Python keeps the original stdout, and fd 1 now points at stderr.
+        sys.stdout.flush()
+        sys.stdout = os.fdopen(os.dup(1), "w")
+        os.dup2(2, 1)
         torch.cuda.set_device(local_rank)
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
                                 device_id=torch.device("cuda", local_rank))
