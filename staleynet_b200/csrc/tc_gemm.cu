@@ -509,15 +509,21 @@ namespace {
 constexpr uint64_t kStaticScratchBytes = 8ull << 20;
 static __device__ __align__(256) float g_attention_scratch[kStaticScratchBytes / sizeof(float)];
 
-// The scratch array's device address on the current device, looked up once per device.
+// The scratch array's device address on the current device, looked up once per device (the first no-alloc call
+// on a device does it). A cudaDeviceReset of that device unloads the library's module from it, so the cached address
+// is no longer valid afterwards: a process that resets a device does not use the no-alloc entry point on it again.
 int static_scratch(float** ptr, std::string* err) {
     static std::mutex mu;
     static float* cached[64] = {};
     int dev = 0;
     cudaError_t e = cudaGetDevice(&dev);
-    if (e != cudaSuccess || dev < 0 || dev >= 64) {
+    if (e != cudaSuccess) {
         *err = cuda_message("cudaGetDevice", e);
         return SNB_ERR_CUDA;
+    }
+    if (dev < 0 || dev >= 64) {
+        *err = "no-alloc scratch: device ordinal " + std::to_string(dev) + " is beyond the 64 devices it tracks";
+        return SNB_ERR_UNSUPPORTED;
     }
     std::lock_guard<std::mutex> lock(mu);
     if (cached[dev] == nullptr) {
@@ -540,21 +546,27 @@ int fused_attention_backward(cudaStream_t stream, const void* q, const void* k, 
                              uint64_t keys, float scale, uint64_t query_offset, float* dq, float* dk, float* dv,
                              bool static_scratch_only, std::string* err) {
     if (count == 0) return SNB_OK;
-    DeviceInfo dev;
-    int rc = current_device_info(&dev, err);
-    if (rc != SNB_OK) return rc;
-    if (dev.major != 10) {
-        *err = "fused attention needs an sm_100 device";
-        return SNB_ERR_UNSUPPORTED;
-    }
+    // Sizes and alignment are checked before any CUDA call, so a refused call touches neither the device nor a
+    // buffer.
     const uint64_t lim = (1ull << 31) - 256;
     if (count > lim || queries > lim || keys > lim) {
         *err = "fused attention backward: sizes out of range";
         return SNB_ERR_INVALID_ARGUMENT;
     }
     // Scratch: per query (-lse * log2(e), D), matrices `stride` floats apart (16-byte multiple for the tensor map).
+    // Every byte count below is formed with overflow checks: count and queries may each be close to 2^31, and a
+    // wrapped product would pass the size check of the static scratch or ask for a too-small allocation.
     const uint64_t stride = (2 * queries + 3) / 4 * 4;
-    const uint64_t scratch_bytes = count * stride * sizeof(float);
+    uint64_t scratch_bytes = 0, dq_bytes = 0, dkv_bytes = 0;
+    if (__builtin_mul_overflow(count, stride, &scratch_bytes) ||
+        __builtin_mul_overflow(scratch_bytes, sizeof(float), &scratch_bytes) ||
+        __builtin_mul_overflow(count, queries, &dq_bytes) ||
+        __builtin_mul_overflow(dq_bytes, FB_D * sizeof(float), &dq_bytes) ||
+        __builtin_mul_overflow(count, keys, &dkv_bytes) ||
+        __builtin_mul_overflow(dkv_bytes, FB_D * sizeof(float), &dkv_bytes)) {
+        *err = "fused attention backward: count * queries (or keys) * head size overflows 64 bits";
+        return SNB_ERR_INVALID_ARGUMENT;
+    }
     if (static_scratch_only && queries > 0 && keys > 0 && scratch_bytes > kStaticScratchBytes) {
         *err = "fused attention backward (no-alloc): needs " + std::to_string(scratch_bytes) +
                " bytes of row statistics (count * queries * 8, rounded), the static scratch holds " +
@@ -568,6 +580,13 @@ int fused_attention_backward(cudaStream_t stream, const void* q, const void* k, 
             return SNB_ERR_INVALID_ARGUMENT;
         }
     }
+    DeviceInfo dev;
+    int rc = current_device_info(&dev, err);
+    if (rc != SNB_OK) return rc;
+    if (dev.major != 10) {
+        *err = "fused attention needs an sm_100 device";
+        return SNB_ERR_UNSUPPORTED;
+    }
     auto memset_or_fail = [&](void* ptr, uint64_t bytes, const char* what) -> int {
         if (bytes == 0) return SNB_OK;
         cudaError_t e = cudaMemsetAsync(ptr, 0, bytes, stream);
@@ -578,12 +597,17 @@ int fused_attention_backward(cudaStream_t stream, const void* q, const void* k, 
         return SNB_OK;
     };
     // dQ is accumulated into by TMA reductions; with no queries or no keys every gradient is zero.
-    rc = memset_or_fail(dq, count * queries * FB_D * sizeof(float), "cudaMemsetAsync(dq)");
+    rc = memset_or_fail(dq, dq_bytes, "cudaMemsetAsync(dq)");
     if (rc != SNB_OK) return rc;
     if (queries == 0 || keys == 0) {
-        rc = memset_or_fail(dk, count * keys * FB_D * sizeof(float), "cudaMemsetAsync(dk)");
-        if (rc == SNB_OK) rc = memset_or_fail(dv, count * keys * FB_D * sizeof(float), "cudaMemsetAsync(dv)");
+        rc = memset_or_fail(dk, dkv_bytes, "cudaMemsetAsync(dk)");
+        if (rc == SNB_OK) rc = memset_or_fail(dv, dkv_bytes, "cudaMemsetAsync(dv)");
         return rc;
+    }
+    // The row-statistics grid covers count * queries rows, 32 per block (8 for the scalar form).
+    if (count * queries > 8ull * 0x7fffffffull) {
+        *err = "fused attention backward: count * queries exceeds the row-statistics grid";
+        return SNB_ERR_INVALID_ARGUMENT;
     }
     float* stats = nullptr;
     cudaError_t e = cudaSuccess;

@@ -124,3 +124,17 @@ def test_gemm_rejects_mismatched_precision():
     a.output_type = a.aux_type = _ffi.TYPE_F32
     a.precision = _ffi.PRECISION_BF16
     assert lib.snb_gemm(None, ctypes.byref(a)) == _ffi.ERR_INVALID_ARGUMENT
+
+
+def test_attention_backward_rejects_sizes_whose_byte_counts_overflow():
+    # count * ceil4(2 * queries) * 4 wraps 64 bits to about 128 KiB for this pair; without overflow checks the no-alloc
+    # entry point would accept it as fitting its static scratch. Both entry points must refuse it before any CUDA call
+    # (the fake pointers are never dereferenced).
+    lib = _ffi.load()
+    count, queries, keys = 2 ** 30 + 2 ** 15, 2 ** 31 - 65534, 128
+    fake = 0x1000
+    for fn in (lib.snb_causal_attention_backward_noalloc, lib.snb_causal_attention_backward):
+        code = fn(None, fake, fake, fake, fake, _ffi.TYPE_F32, fake, fake, count, queries, keys, 64, 0.125, 0, fake,
+                  fake, fake)
+        assert code == _ffi.ERR_INVALID_ARGUMENT
+        assert "overflow" in _ffi.last_error()
