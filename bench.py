@@ -1,19 +1,25 @@
-"""Benchmark: GEMM TFLOP/s of the fwd+dX+dW products of one training step of StaleyNET's width-768 decoder.
+"""Benchmark: GEMM TFLOP/s of the fwd+dX+dW products of StaleyNET's width-768 decoder's training step.
 
-    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference] [--global-batch S]
     torchrun --nproc-per-node N bench.py --gpus N ...      (one rank per GPU, NCCL)
 
-Workload (config 5 at N=8): per GPU, one micro-batch of 32 x 2048 = 65,536 tokens through the
-12-block width-768 decoder's linear GEMMs (QKV 768->2304, output 768->768, FFN 768->3072->768) and the 16 x 1024
-codebook head, forward, dX and dW, bf16 operands with f32 accumulation and fused bias / GELU / residual epilogues
-(staleynet_b200/step.py). 38.35 TFLOP per GPU per step. N GPUs run N micro-batches (weak scaling, global batch
-N x 32 x 2048) and all-reduce the f32 weight gradients with NCCL, per block, overlapped with the backward pass.
+Workload (BASELINE config 5 on the config 3 model, at every N): one optimizer step's worth of work over a global
+batch of 256 sequences x 2048 tokens, split over the N ranks by whole sequences; each rank runs its 256/N sequences
+as 32 x 2048 = 65,536-token micro-batches (8/N of them), each through the 12-block width-768 decoder's linear GEMMs
+(QKV 768->2304, output 768->768, FFN 768->3072->768) and the 16 x 1024 codebook head, forward, every codebook's
+cross-entropy, dX and dW, bf16 operands with f32 accumulation and fused bias / GELU / residual epilogues
+(staleynet_b200/step.py). dW accumulates over the micro-batches; the f32 weight gradients are all-reduced with NCCL
+once per step, per block, overlapped with the last micro-batch's backward. 38.35 TFLOP per micro-batch, 306.8 TFLOP
+per step; the total work is fixed as N grows (strong scaling). --global-batch 0 runs one micro-batch per GPU
+instead (config 3 per GPU, weak scaling).
 
 One JSON line (rank 0): `value` = whole-job TFLOP/s with inputs resident in HBM; `e2e` = the same step through
-the C ABI with the step's input activations copied from pinned host memory and a result read back every step;
-`roofline` = the tcgen05 GEMM kernel's FLOP rate from CUDA events around each launch in the timed region, against
-the measured bf16 peak; `cpu_baseline` = the CPU restatement of the reference's f32 GEMM loop on the host cores,
-timed on a sample of every GEMM's output rows and extrapolated by rows.
+the C ABI with every micro-batch's input activations copied from pinned host memory and the per-codebook loss sums
+read back every step; `roofline` = the tcgen05 GEMM kernels' FLOP rate from CUDA events around each launch in the
+timed region, against the measured bf16 peak; `gemms` = the same per GEMM of the step; `communication` (N > 1) =
+the all-reduce time left exposed after the last GEMM; `dp_parity` (N > 1) = the all-reduced gradients against
+rank 0 recomputing the global batch alone; `cpu_baseline` = the CPU restatement of the reference's f32 GEMM loop on
+the host cores, timed on a sample of every GEMM's output rows and extrapolated by rows.
 `--impl reference` times that CPU path alone (the reference's own implementation cannot be built here).
 """
 from __future__ import annotations
@@ -78,21 +84,30 @@ def load_kernel_traffic(kernel: str):
     return load_profile_traffic("fused_attention_cfg4_kernels.json", kernel)
 
 
-def workload_config(shape, n_gpus: int) -> dict:
+def workload_config(shape, n_gpus: int, global_sequences: int = 256, micro_per_rank: int = 8) -> dict:
+    if global_sequences:
+        workload = (f"cfg5 data-parallel training step of the cfg3 model (12 blocks, width 768): global batch "
+                    f"{global_sequences} x 2048 tokens split over {n_gpus} GPU(s), {micro_per_rank} micro-batch(es) "
+                    f"of 32 x 2048 per GPU accumulating dW, linear + 16x1024 codebook-head GEMMs fwd+dX+dW with "
+                    f"the codebook cross-entropy between them, f32 dW all-reduced once per step")
+    else:
+        workload = ("cfg3 12-block width-768 decoder: linear + 16x1024 codebook-head GEMMs, fwd+dX+dW with the "
+                    "codebook cross-entropy between them, one 32x2048 micro-batch per GPU")
     return {
-        "workload": "cfg3 12-block width-768 decoder: linear + 16x1024 codebook-head GEMMs, fwd+dX+dW, "
-                    "32x2048 tokens per GPU (cfg5 data-parallel step at N=8)",
+        "workload": workload,
         "model": "staleynet width-768 12-block decoder (111.5M), linear/head GEMMs",
         "blocks": shape.blocks,
         "width": shape.width,
         "ffn": shape.ffn,
         "head": f"{shape.codebooks}x{shape.codebook_size}",
-        "tokens_per_gpu": shape.tokens,
-        "global_batch": 32 * n_gpus,
-        "seq_len": 2048,
+        "tokens_per_micro_batch": shape.tokens,
+        "micro_batches_per_gpu": micro_per_rank,
+        "global_batch": global_sequences if global_sequences else 32 * n_gpus,
+        "seq_len": SEQ_LEN,
         "parallelism": f"dp{n_gpus}",
         "operands": "bf16 in, f32 accumulate; dW f32 via reduce-add; activations bf16",
-        "l2": "inputs larger than L2: one step moves > 20 GB through HBM (126 MB L2 flushed by the step itself)",
+        "l2": "inputs larger than L2: one micro-batch moves > 20 GB through HBM (126 MB L2 flushed by the work "
+              "itself)",
         "not_in_step": "attention score/softmax products, norms, bias-gradient column sums (not linear GEMMs)",
     }
 
@@ -162,13 +177,33 @@ class ClockSampler:
 
 
 # ------------------------------------------------------------------------------------------------ CPU baseline
-def cpu_baseline(shape, budget_flops: float = 20e9, threads: int = 0) -> dict:
+_OPERANDS: dict = {}
+
+
+def _seeded_operand(stored_rows: int, stored_cols: int, slot: int = 0):
+    """A dense row-major [stored_rows, stored_cols] f32 operand holding the parity tests' seeded LCG values
+    (kernels_match_reference.rs:26-38), written straight into the buffer in address order. Kept for the process
+    (keyed by shape and slot: slot 1 is a second operand of the same shape), so repeated CPU timings reuse it."""
+    import numpy as np
+
+    from oracle import oracle as o
+
+    key = (stored_rows, stored_cols, slot)
+    buf = _OPERANDS.get(key)
+    if buf is None:
+        buf = np.empty(stored_rows * stored_cols, np.float32)
+        o.lib().snb_oracle_fill_lcg(1 + len(_OPERANDS), o._f(buf), buf.size)
+        _OPERANDS[key] = buf
+    return buf
+
+
+def cpu_baseline(shape, budget_flops: float = 40e9, threads: int = 0) -> dict:
     """Times the CPU oracle (the reference's f32 GEMM loop, reference.rs:18-38) on a sample of every GEMM of the
     step and extrapolates by output elements (each output element costs the same `inner` multiply-adds).
 
     The sample of a GEMM is its first rows x cols output block with cols = min(N, 256), sized to `budget_flops`
-    over the whole step; operands keep the step's true strides (zero pages are mapped lazily, so only the lines
-    the sample reads become resident). Each sample runs twice and the second run is timed."""
+    over the whole step. Operands are dense f32 tensors of the step's true shapes and strides, filled with seeded
+    values. Each sample runs once untimed, then twice timed; the faster timed run counts."""
     import numpy as np
 
     from oracle import oracle as o
@@ -191,22 +226,28 @@ def cpu_baseline(shape, budget_flops: float = 20e9, threads: int = 0) -> dict:
     for mult, M, N, K, lt, rt in gemms:
         cols = min(N, 256)
         rows = min(M, max(1, int(round(frac * M * N / cols))))
-        left = np.zeros(M * K, np.float32)
-        right = np.zeros(K * N, np.float32)
+        # Stored shapes: a transposed left is [K, M], a transposed right [N, K].
+        left_shape = (K, M) if lt else (M, K)
+        right_shape = (N, K) if rt else (K, N)
+        left = _seeded_operand(*left_shape)
+        right = _seeded_operand(*right_shape, slot=1 if right_shape == left_shape else 0)
         out = np.zeros(rows * cols, np.float32)
         p = o.product(rows, cols, K, o.storage_strides(lt, M, K, 0), o.storage_strides(rt, K, N, 0), 0)
         o.matmul_rows(p, 1, left, right, out, 0, rows, threads)
-        t0 = time.perf_counter()
-        used_threads = o.matmul_rows(p, 1, left, right, out, 0, rows, threads)
-        dt = time.perf_counter() - t0
+        dt = float("inf")
+        for _ in range(2):
+            t0 = time.perf_counter()
+            used_threads = o.matmul_rows(p, 1, left, right, out, 0, rows, threads)
+            dt = min(dt, time.perf_counter() - t0)
         seconds_full += mult * dt * (M * N) / (rows * cols)
         sampled_flops += 2.0 * rows * cols * K
-        del left, right, out
+        del out
     wall = time.perf_counter() - t_start
     return {"value": total / seconds_full / 1e12, "unit": UNIT, "cores": used_threads, "kind": "port",
             "sample": f"first rows x min(N,256) output block of every GEMM of the step, {frac:.2e} of its "
-                      f"outputs ({sampled_flops / 1e9:.1f} GFLOP timed, {wall:.1f} s wall incl. an untimed "
-                      f"first pass), extrapolated by output elements; f32 operands at the step's strides",
+                      f"outputs ({sampled_flops / 1e9:.1f} GFLOP per timed run, best of 2 after an untimed run, "
+                      f"{wall:.1f} s wall), extrapolated by output elements; dense f32 operands of the step's true "
+                      f"shapes and strides, seeded with the reference's parity-test LCG",
             "seconds_per_step_extrapolated": seconds_full}
 
 
@@ -223,21 +264,27 @@ def run_reference(args, shape, rank: int, world: int) -> int:
     from oracle import oracle as o
 
     o.build()
+    # Each step times a tenth of the GPU arm's CPU sample, so that --steps 20 --warmup 5 stays within minutes; the
+    # operands are filled once and reused.
+    budget = args.cpu_sample_flops / 10
     for _ in range(args.warmup):
-        cpu_baseline(shape, budget_flops=args.cpu_sample_flops)
+        cpu_baseline(shape, budget_flops=budget)
     vals, secs = [], []
     for _ in range(args.steps):
-        r = cpu_baseline(shape, budget_flops=args.cpu_sample_flops)
+        r = cpu_baseline(shape, budget_flops=budget)
         vals.append(r["value"])
         secs.append(r["seconds_per_step_extrapolated"])
     value = statistics.median(vals)
     line = {
         "impl": "reference", "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": args.gpus,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": statistics.median(secs) * 1e3,
-        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
-        "config": workload_config(shape, args.gpus),
+        "higher_is_better": True, "scaling": "strong" if args.global_batch else "weak", "vs_baseline": None,
+        "dtype": "f32", "data": "synthetic",
+        "config": workload_config(shape, args.gpus, args.global_batch,
+                                  max(1, args.global_batch // MICRO_SEQUENCES // max(1, args.gpus))
+                                  if args.global_batch else 1),
         "cpu_baseline": {"value": value, "unit": UNIT, "cores": r["cores"], "kind": "port", "sample": r["sample"],
-                         "single_thread": single_thread_baseline(shape, args.cpu_sample_flops / 20)},
+                         "single_thread": single_thread_baseline(shape, args.cpu_sample_flops / 40)},
         "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
         "note": "CPU restatement of reference::matmul (crates/staleynet-cuda/src/reference.rs:18-38); the "
                 "reference's Rust CPU path cannot be built here (no Rust toolchain)",
@@ -246,37 +293,99 @@ def run_reference(args, shape, rank: int, world: int) -> int:
     return 0
 
 
+SEQ_LEN = 2048
+MICRO_SEQUENCES = 32   # sequences per micro-batch: config 3's 32 x 2048 tokens
+
+
+def micro_batch_plan(global_sequences: int, world: int, rank: int) -> tuple[int, int, int]:
+    """(first global micro-batch, micro-batches of this rank, micro-batches of the whole step).
+
+    global_sequences > 0 (config 5): the global batch is split by whole sequences (shard_sequences) and each rank
+    runs its sequences as 32 x 2048 micro-batches that accumulate into dW; the total work is fixed as N grows.
+    global_sequences == 0: one micro-batch per rank (global batch 32 x N; per-GPU work fixed as N grows)."""
+    from staleynet_b200.data_parallel import shard_sequences
+
+    if global_sequences == 0:
+        return rank, 1, world
+    shard = shard_sequences(global_sequences, world, rank)
+    if shard.first % MICRO_SEQUENCES or shard.count % MICRO_SEQUENCES or shard.count == 0:
+        raise SystemExit(f"--global-batch {global_sequences} over {world} ranks gives rank {rank} sequences "
+                         f"[{shard.first}, {shard.first + shard.count}), not whole {MICRO_SEQUENCES}-sequence "
+                         f"micro-batches")
+    return shard.first // MICRO_SEQUENCES, shard.count // MICRO_SEQUENCES, global_sequences // MICRO_SEQUENCES
+
+
+def relative_frobenius(expected, actual) -> float:
+    import torch
+
+    e = expected.double()
+    return float(torch.linalg.vector_norm(actual.double() - e) / torch.clamp(torch.linalg.vector_norm(e), min=1e-300))
+
+
+def gemm_breakdown(step, ev_steps, peak_sus: float, peak_burst: float) -> dict:
+    """Per GEMM of the step: launches, device ms per step, TFLOP/s from the CUDA events around each launch, and
+    that rate as a percentage of the measured bf16 peaks."""
+    table = {}
+    n_steps = len(ev_steps)
+    for ev_micro in ev_steps:
+        for pairs in ev_micro:
+            for (name, flops, _), (a, b) in zip(step.plan, pairs):
+                row = table.setdefault(name, {"launches": 0, "ms": 0.0, "flops": 0.0})
+                row["launches"] += 1
+                row["ms"] += a.elapsed_time(b)
+                row["flops"] += flops
+    out = {}
+    total_ms = sum(r["ms"] for r in table.values())
+    for name, row in table.items():
+        tflops = row["flops"] / (row["ms"] / 1e3) / 1e12
+        out[name] = {"launches_per_step": row["launches"] // n_steps, "ms_per_step": row["ms"] / n_steps,
+                     "tflops": tflops, "pct_sustained": 100.0 * tflops / peak_sus,
+                     "pct_burst": 100.0 * tflops / peak_burst, "share": row["ms"] / total_ms}
+    return out
+
+
 def run_ours(args, shape, rank: int, world: int, local_rank: int) -> int:
     import torch
     import torch.distributed as dist
 
-    from staleynet_b200.data_parallel import OverlappedAllReduce
+    from staleynet_b200.data_parallel import OverlappedAllReduce, global_grad_scale
     from staleynet_b200.step import TrainingStepGemms
 
     torch.cuda.set_device(local_rank)
     device = torch.device("cuda", local_rank)
     stream = torch.cuda.current_stream(device)
-    step = TrainingStepGemms(shape, device, seed=1234 + rank)
+    first_micro, n_micro, global_micro = micro_batch_plan(args.global_batch, world, rank)
+    # The loss-gradient scale counts the valid targets of the whole global batch (training.rs:214-221 counts the
+    # local batch; every target drawn by below(1024) is valid).
+    scale = global_grad_scale(n_micro * shape.tokens, shape.codebooks) if world > 1 else \
+        1.0 / (n_micro * shape.tokens * shape.codebooks)
+    step = TrainingStepGemms(shape, device, micro_batches=n_micro, first_micro_batch=first_micro, grad_scale=scale,
+                             deterministic=args.deterministic)
     handle = stream.cuda_stream
-
     reducer = OverlappedAllReduce(compute_stream=stream) if world > 1 else None
 
-    def one_step(events=None):
-        step.zero_grads()
+    def on_block(b):
+        # The head's gradient is complete before block L-1's; both go out once block L-1's backward is queued.
+        if b == shape.blocks - 1:
+            reducer.submit(step.head_grad)
+        reducer.submit(step.block_grad_flat[b])
 
-        def on_block(b):
-            # The head's gradient is complete before block L-1's; both go out once block L-1's backward is queued.
-            if b == shape.blocks - 1:
-                reducer.submit(step.head_grad)
-            reducer.submit(step.block_grad_flat[b])
+    hook = on_block if world > 1 else None
 
-        step.run(handle, on_block_done=on_block if world > 1 else None, events=events)
+    def finish(marks=None):
+        """Ends a step: the compute stream waits for every all-reduce. With `marks` (two events) the exposed
+        communication is bracketed: from the last GEMM's completion to the last all-reduce's."""
+        if marks is not None:
+            marks[0].record(stream)
         if reducer is not None:
             reducer.wait()
+        if marks is not None:
+            marks[1].record(stream)
 
     # Warm-up (also configures every kernel variant and builds the NCCL communicator).
     for _ in range(args.warmup):
-        one_step()
+        step.run_step(handle, on_block_done=hook)
+        finish()
     torch.cuda.synchronize()
     if world > 1:
         dist.barrier()
@@ -284,105 +393,125 @@ def run_ours(args, shape, rank: int, world: int, local_rank: int) -> int:
 
     # Timed region: device-resident inputs.
     n_launch = step.launches_per_step()
-    ev_pairs = [[(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
-                 for _ in range(n_launch)] for _ in range(args.steps)]
+    timed = lambda: torch.cuda.Event(enable_timing=True)  # noqa: E731
+    ev_steps = [[[(timed(), timed()) for _ in range(n_launch)] for _ in range(n_micro)] for _ in range(args.steps)]
+    comm_marks = [(timed(), timed()) for _ in range(args.steps)]
     clocks = ClockSampler(local_rank)
     clocks.start()
-    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    start, end = timed(), timed()
     start.record(stream)
     for k in range(args.steps):
-        one_step(events=ev_pairs[k])
+        step.run_step(handle, on_block_done=hook, events=ev_steps[k])
+        finish(comm_marks[k])
     end.record(stream)
     torch.cuda.synchronize()
     clock_info = clocks.stop()
     if world > 1:
         dist.barrier()
     ms_total = start.elapsed_time(end)
-    kernel_ms = sum(a.elapsed_time(b) for pairs in ev_pairs for a, b in pairs)
-    if args.breakdown and rank == 0:
-        table = {}
-        for pairs in ev_pairs:
-            for (name, flops, _), (a, b) in zip(step.plan, pairs):
-                row = table.setdefault(name, {"launches": 0, "ms": 0.0, "flops": 0.0})
-                row["launches"] += 1
-                row["ms"] += a.elapsed_time(b)
-                row["flops"] += flops
-        for row in table.values():
-            row["tflops"] = row["flops"] / (row["ms"] / 1e3) / 1e12
-            row["ms_per_step"] = row["ms"] / args.steps
-            row["share"] = row["ms"] / kernel_ms
-        Path(args.breakdown).write_text(json.dumps(table, indent=1) + "\n")
+    kernel_ms = sum(a.elapsed_time(b) for ev_micro in ev_steps for pairs in ev_micro for a, b in pairs)
+    exposed_ms = sum(a.elapsed_time(b) for a, b in comm_marks) / args.steps
 
-    # End-to-end: the step's input activations come from pinned host memory every step and one result value is
-    # read back; everything else as above. As a training loop does, the next step's input is copied on a separate
-    # stream into a second buffer while the current step runs (each step's copy still starts inside the timed
-    # region; the first one is not overlapped).
-    host_x = torch.empty(step.x_in.numel(), dtype=step.x_in.dtype, pin_memory=True)
-    host_x.copy_(step.x_in.cpu())
-    host_out = torch.empty(1, dtype=torch.float32, pin_memory=True)
+    # End-to-end: every micro-batch's input activations come from pinned host memory and the step's per-codebook
+    # loss sums are read back (the reference downloads its losses every step, training.rs:232). As a training loop
+    # does, the next micro-batch's input is copied on a separate stream into the other of two buffers while the
+    # current one runs (every copy starts inside the timed region; the first one is not overlapped).
+    host_x = torch.empty(step.inputs.shape, dtype=step.inputs.dtype, pin_memory=True)
+    host_x.copy_(step.inputs.cpu())
+    host_loss = torch.empty(step.loss_sums.shape, dtype=torch.float32, pin_memory=True)
     h2d = host_x.numel() * host_x.element_size()
-    d2h = host_out.numel() * host_out.element_size()
+    d2h = host_loss.numel() * host_loss.element_size()
     torch.cuda.synchronize()
     if world > 1:
         dist.barrier()
-    e_start, e_end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e_start, e_end = timed(), timed()
     copy_stream = torch.cuda.Stream(device)
-    inputs = [step.x_in, torch.empty_like(step.x_in)]
+    bufs = [torch.empty_like(step.x_in), torch.empty_like(step.x_in)]
     ready = [torch.cuda.Event(), torch.cuda.Event()]
     released = [torch.cuda.Event(), torch.cuda.Event()]
     e_start.record(stream)
     copy_stream.wait_event(e_start)
+    total_micro = args.steps * n_micro
 
     def upload(i):
         b = i % 2
         with torch.cuda.stream(copy_stream):
             if i >= 2:
-                copy_stream.wait_event(released[b])   # step i-2, which read this buffer, has finished
-            inputs[b].copy_(host_x, non_blocking=True)
+                copy_stream.wait_event(released[b])   # micro-batch i-2, which read this buffer, has finished
+            bufs[b].copy_(host_x[i % n_micro], non_blocking=True)
             ready[b].record(copy_stream)
 
     upload(0)
-    for i in range(args.steps):
-        if i + 1 < args.steps:
-            upload(i + 1)
-        stream.wait_event(ready[i % 2])
-        step.use_input(inputs[i % 2])
-        one_step()
-        released[i % 2].record(stream)
-        host_out.copy_(step.head_grad[:1], non_blocking=True)
+    for k in range(args.steps):
+        step.zero_grads()
+        for m in range(n_micro):
+            i = k * n_micro + m
+            if i + 1 < total_micro:
+                upload(i + 1)
+            stream.wait_event(ready[i % 2])
+            step.run(handle, on_block_done=hook if m == n_micro - 1 else None, micro_batch=m, x=bufs[i % 2])
+            released[i % 2].record(stream)
+        finish()
+        host_loss.copy_(step.loss_sums, non_blocking=True)
     e_end.record(stream)
     torch.cuda.synchronize()
-    step.use_input(step.x_in)
     if world > 1:
         dist.barrier()
     e2e_ms_total = e_start.elapsed_time(e_end)
+    local_loss = float(host_loss.sum()) / (n_micro * shape.tokens * shape.codebooks)
 
-    stats = torch.tensor([ms_total, e2e_ms_total, kernel_ms], device=device, dtype=torch.float64)
+    stats = torch.tensor([ms_total, e2e_ms_total, kernel_ms, exposed_ms], device=device, dtype=torch.float64)
     if world > 1:
         dist.all_reduce(stats, op=dist.ReduceOp.MAX)
-    ms_total, e2e_ms_total, kernel_ms = stats.tolist()
+    ms_total, e2e_ms_total, kernel_ms, exposed_max = stats.tolist()
+
+    # Data-parallel parity: the all-reduced gradients of one step against rank 0 recomputing the whole global batch
+    # alone through the same kernels (every micro-batch rebuilt from the seeded streams, no collective).
+    dp_parity = None
+    if world > 1:
+        step.run_step(handle, on_block_done=hook)
+        finish()
+        check_blocks = sorted({0, shape.blocks - 1})
+        reduced = [step.head_grad.clone()] + [step.block_grad_flat[b].clone() for b in check_blocks]
+        torch.cuda.synchronize()
+        if rank == 0:
+            step.zero_grads()
+            for g in range(global_micro):
+                step.load_micro_batch(g, step.inputs[0], step.targets[0])
+                step.run(handle, micro_batch=0)
+            torch.cuda.synchronize()
+            alone = [step.head_grad] + [step.block_grad_flat[b] for b in check_blocks]
+            errs = [relative_frobenius(x, r) for x, r in zip(alone, reduced)]
+            names = ["head"] + [f"block{b}" for b in check_blocks]
+            dp_parity = {"relative_frobenius": dict(zip(names, errs)), "max": max(errs), "tolerance": 1e-2,
+                         "ok": max(errs) <= 1e-2,
+                         "how": f"all-reduced dW of one step vs rank 0 alone over all {global_micro} micro-batches"}
+        dist.barrier()
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         cpu = cpu_baseline(shape, budget_flops=args.cpu_sample_flops)
-        cpu["single_thread"] = single_thread_baseline(shape, args.cpu_sample_flops / 20)
+        cpu["single_thread"] = single_thread_baseline(shape, args.cpu_sample_flops / 40)
 
     if rank == 0:
         peaks, source = load_peaks()
         traffic = load_traffic(shape)
-        flops_step = step.plan_flops
-        ms_step = ms_total / args.steps
-        value = flops_step * world * args.steps / (ms_total / 1e3) / 1e12
-        e2e_value = flops_step * world * args.steps / (e2e_ms_total / 1e3) / 1e12
-        achieved = flops_step * args.steps / (kernel_ms / 1e3) / 1e12
         peak_sus = float(peaks.get("bf16_tflops_sustained", FALLBACK_PEAKS["bf16_tflops_sustained"]))
         peak_burst = float(peaks.get("bf16_tflops", FALLBACK_PEAKS["bf16_tflops"]))
+        flops_rank = step.plan_flops * n_micro
+        ms_step = ms_total / args.steps
+        value = flops_rank * world * args.steps / (ms_total / 1e3) / 1e12
+        e2e_value = flops_rank * world * args.steps / (e2e_ms_total / 1e3) / 1e12
+        achieved = flops_rank * args.steps / (kernel_ms / 1e3) / 1e12
+        launches = n_launch * n_micro
         line = {
             "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
-            "warmup": args.warmup, "ms_per_step": ms_step, "higher_is_better": True, "scaling": "weak",
+            "warmup": args.warmup, "ms_per_step": ms_step, "higher_is_better": True,
+            "scaling": "strong" if args.global_batch else "weak",
             "vs_baseline": None, "dtype": "bf16", "data": "synthetic: " + GENERATOR + "; activations "
-                                                           "N(0,1), weights N(0,1/sqrt(768))",
-            "config": workload_config(shape, world),
+                                                           "N(0,1), weights N(0,1/sqrt(768)), targets below(1024)",
+            "config": dict(workload_config(shape, world, args.global_batch, n_micro),
+                           **({"deterministic": True} if args.deterministic else {})),
             "pct_bf16_peak_sustained": 100.0 * (value / world) / peak_sus,
             "pct_bf16_peak_burst": 100.0 * (value / world) / peak_burst,
             "roofline": {
@@ -390,20 +519,33 @@ def run_ours(args, shape, rank: int, world: int, local_rank: int) -> int:
                 "frac": achieved / peak_sus, "traffic": traffic.get("traffic_bytes_per_launch"),
                 "traffic_source": traffic.get("source"),
                 "algorithmic_bytes_per_launch": traffic.get("algorithmic_bytes_per_launch"),
-                "achieved_hbm_gbs": (traffic["algorithmic_bytes_per_launch"] * n_launch * args.steps /
+                "achieved_hbm_gbs": (traffic["algorithmic_bytes_per_launch"] * launches * args.steps /
                                      (kernel_ms / 1e3) / 1e9) if "algorithmic_bytes_per_launch" in traffic else None,
                 "hbm_peak_gbs": float(peaks.get("hbm_gbs", FALLBACK_PEAKS["hbm_gbs"])),
-                "kernel": "snb::tc_gemm_kernel (all launches of one step on rank 0)",
+                "kernel": "snb::tc_gemm_kernel / tc_gemm_pair_kernel (all GEMM launches of a step on rank 0)",
                 "peak_source": f"{source} bf16_tflops_sustained (kernel timed inside a long step); "
                                f"burst {peak_burst}",
-                "launches_per_step": n_launch,
-                "flops_per_step": flops_step,
+                "launches_per_step": launches,
+                "flops_per_step": flops_rank,
             },
+            "gemms": gemm_breakdown(step, ev_steps, peak_sus, peak_burst),
             "e2e": {"value": e2e_value, "unit": UNIT, "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
-                    "ms_per_step": e2e_ms_total / args.steps, "path": "snb_gemm C ABI via ctypes"},
-            "gpu_launches": n_launch * args.steps,
+                    "ms_per_step": e2e_ms_total / args.steps,
+                    "path": "snb_gemm + snb_codebook_cross_entropy C ABI via ctypes; inputs from pinned host memory, "
+                            "per-codebook loss sums read back every step", "loss": local_loss},
+            "gpu_launches": (launches + n_micro) * args.steps,
             "clocks": clock_info,
         }
+        if world > 1:
+            line["communication"] = {
+                "exposed_ms_per_step": exposed_max,
+                "what": "per step, from the last GEMM's completion to the last gradient all-reduce's (CUDA events "
+                        "on the compute stream; max over ranks)",
+                "all_reduce_bytes_per_step": 4 * (sum(t.numel() for t in step.block_grad_flat) +
+                                                  step.head_grad.numel()),
+                "collective": "NCCL all-reduce (sum, f32) per bucket: head, then blocks L-1..0, on a side stream",
+            }
+            line["dp_parity"] = dp_parity
         if cpu is not None:
             line["cpu_baseline"] = {k: cpu[k] for k in ("value", "unit", "cores", "kind", "sample", "single_thread")}
         print(json.dumps(line), flush=True)
@@ -868,9 +1010,13 @@ def main(argv=None) -> int:
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--tokens", type=int, default=32 * 2048, help="tokens per GPU (default: BASELINE config 3)")
-    ap.add_argument("--cpu-sample-flops", type=float, default=20e9)
+    ap.add_argument("--cpu-sample-flops", type=float, default=40e9)
+    ap.add_argument("--deterministic", action="store_true",
+                    help="step workload: every GEMM with SNB_GEMM_DETERMINISTIC (fixed-order split-K sums)")
+    ap.add_argument("--global-batch", type=int, default=256,
+                    help="sequences of 2048 tokens per step over all GPUs (config 5: 256, run as 32-sequence "
+                         "micro-batches); 0 = one 32-sequence micro-batch per GPU")
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--breakdown", default=None, help="write per-GEMM kernel times of the timed region here (JSON)")
     ap.add_argument("--workload", choices=["step", "attention", "head", "optimizer", "norm"], default="step",
                     help="step: the cfg3 training-step GEMMs (default); attention: the cfg4 attention layer; "
                          "head: the cfg3 output layer's forward + cross-entropy; optimizer: the cfg3 AdamW step; "

@@ -14,6 +14,9 @@
  *                                  `add_scaled` residual adds (kernels/elementwise.rs:37), fused into the epilogue
  *   snb_causal_softmax          <- `Gpu::causal_softmax`, crates/staleynet-cuda/src/ops/attention.rs:61-81
  *   snb_softmax_backward        <- `Gpu::softmax_backward`, crates/staleynet-cuda/src/ops/attention.rs:84-100
+ *   snb_head_layout             <- `HeadLayout`, crates/staleynet-cuda/src/kernels/attention.rs:19-41
+ *   snb_split_heads             <- `Gpu::split_heads`, crates/staleynet-cuda/src/ops/attention.rs:20-36
+ *   snb_merge_heads             <- `Gpu::merge_heads`, crates/staleynet-cuda/src/ops/attention.rs:38-52
  *
  * Conventions shared by every entry point:
  *   - All pointers are caller-owned device pointers; nothing is allocated or freed inside a call.
@@ -60,6 +63,21 @@ typedef struct snb_product {
     float scale;
     uint32_t accumulate; /* 1: C += scale*A*B; 0: C = scale*A*B (`WriteMode::flag`, ops/mod.rs:36-43) */
 } snb_product;
+
+/* Where a group of attention heads lives in two layouts. Packed: [batch * time, width], head h of a row at columns
+ * column_offset + h * head_dim ..; head-major: [batch, heads, time_capacity, head_dim], the moved time steps at
+ * rows time_offset .. (which lets the same copy append to a key/value cache). Byte-identical to the reference's
+ * `HeadLayout` (crates/staleynet-cuda/src/kernels/attention.rs:19-41, repr(C), 8 x usize = 64 bytes). */
+typedef struct snb_head_layout {
+    uint64_t batch;
+    uint64_t time;
+    uint64_t heads;
+    uint64_t head_dim;
+    uint64_t width;
+    uint64_t column_offset;
+    uint64_t time_capacity;
+    uint64_t time_offset;
+} snb_head_layout;
 
 /* Arithmetic of a product. Maps `MatmulKernel` (device.rs:38-67): Naive/Tiled/Blocked compute exact f32
  * (tolerance 1e-5) -> SNB_PRECISION_F32; TensorCore rounds inputs to TF32 (tolerance 2e-3) -> SNB_PRECISION_TF32.
@@ -164,15 +182,53 @@ typedef struct snb_gemm_args {
     const void* gelu_input;     /* GELU_GRAD: the forward pre-activation, laid out like the output */
     const void* residual;       /* laid out like the output, same type as the output; or NULL */
     int32_t causal;             /* SNB_CAUSAL_*: structure of a batched attention product (work it may skip) */
-    int32_t reserved;
+    int32_t flags;              /* SNB_GEMM_* bits; 0 for the default behaviour */
     int64_t causal_offset;      /* query q sees keys 0..=q+causal_offset (the softmax's query_offset) */
     const float* row_scale;     /* [rows] multiplier of each output row before the bias (count 1 only), or NULL:
                                  * with the RMSNorm gain folded into the right operand (snb_scale_rows) and
                                  * row_scale = the rows' 1/rms (snb_rms_norm_stats), left * right = rms_norm(left)
                                  * times the unscaled right operand, without a normalised copy of left. */
+    /* Head-major operands (count 1; NULL = off), which fuse the reference's split_heads / merge_heads permutes
+     * (crates/staleynet-model/src/layers/attention.rs:201-214, 233, 262-264) into the products around attention.
+     * left_heads: `left` is the head-major form ([batch, heads, time_capacity, head_dim]) of the packed tensor
+     * [batch * time, width] (width = heads * head_dim, column_offset 0) that product->left describes, RowMajor
+     * (rows = batch * time, inner = width) or Transposed (rows = width, inner = batch * time); left_len counts the
+     * head-major tensor. E.g. the attention output projection reading the attention context, and its weight
+     * gradient. Needs head_dim a multiple of 64 (bf16) / 32 (tf32) and time a multiple of 128 (RowMajor) or
+     * 64 (bf16) / 32 (tf32) (Transposed).
+     * output_heads: the output [rows, cols] = [batch * time, cols] is written as cols / (heads * head_dim)
+     * head-major tensors [batch, heads, time_capacity, head_dim] one after the other (output_heads->width = cols,
+     * column_offset 0): column (p * heads + h) * head_dim + d of row b * time + s goes to element
+     * ((b * heads + h) * time_capacity + time_offset + s) * head_dim + d of tensor p. E.g. the fused QKV
+     * projection writing queries, keys and values head-major. Needs an overwrite without residual,
+     * pre-activation or GELU input, head_dim a multiple of 64 (bf16 output) / 32 (f32) and time a multiple of 32;
+     * output_len counts all the head-major tensors.
+     * Both run on the tensor-core kernel only; other shapes return SNB_ERR_UNSUPPORTED (use snb_permute_heads). */
+    const snb_head_layout* left_heads;
+    const snb_head_layout* output_heads;
 } snb_gemm_args;
 
 SNB_API int snb_gemm(void* stream, const snb_gemm_args* args);
+
+/* snb_gemm_args.flags bits.
+ * Run-to-run reproducibility. By default a product whose K range the tensor-core kernel splits across CTAs (f32
+ * outputs without activation, when its cost model finds idle SMs otherwise, e.g. weight gradients with K = tokens)
+ * adds the splits' partial sums into the output with TMA reduce-adds in arrival order, so two runs on the same
+ * inputs can differ in the last bits of those outputs. The reference's sum is a fixed-order f32 loop
+ * (crates/staleynet-cuda/src/reference.rs:18-38). With SNB_GEMM_DETERMINISTIC every output element is summed in a
+ * fixed order: each split stores its partial tile into its own slab of a stream-ordered workspace (cudaMallocAsync /
+ * cudaFreeAsync on the call's stream, splits x rows x cols floats), then one kernel adds the slabs into the output
+ * in split order (after the output's previous contents when accumulating); batched products (count > 1) are not
+ * split at all. Results are then bit-identical between runs on the same device; the cost is the slabs' traffic.
+ * Unsplit products, the SIMT kernel and the attention-product paths are deterministic either way. */
+enum {
+    SNB_GEMM_DETERMINISTIC = 1
+};
+
+/* Sets, for the calling thread, whether snb_matmul, snb_matmul_bf16 and snb_gemm run as with SNB_GEMM_DETERMINISTIC
+ * (enabled != 0) — the switch for callers of the f32 drop-in, which has no flags argument. Returns the previous
+ * setting (0 or 1). Off by default. No reference counterpart. */
+SNB_API int snb_set_deterministic(int32_t enabled);
 
 /* In-place causal softmax of scores [rows, keys] (rows = matrices * queries): query q of each matrix sees keys
  * 0..=q+query_offset, scaled by `scale`, later keys become 0. Replaces `Gpu::causal_softmax`
@@ -196,6 +252,36 @@ SNB_API int snb_causal_softmax_bf16(void* stream, float* scores, uint64_t scores
  * wherever the latter's inputs are finite. Optionally also writes grad as bf16 (grad_bf16, may be NULL). */
 SNB_API int snb_causal_softmax_backward(void* stream, const float* probabilities, float* grad, uint64_t rows,
                                         uint64_t queries, uint64_t cols, uint64_t query_offset, uint16_t* grad_bf16);
+
+/* Packed columns -> head-major tensor (f32): replaces `Gpu::split_heads` (crates/staleynet-cuda/src/ops/attention.rs:
+ * 20-36; kernel kernels/attention.rs:112-121). Element (b, h, s, d) moves from packed[(b * time + s) * width +
+ * column_offset + h * head_dim + d] to head_major[((b * heads + h) * time_capacity + time_offset + s) * head_dim + d].
+ * The reference's checks (`check_layout`, ops/attention.rs:11-18) in its order and words, each returning
+ * SNB_ERR_INVALID_ARGUMENT: "HeadLayout: time range exceeds capacity" (time_offset + time > time_capacity),
+ * "HeadLayout: packed tensor too small" (packed_len < batch * time * width), "HeadLayout: head-major tensor too
+ * small" (head_major_len < batch * heads * time_capacity * head_dim). Also refused: a head that does not fit in the
+ * packed row (column_offset + heads * head_dim > width). */
+SNB_API int snb_split_heads(void* stream, const float* packed, uint64_t packed_len, float* head_major,
+                            uint64_t head_major_len, const snb_head_layout* layout);
+
+/* Head-major tensor -> packed columns (f32), other columns untouched: replaces `Gpu::merge_heads`
+ * (ops/attention.rs:38-52; kernel kernels/attention.rs:129-138). The same checks as snb_split_heads, in the same
+ * order (the reference runs one check_layout for both directions). */
+SNB_API int snb_merge_heads(void* stream, const float* head_major, uint64_t head_major_len, float* packed,
+                            uint64_t packed_len, const snb_head_layout* layout);
+
+/* Directions of snb_permute_heads. */
+enum {
+    SNB_HEADS_SPLIT = 0, /* packed -> head-major */
+    SNB_HEADS_MERGE = 1  /* head-major -> packed */
+};
+
+/* snb_split_heads / snb_merge_heads with element types of their own: src_type and dst_type SNB_TYPE_F32 or
+ * SNB_TYPE_BF16 (f32 -> bf16 rounds to nearest even). E.g. the f32 query/key/value gradients of
+ * snb_causal_attention_backward merged into the bf16 packed gradient of the QKV projection. Same checks as the two
+ * drop-ins. No reference counterpart. */
+SNB_API int snb_permute_heads(void* stream, int32_t direction, const void* src, int32_t src_type, uint64_t src_len,
+                              void* dst, int32_t dst_type, uint64_t dst_len, const snb_head_layout* layout);
 
 /* Message of the last failed call on the calling thread ("" if none). Valid until the next call. */
 SNB_API const char* snb_last_error(void);
@@ -281,6 +367,16 @@ SNB_API int snb_cross_entropy(void* stream, const float* logits, uint64_t rows, 
 SNB_API int snb_head_cross_entropy(void* stream, const snb_gemm_args* head, const uint32_t* targets,
                                    uint64_t targets_len, uint64_t codebooks, uint64_t codebook_size,
                                    const float* grad_scales, float* loss_sums, void* logits_grad, int32_t grad_type);
+
+/* The loss half of snb_head_cross_entropy on logits a caller has already computed: every codebook's softmax
+ * cross-entropy of logits [rows, codebooks * codebook_size] (logits_type SNB_TYPE_F32 or SNB_TYPE_BF16) in one
+ * launch, with the same targets, grad_scales, loss_sums (zeroed first) and logits_grad (may be logits itself when
+ * grad_type equals logits_type) as snb_head_cross_entropy. Replaces the reference's `codebook_losses` loop of one
+ * `Gpu::cross_entropy` and one host download per codebook (crates/staleynet-model/src/training.rs:209-235). */
+SNB_API int snb_codebook_cross_entropy(void* stream, const void* logits, int32_t logits_type, uint64_t rows,
+                                       uint64_t codebooks, uint64_t codebook_size, const uint32_t* targets,
+                                       uint64_t targets_len, const float* grad_scales, float* loss_sums,
+                                       void* logits_grad, int32_t grad_type);
 
 /* ---------------------------------------------------------------------------------------------- RMSNorm, AdamW */
 

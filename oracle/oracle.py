@@ -184,6 +184,34 @@ def lcg_values(count: int, seed: int) -> np.ndarray:
     return out
 
 
+def head_indices(layout) -> tuple[np.ndarray, np.ndarray]:
+    """(packed index, head-major index) of every element a head permute moves, enumerated as `HeadLayout::element`
+    does (dim fastest, then step, head, batch) with `packed_index` / `head_major_index`
+    (crates/staleynet-cuda/src/kernels/attention.rs:71-96). `layout` has the eight HeadLayout fields."""
+    L = layout
+    e = np.arange(L.batch * L.heads * L.time * L.head_dim, dtype=np.int64)
+    dim = e % L.head_dim
+    step = (e // L.head_dim) % L.time
+    head = (e // (L.head_dim * L.time)) % L.heads
+    batch = e // (L.head_dim * L.time * L.heads)
+    packed = (batch * L.time + step) * L.width + L.column_offset + head * L.head_dim + dim
+    head_major = ((batch * L.heads + head) * L.time_capacity + L.time_offset + step) * L.head_dim + dim
+    return packed, head_major
+
+
+def split_heads(packed: np.ndarray, head_major: np.ndarray, layout) -> None:
+    """`split_heads` (kernels/attention.rs:112-121): head_major[head_major_index] = packed[packed_index]."""
+    p, h = head_indices(layout)
+    head_major[h] = packed[p]
+
+
+def merge_heads(head_major: np.ndarray, packed: np.ndarray, layout) -> None:
+    """`merge_heads` (kernels/attention.rs:129-138): packed[packed_index] = head_major[head_major_index]; other
+    columns untouched."""
+    p, h = head_indices(layout)
+    packed[p] = head_major[h]
+
+
 def gelu(x: np.ndarray) -> np.ndarray:
     x = np.ascontiguousarray(x, dtype=np.float32)
     out = np.empty_like(x)

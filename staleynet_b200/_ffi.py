@@ -29,6 +29,11 @@ CAUSAL_SKIP_MASKED_OUTPUT = 1
 CAUSAL_LEFT_MASKED = 2
 CAUSAL_LEFT_T_MASKED = 3
 
+GEMM_DETERMINISTIC = 1   # snb_gemm_args.flags: split-K partials summed in a fixed order
+
+HEADS_SPLIT = 0          # snb_permute_heads directions
+HEADS_MERGE = 1
+
 OK = 0
 ERR_LEFT_TOO_SMALL = 1
 ERR_RIGHT_TOO_SMALL = 2
@@ -49,6 +54,7 @@ EXPORTED_SYMBOLS = (
     "snb_matmul",
     "snb_matmul_bf16",
     "snb_gemm",
+    "snb_set_deterministic",
     "snb_causal_softmax",
     "snb_softmax_backward",
     "snb_causal_softmax_bf16",
@@ -61,6 +67,10 @@ EXPORTED_SYMBOLS = (
     "snb_causal_attention_backward_noalloc",
     "snb_cross_entropy",
     "snb_head_cross_entropy",
+    "snb_codebook_cross_entropy",
+    "snb_split_heads",
+    "snb_merge_heads",
+    "snb_permute_heads",
     "snb_rms_norm_forward",
     "snb_rms_norm_backward",
     "snb_rms_norm_stats",
@@ -110,6 +120,23 @@ class AdamWTensor(ctypes.Structure):
                 ("second_moment", c_void_p), ("count", c_uint64), ("weight_decay", c_float), ("reserved", c_uint32)]
 
 
+class HeadLayout(ctypes.Structure):
+    """snb_head_layout: the reference's `HeadLayout` (crates/staleynet-cuda/src/kernels/attention.rs:19-41), 8 x u64."""
+
+    _fields_ = [(name, c_uint64) for name in ("batch", "time", "heads", "head_dim", "width", "column_offset",
+                                               "time_capacity", "time_offset")]
+
+    @staticmethod
+    def dense(batch, time, heads, head_dim, width, column_offset) -> "HeadLayout":
+        """`HeadLayout::dense` (kernels/attention.rs:62-64): capacity = time, offset 0."""
+        return HeadLayout(batch, time, heads, head_dim, width, column_offset, time, 0)
+
+    def in_cache(self, capacity, offset) -> "HeadLayout":
+        """`HeadLayout::in_cache` (kernels/attention.rs:67-69): the same heads in a cache of `capacity` steps."""
+        return HeadLayout(self.batch, self.time, self.heads, self.head_dim, self.width, self.column_offset, capacity,
+                          offset)
+
+
 class GemmArgs(ctypes.Structure):
     _fields_ = [
         ("product", Product),
@@ -131,14 +158,17 @@ class GemmArgs(ctypes.Structure):
         ("gelu_input", c_void_p),
         ("residual", c_void_p),
         ("causal", c_int32),
-        ("reserved", c_int32),
+        ("flags", c_int32),
         ("causal_offset", ctypes.c_int64),
         ("row_scale", c_void_p),
+        ("left_heads", POINTER(HeadLayout)),
+        ("output_heads", POINTER(HeadLayout)),
     ]
 
 
 assert ctypes.sizeof(Operand) == 24
 assert ctypes.sizeof(Product) == 88
+assert ctypes.sizeof(HeadLayout) == 64
 
 _lock = threading.Lock()
 _lib: ctypes.CDLL | None = None
@@ -162,6 +192,8 @@ def load() -> ctypes.CDLL:
         lib.snb_matmul_bf16.restype = c_int
         lib.snb_gemm.argtypes = [c_void_p, POINTER(GemmArgs)]
         lib.snb_gemm.restype = c_int
+        lib.snb_set_deterministic.argtypes = [c_int32]
+        lib.snb_set_deterministic.restype = c_int
         lib.snb_causal_softmax.argtypes = [c_void_p, c_void_p, c_uint64, c_uint64, c_uint64, c_uint64, c_float,
                                            c_uint64]
         lib.snb_causal_softmax.restype = c_int
@@ -195,6 +227,16 @@ def load() -> ctypes.CDLL:
         lib.snb_head_cross_entropy.argtypes = [c_void_p, POINTER(GemmArgs), c_void_p, c_uint64, c_uint64, c_uint64,
                                                c_void_p, c_void_p, c_void_p, c_int32]
         lib.snb_head_cross_entropy.restype = c_int
+        lib.snb_codebook_cross_entropy.argtypes = [c_void_p, c_void_p, c_int32, c_uint64, c_uint64, c_uint64,
+                                                   c_void_p, c_uint64, c_void_p, c_void_p, c_void_p, c_int32]
+        lib.snb_codebook_cross_entropy.restype = c_int
+        lib.snb_split_heads.argtypes = [c_void_p, c_void_p, c_uint64, c_void_p, c_uint64, POINTER(HeadLayout)]
+        lib.snb_split_heads.restype = c_int
+        lib.snb_merge_heads.argtypes = [c_void_p, c_void_p, c_uint64, c_void_p, c_uint64, POINTER(HeadLayout)]
+        lib.snb_merge_heads.restype = c_int
+        lib.snb_permute_heads.argtypes = [c_void_p, c_int32, c_void_p, c_int32, c_uint64, c_void_p, c_int32, c_uint64,
+                                          POINTER(HeadLayout)]
+        lib.snb_permute_heads.restype = c_int
         lib.snb_rms_norm_forward.argtypes = [c_void_p, c_void_p, c_uint64, c_uint64, c_void_p, c_uint64, c_void_p,
                                              c_void_p, c_uint64, c_float]
         lib.snb_rms_norm_backward.argtypes = [c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p,

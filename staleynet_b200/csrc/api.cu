@@ -15,6 +15,7 @@ namespace {
 
 thread_local std::string t_last_error;
 thread_local int t_last_path = SNB_PATH_NONE;
+thread_local bool t_deterministic = false;   // snb_set_deterministic
 
 int fail(int code, const std::string& message) {
     t_last_error = message;
@@ -63,6 +64,11 @@ int run(cudaStream_t stream, const GemmRequest& r, uint64_t left_len, uint64_t r
         t_last_path = path;
         return SNB_OK;
     }
+    if (r.a_heads != nullptr || r.c_heads != nullptr)
+        return fail(SNB_ERR_UNSUPPORTED,
+                    err.empty() ? "gemm: head-major operands run on the sm_100 tensor-core kernel only (bf16 or tf32 "
+                                  "operands with unit-stride, 16-byte aligned layouts)"
+                                : "gemm: " + err);
     rc = simt_gemm(stream, r, &err);
     if (rc != SNB_OK) return fail(rc, err);
     t_last_path = SNB_PATH_SIMT;
@@ -71,6 +77,30 @@ int run(cudaStream_t stream, const GemmRequest& r, uint64_t left_len, uint64_t r
 
 std::mutex g_info_mu;
 std::vector<DeviceInfo> g_info;
+
+// a * b, or false when it overflows 64 bits.
+bool mul_ok(uint64_t a, uint64_t b, uint64_t* out) { return !__builtin_mul_overflow(a, b, out); }
+
+// Elements of a head-major tensor [batch, heads, time_capacity, head_dim], or false on overflow.
+bool head_major_elements(const snb_head_layout& L, uint64_t* n) {
+    uint64_t t = 0;
+    return mul_ok(L.batch, L.heads, &t) && mul_ok(t, L.time_capacity, &t) && mul_ok(t, L.head_dim, n);
+}
+
+// The reference's check_layout (crates/staleynet-cuda/src/ops/attention.rs:11-18), in its order and words, plus the
+// packed row holding the heads; empty string when the layout is usable.
+std::string check_head_layout(const snb_head_layout& L, uint64_t packed_len, uint64_t head_major_len) {
+    if (L.time_offset > L.time_capacity || L.time > L.time_capacity - L.time_offset)
+        return "HeadLayout: time range exceeds capacity";
+    uint64_t packed = 0, head_major = 0, span = 0;
+    if (!mul_ok(L.batch, L.time, &packed) || !mul_ok(packed, L.width, &packed) || packed_len < packed)
+        return "HeadLayout: packed tensor too small";
+    if (!head_major_elements(L, &head_major) || head_major_len < head_major)
+        return "HeadLayout: head-major tensor too small";
+    if (!mul_ok(L.heads, L.head_dim, &span) || L.column_offset > L.width || span > L.width - L.column_offset)
+        return "HeadLayout: heads exceed the packed row";
+    return "";
+}
 
 }  // namespace
 
@@ -110,7 +140,7 @@ using namespace snb;
 
 extern "C" {
 
-int snb_abi_version(void) { return 102; }
+int snb_abi_version(void) { return 105; }
 
 const char* snb_last_error(void) { return t_last_error.c_str(); }
 
@@ -132,6 +162,7 @@ int snb_matmul(void* stream, const snb_product* product, uint64_t count, const f
     r.B = right;
     r.C = output;
     r.aux_type = SNB_TYPE_F32;
+    r.deterministic = t_deterministic;
     return run(static_cast<cudaStream_t>(stream), r, left_len, right_len, output_len);
 }
 
@@ -149,7 +180,14 @@ int snb_matmul_bf16(void* stream, const snb_product* product, uint64_t count, co
     r.B = right;
     r.C = output;
     r.aux_type = SNB_TYPE_F32;
+    r.deterministic = t_deterministic;
     return run(static_cast<cudaStream_t>(stream), r, left_len, right_len, output_len);
+}
+
+int snb_set_deterministic(int32_t enabled) {
+    const int previous = t_deterministic ? 1 : 0;
+    t_deterministic = enabled != 0;
+    return previous;
 }
 
 int snb_gemm(void* stream, const snb_gemm_args* a) {
@@ -170,6 +208,39 @@ int snb_gemm(void* stream, const snb_gemm_args* a) {
         return fail(SNB_ERR_INVALID_ARGUMENT, "gemm: unknown causal mode or negative offset");
     if (a->row_scale != nullptr && a->count != 1)
         return fail(SNB_ERR_INVALID_ARGUMENT, "gemm: row_scale needs count 1");
+    if ((a->flags & ~SNB_GEMM_DETERMINISTIC) != 0) return fail(SNB_ERR_INVALID_ARGUMENT, "gemm: unknown flags");
+    const snb_product& gp = a->product;
+    if (a->left_heads != nullptr) {
+        const snb_head_layout& L = *a->left_heads;
+        uint64_t tokens = 0, n = 0;
+        const bool geometry = L.column_offset == 0 && L.heads > 0 && L.head_dim > 0 &&
+                              L.width == L.heads * L.head_dim && L.time_offset <= L.time_capacity &&
+                              L.time <= L.time_capacity - L.time_offset && mul_ok(L.batch, L.time, &tokens);
+        const bool row_major = gp.left.row_stride == L.width && gp.left.col_stride == 1 && gp.rows == tokens &&
+                               gp.inner == L.width;
+        const bool transposed = gp.left.row_stride == 1 && gp.left.col_stride == L.width && gp.rows == L.width &&
+                                gp.inner == tokens;
+        if (a->count != 1 || !geometry || !(row_major || transposed))
+            return fail(SNB_ERR_INVALID_ARGUMENT,
+                        "gemm: left_heads must describe the packed left operand [batch * time, heads * head_dim] "
+                        "(RowMajor or Transposed, column_offset 0, count 1)");
+        if (!head_major_elements(L, &n) || a->left_len < n)
+            return fail(SNB_ERR_LEFT_TOO_SMALL, "matmul: left operand too small");
+    }
+    if (a->output_heads != nullptr) {
+        const snb_head_layout& L = *a->output_heads;
+        uint64_t tokens = 0, n = 0, span = 0;
+        const bool geometry = L.column_offset == 0 && L.heads > 0 && L.head_dim > 0 && L.width == gp.cols &&
+                              mul_ok(L.heads, L.head_dim, &span) && gp.cols % span == 0 &&
+                              L.time_offset <= L.time_capacity && L.time <= L.time_capacity - L.time_offset &&
+                              mul_ok(L.batch, L.time, &tokens) && gp.rows == tokens;
+        if (a->count != 1 || !geometry)
+            return fail(SNB_ERR_INVALID_ARGUMENT,
+                        "gemm: output_heads must describe the output [batch * time, P * heads * head_dim] "
+                        "(width = cols, column_offset 0, count 1)");
+        if (!head_major_elements(L, &n) || !mul_ok(n, gp.cols / span, &n) || a->output_len < n)
+            return fail(SNB_ERR_OUTPUT_TOO_SMALL, "matmul: output too small");
+    }
     GemmRequest r{};
     r.p = a->product;
     r.count = a->count;
@@ -189,7 +260,57 @@ int snb_gemm(void* stream, const snb_gemm_args* a) {
     r.causal = a->causal;
     r.causal_offset = a->causal_offset;
     r.row_scale = a->row_scale;
+    r.deterministic = t_deterministic || (a->flags & SNB_GEMM_DETERMINISTIC) != 0;
+    r.a_heads = a->left_heads;
+    r.c_heads = a->output_heads;
     return run(static_cast<cudaStream_t>(stream), r, a->left_len, a->right_len, a->output_len);
+}
+
+namespace {
+
+int permute_heads_entry(const char* name, void* stream, bool split, const void* src, int32_t src_type,
+                        uint64_t src_len, void* dst, int32_t dst_type, uint64_t dst_len, const snb_head_layout* layout) {
+    t_last_path = SNB_PATH_NONE;
+    if (layout == nullptr) return fail(SNB_ERR_INVALID_ARGUMENT, std::string(name) + ": layout is null");
+    if ((src_type != SNB_TYPE_F32 && src_type != SNB_TYPE_BF16) || (dst_type != SNB_TYPE_F32 && dst_type != SNB_TYPE_BF16))
+        return fail(SNB_ERR_INVALID_ARGUMENT, std::string(name) + ": unknown element type");
+    const uint64_t packed_len = split ? src_len : dst_len;
+    const uint64_t head_major_len = split ? dst_len : src_len;
+    const std::string bad = check_head_layout(*layout, packed_len, head_major_len);
+    if (!bad.empty()) return fail(SNB_ERR_INVALID_ARGUMENT, bad);
+    const snb_head_layout& L = *layout;
+    if (L.batch == 0 || L.time == 0 || L.heads == 0 || L.head_dim == 0) {
+        t_last_path = SNB_PATH_EMPTY;
+        return SNB_OK;
+    }
+    if (src == nullptr || dst == nullptr) return fail(SNB_ERR_INVALID_ARGUMENT, std::string(name) + ": null pointer");
+    std::string err;
+    const int rc = permute_heads_launch(static_cast<cudaStream_t>(stream), split, src, src_type, dst, dst_type, L, &err);
+    if (rc != SNB_OK) return fail(rc, err);
+    t_last_path = SNB_PATH_SIMT;
+    return SNB_OK;
+}
+
+}  // namespace
+
+int snb_split_heads(void* stream, const float* packed, uint64_t packed_len, float* head_major, uint64_t head_major_len,
+                    const snb_head_layout* layout) {
+    return permute_heads_entry("split_heads", stream, true, packed, SNB_TYPE_F32, packed_len, head_major, SNB_TYPE_F32,
+                               head_major_len, layout);
+}
+
+int snb_merge_heads(void* stream, const float* head_major, uint64_t head_major_len, float* packed, uint64_t packed_len,
+                    const snb_head_layout* layout) {
+    return permute_heads_entry("merge_heads", stream, false, head_major, SNB_TYPE_F32, head_major_len, packed,
+                               SNB_TYPE_F32, packed_len, layout);
+}
+
+int snb_permute_heads(void* stream, int32_t direction, const void* src, int32_t src_type, uint64_t src_len, void* dst,
+                      int32_t dst_type, uint64_t dst_len, const snb_head_layout* layout) {
+    if (direction != SNB_HEADS_SPLIT && direction != SNB_HEADS_MERGE)
+        return fail(SNB_ERR_INVALID_ARGUMENT, "permute_heads: unknown direction");
+    return permute_heads_entry("permute_heads", stream, direction == SNB_HEADS_SPLIT, src, src_type, src_len, dst,
+                               dst_type, dst_len, layout);
 }
 
 int snb_causal_softmax_bf16(void* stream, float* scores, uint64_t scores_len, uint64_t rows, uint64_t queries,
@@ -318,6 +439,43 @@ int snb_cross_entropy(void* stream, const float* logits, uint64_t rows, uint64_t
     return SNB_OK;
 }
 
+namespace {
+
+// The loss half of the output layer: every codebook's cross-entropy of logits [rows, codebooks * codebook_size]
+// (logits_type) in one launch, loss_sums zeroed first. Arguments are checked by the callers.
+int codebook_losses(cudaStream_t s, const void* logits, int32_t logits_type, uint64_t rows, uint64_t codebooks,
+                    uint64_t codebook_size, const uint32_t* targets, const float* grad_scales, float* loss_sums,
+                    void* logits_grad, int32_t grad_type) {
+    cudaError_t e = cudaMemsetAsync(loss_sums, 0, codebooks * sizeof(float), s);
+    if (e != cudaSuccess) return fail(SNB_ERR_CUDA, cuda_message("cudaMemsetAsync(loss_sums)", e));
+    std::string err;
+    const int rc = cross_entropy_launch(s, logits, logits_type, rows, codebooks * codebook_size, targets, codebooks,
+                                        codebooks, 0, codebook_size, 0, grad_scales, 0.0f, nullptr, loss_sums,
+                                        logits_grad, grad_type, &err);
+    if (rc != SNB_OK) return fail(rc, err);
+    return SNB_OK;
+}
+
+// Checks shared by snb_head_cross_entropy and snb_codebook_cross_entropy (messages prefixed with `name`).
+int check_codebook_args(const char* name, uint64_t rows, uint64_t cols, const void* logits, int32_t logits_type,
+                        const uint32_t* targets, uint64_t targets_len, uint64_t codebooks, uint64_t codebook_size,
+                        const float* grad_scales, const float* loss_sums, const void* logits_grad,
+                        int32_t grad_type) {
+    const std::string n(name);
+    if (codebooks == 0 || codebook_size == 0 || cols / codebooks != codebook_size || cols % codebooks != 0)
+        return fail(SNB_ERR_INVALID_ARGUMENT, n + ": logits columns differ from codebooks * codebook_size");
+    if (grad_type != SNB_TYPE_F32 && grad_type != SNB_TYPE_BF16)
+        return fail(SNB_ERR_INVALID_ARGUMENT, n + ": unknown gradient type");
+    if (logits_grad == logits && grad_type != logits_type)
+        return fail(SNB_ERR_INVALID_ARGUMENT, n + ": an in-place gradient must have the logits' element type");
+    if (rows > 0 && targets_len / codebooks < rows) return fail(SNB_ERR_INVALID_ARGUMENT, n + ": too few targets");
+    if (rows > 0 && (targets == nullptr || grad_scales == nullptr || loss_sums == nullptr || logits_grad == nullptr))
+        return fail(SNB_ERR_INVALID_ARGUMENT, n + ": null pointer");
+    return SNB_OK;
+}
+
+}  // namespace
+
 int snb_head_cross_entropy(void* stream, const snb_gemm_args* head, const uint32_t* targets, uint64_t targets_len,
                            uint64_t codebooks, uint64_t codebook_size, const float* grad_scales, float* loss_sums,
                            void* logits_grad, int32_t grad_type) {
@@ -325,28 +483,40 @@ int snb_head_cross_entropy(void* stream, const snb_gemm_args* head, const uint32
     if (head == nullptr) return fail(SNB_ERR_INVALID_ARGUMENT, "head_cross_entropy: head is null");
     const snb_product& p = head->product;
     if (head->count != 1) return fail(SNB_ERR_INVALID_ARGUMENT, "head_cross_entropy: the head GEMM must have count 1");
-    if (codebooks == 0 || codebook_size == 0 || p.cols / codebooks != codebook_size || p.cols % codebooks != 0)
-        return fail(SNB_ERR_INVALID_ARGUMENT, "head_cross_entropy: logits columns differ from codebooks * codebook_size");
-    if (grad_type != SNB_TYPE_F32 && grad_type != SNB_TYPE_BF16)
-        return fail(SNB_ERR_INVALID_ARGUMENT, "head_cross_entropy: unknown gradient type");
-    if (logits_grad == head->output && grad_type != head->output_type)
-        return fail(SNB_ERR_INVALID_ARGUMENT,
-                    "head_cross_entropy: an in-place gradient must have the logits' element type");
-    if (p.rows > 0 && targets_len / codebooks < p.rows)
-        return fail(SNB_ERR_INVALID_ARGUMENT, "head_cross_entropy: too few targets");
-    if (p.rows > 0 && (targets == nullptr || grad_scales == nullptr || loss_sums == nullptr || logits_grad == nullptr))
-        return fail(SNB_ERR_INVALID_ARGUMENT, "head_cross_entropy: null pointer");
-    int rc = snb_gemm(stream, head);
+    int rc = check_codebook_args("head_cross_entropy", p.rows, p.cols, head->output, head->output_type, targets,
+                                 targets_len, codebooks, codebook_size, grad_scales, loss_sums, logits_grad, grad_type);
+    if (rc != SNB_OK) return rc;
+    rc = snb_gemm(stream, head);
     if (rc != SNB_OK) return rc;   // (snb_gemm has set the message)
     const int gemm_path = t_last_path;
-    cudaStream_t s = static_cast<cudaStream_t>(stream);
-    cudaError_t e = cudaMemsetAsync(loss_sums, 0, codebooks * sizeof(float), s);
-    if (e != cudaSuccess) return fail(SNB_ERR_CUDA, cuda_message("cudaMemsetAsync(loss_sums)", e));
-    std::string err;
-    rc = cross_entropy_launch(s, head->output, head->output_type, p.rows, p.cols, targets, codebooks, codebooks, 0,
-                              codebook_size, 0, grad_scales, 0.0f, nullptr, loss_sums, logits_grad, grad_type, &err);
-    if (rc != SNB_OK) return fail(rc, err);
+    rc = codebook_losses(static_cast<cudaStream_t>(stream), head->output, head->output_type, p.rows, codebooks,
+                         codebook_size, targets, grad_scales, loss_sums, logits_grad, grad_type);
+    if (rc != SNB_OK) return rc;
     t_last_path = gemm_path;
+    return SNB_OK;
+}
+
+int snb_codebook_cross_entropy(void* stream, const void* logits, int32_t logits_type, uint64_t rows,
+                               uint64_t codebooks, uint64_t codebook_size, const uint32_t* targets,
+                               uint64_t targets_len, const float* grad_scales, float* loss_sums, void* logits_grad,
+                               int32_t grad_type) {
+    t_last_path = SNB_PATH_NONE;
+    if (logits_type != SNB_TYPE_F32 && logits_type != SNB_TYPE_BF16)
+        return fail(SNB_ERR_INVALID_ARGUMENT, "codebook_cross_entropy: unknown logits type");
+    if (rows > 0 && logits == nullptr) return fail(SNB_ERR_INVALID_ARGUMENT, "codebook_cross_entropy: null pointer");
+    int rc = check_codebook_args("codebook_cross_entropy", rows, codebooks * codebook_size, logits, logits_type,
+                                 targets, targets_len, codebooks, codebook_size, grad_scales, loss_sums, logits_grad,
+                                 grad_type);
+    if (rc != SNB_OK) return rc;
+    if (rows == 0) {
+        if (loss_sums == nullptr) return SNB_OK;
+        const cudaError_t e = cudaMemsetAsync(loss_sums, 0, codebooks * sizeof(float), static_cast<cudaStream_t>(stream));
+        return e == cudaSuccess ? SNB_OK : fail(SNB_ERR_CUDA, cuda_message("cudaMemsetAsync(loss_sums)", e));
+    }
+    rc = codebook_losses(static_cast<cudaStream_t>(stream), logits, logits_type, rows, codebooks, codebook_size,
+                         targets, grad_scales, loss_sums, logits_grad, grad_type);
+    if (rc != SNB_OK) return rc;
+    t_last_path = SNB_PATH_SIMT;
     return SNB_OK;
 }
 

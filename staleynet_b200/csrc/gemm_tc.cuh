@@ -25,8 +25,10 @@
 // without any transposition pass. Every operand uses a 128-byte swizzle with 16-byte atoms except MN-major tf32
 // operands, which the tensor core reads only with 32-byte atoms (TMA's SWIZZLE_128B_ATOM_32B).
 //
-// Split-K: a work unit may cover only part of K; partial sums then always reach C through TMA reduce-add, which
-// adds element-wise in L2 (C must be pre-zeroed by the host for an overwrite).
+// Split-K: a work unit may cover only part of K; partial sums then reach C through TMA reduce-add, which adds
+// element-wise in L2 in arrival order (C must be pre-zeroed by the host for an overwrite), or, in the deterministic
+// mode (split_slabs), each split stores its partial into its own workspace slab and the host sums the slabs into C
+// in split order afterwards.
 #pragma once
 
 #include <cuda.h>
@@ -68,6 +70,16 @@ struct TcParams {
     int32_t causal;           // SNB_CAUSAL_* work-skipping hint of a batched attention product
     int64_t causal_offset;    // query q sees keys 0..=q+causal_offset
     const float* row_scale;   // [M] output-row multipliers (one matrix), or nullptr
+    int32_t split_slabs;      // 1: split s of the K range stores its partial tile into slab s of the output map (a
+                              // [splits, M, N] workspace, count 1), summed later in split order; 0: C itself
+    // Head-major operands (count 1). A packed activation [batch * time, heads * head_dim] whose heads are stored
+    // head-major, [batch, heads, capacity, head_dim] with time step s at row time_offset + s (the reference's
+    // HeadLayout, crates/staleynet-cuda/src/kernels/attention.rs:19-41), is read or written through 4-D / 5-D tensor
+    // maps instead of a packed copy: a_heads = A is such a tensor (tm_a 4-D: head_dim, capacity, heads, batch;
+    // K-major = tokens are A's rows, MN-major = tokens are the K index); c_heads = C is written to P such tensors
+    // side by side (tm_c 5-D: head_dim, capacity, heads, batch, P), columns (p * heads + h) * head_dim + d.
+    int32_t a_heads, a_hd, a_time, a_toff;
+    int32_t c_heads, c_hd, c_nheads, c_time, c_toff;
 };
 
 // Epilogue staging modes (see epilogue_tile); the host picks one per launch.
@@ -366,6 +378,64 @@ __device__ __forceinline__ void epilogue_half(const TcParams& p, uint32_t taddr,
     }
 }
 
+// Stores (or reduce-adds) one staged output box at column col0, row row0 of matrix/slab cz: through the 3-D map of
+// C, or, with c_heads, through the 5-D map of the head-major output (the box's 32 rows lie in one sequence and its
+// columns in one head: the host checks time % 32 == 0 and head_dim % box columns == 0).
+__device__ __forceinline__ void store_c_box(const TcParams& p, const CUtensorMap* tm_c, uint32_t box, int32_t col0,
+                                            int32_t row0, int32_t cz) {
+    if (p.c_heads) {
+        const int32_t head = col0 / p.c_hd;
+        tma_store_5d(tm_c, box, col0 - head * p.c_hd, p.c_toff + row0 % p.c_time, head % p.c_nheads,
+                     row0 / p.c_time, head / p.c_nheads);
+    } else if (p.reduce) {
+        tma_reduce_add_3d(tm_c, box, col0, row0, cz);
+    } else {
+        tma_store_3d(tm_c, box, col0, row0, cz);
+    }
+}
+
+// Loads A's K slice k0 for the 128 output rows from m0 into the ring slot at `sa` (completion on `bar`): one box of
+// 128 rows x BK for a K-major A, 128 / MN_BOX boxes of MN_BOX x BK for an MN-major A; with a_heads the boxes come
+// from the head-major 4-D map (a K-major box stays inside one head and one sequence: head_dim % BK == 0 and
+// time % 128 == 0; an MN-major box likewise with head_dim % MN_BOX == 0 and time % BK == 0, checked by the host).
+// PAIR: the load completes on the CTA pair's leader barrier.
+template <int BK, int MN_BOX, bool PAIR>
+__device__ __forceinline__ void load_a_slice(const TcParams& p, const CUtensorMap* tm_a, uint32_t sa, uint32_t bar,
+                                             int32_t m0, int32_t k0, int32_t ba) {
+    if (!p.a_heads) {
+        if (!p.a_mn_major) {
+            if constexpr (PAIR) tma_load_3d_pair(sa, tm_a, bar, k0, m0, ba);
+            else tma_load_3d(sa, tm_a, bar, k0, m0, ba);
+        } else {
+#pragma unroll
+            for (int j = 0; j < 128 / MN_BOX; ++j) {
+                if constexpr (PAIR) tma_load_3d_pair(sa + j * (BK * 128), tm_a, bar, m0 + j * MN_BOX, k0, ba);
+                else tma_load_3d(sa + j * (BK * 128), tm_a, bar, m0 + j * MN_BOX, k0, ba);
+            }
+        }
+        return;
+    }
+    if (!p.a_mn_major) {
+        // rows = tokens (batch-major, then time), K = head * head_dim + d
+        const int32_t h = k0 / p.a_hd;
+        const int32_t b = m0 / p.a_time;
+        const int32_t s = p.a_toff + (m0 - b * p.a_time);
+        if constexpr (PAIR) tma_load_4d_pair(sa, tm_a, bar, k0 - h * p.a_hd, s, h, b);
+        else tma_load_4d(sa, tm_a, bar, k0 - h * p.a_hd, s, h, b);
+    } else {
+        // rows = head * head_dim + d, K = tokens
+        const int32_t b = k0 / p.a_time;
+        const int32_t s = p.a_toff + (k0 - b * p.a_time);
+#pragma unroll
+        for (int j = 0; j < 128 / MN_BOX; ++j) {
+            const int32_t m = m0 + j * MN_BOX;
+            const int32_t h = m / p.a_hd;
+            if constexpr (PAIR) tma_load_4d_pair(sa + j * (BK * 128), tm_a, bar, m - h * p.a_hd, s, h, b);
+            else tma_load_4d(sa + j * (BK * 128), tm_a, bar, m - h * p.a_hd, s, h, b);
+        }
+    }
+}
+
 // Requests, on one lane, the auxiliary input of every column chunk an epilogue warp will stage for tile `u` (the
 // chunks epilogue_tile visits, box j for the j-th): one TMA load of a 32-row box per chunk into staging box j,
 // completing on aux_bar[j]. The boxes must no longer be read by earlier TMA stores.
@@ -399,6 +469,7 @@ __device__ __forceinline__ void epilogue_tile(const TcParams& p, const CUtensorM
     const int32_t row = row0 + lane;
     const bool first_split = u.split == 0;
     const int64_t out_base = static_cast<int64_t>(u.batch) * p.out_batch_stride + static_cast<int64_t>(row) * p.N;
+    const int32_t cz = p.split_slabs ? u.split : u.batch;  // third coordinate of the output map
     int j = 0;
     for (int c = group * CHUNK; c < BN && row0 < p.M && u.n0 + c < p.N; c += 2 * CHUNK, ++j) {
         const int32_t col0 = u.n0 + c;
@@ -419,7 +490,7 @@ __device__ __forceinline__ void epilogue_tile(const TcParams& p, const CUtensorM
             fence_proxy_async_shared();
             __syncwarp();
             if (lane == 0) {
-                tma_store_3d(tm_c, smem_addr(box), col0, row0, u.batch);
+                store_c_box(p, tm_c, smem_addr(box), col0, row0, u.batch);
                 bulk_commit_group();
             }
         } else if constexpr (EPI == TC_EPI_TWO_BOX) {
@@ -441,8 +512,7 @@ __device__ __forceinline__ void epilogue_tile(const TcParams& p, const CUtensorM
             __syncwarp();
             if (lane == 0) {
                 if (pre_box != nullptr) tma_store_3d(tm_pre, smem_addr(pre_box), col0, row0, u.batch);
-                if (p.reduce) tma_reduce_add_3d(tm_c, smem_addr(box), col0, row0, u.batch);
-                else tma_store_3d(tm_c, smem_addr(box), col0, row0, u.batch);
+                store_c_box(p, tm_c, smem_addr(box), col0, row0, cz);
                 bulk_commit_group();
             }
             if (!p.has_pre) ebox ^= 1;
@@ -462,8 +532,7 @@ __device__ __forceinline__ void epilogue_tile(const TcParams& p, const CUtensorM
                 __syncwarp();
                 if (lane == 0) {
                     if (pass == 0) tma_store_3d(tm_pre, smem_addr(box), col0, row0, u.batch);
-                    else if (p.reduce) tma_reduce_add_3d(tm_c, smem_addr(box), col0, row0, u.batch);
-                    else tma_store_3d(tm_c, smem_addr(box), col0, row0, u.batch);
+                    else store_c_box(p, tm_c, smem_addr(box), col0, row0, cz);
                     bulk_commit_group();
                 }
             }
@@ -553,13 +622,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
                     const uint32_t sa = smem_addr(ring + stage * Cfg::STAGE);
                     const uint32_t sb = sa + Cfg::STAGE_A;
                     const int32_t k0 = kb * BK;
-                    if (!p.a_mn_major) {
-                        tma_load_3d(sa, &tm_a, fb, k0, u.m0, ba);
-                    } else {
-#pragma unroll
-                        for (int j = 0; j < TC_BM / MN_BOX; ++j)
-                            tma_load_3d(sa + j * (BK * 128), &tm_a, fb, u.m0 + j * MN_BOX, k0, ba);
-                    }
+                    load_a_slice<BK, MN_BOX, false>(p, &tm_a, sa, fb, u.m0, k0, ba);
                     if (!p.b_mn_major) {
                         tma_load_3d(sb, &tm_b, fb, k0, u.n0, bb);
                     } else {

@@ -123,13 +123,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(TC_THREADS, 1)
                     const uint32_t sa = smem_addr(ring + stage * Cfg::STAGE);
                     const uint32_t sb = sa + Cfg::STAGE_A;
                     const int32_t k0 = kb * BK;
-                    if (!p.a_mn_major) {
-                        tma_load_3d_pair(sa, &tm_a, fb, k0, m0, ba);
-                    } else {
-#pragma unroll
-                        for (int j = 0; j < 128 / MN_BOX; ++j)
-                            tma_load_3d_pair(sa + j * (BK * 128), &tm_a, fb, m0 + j * MN_BOX, k0, ba);
-                    }
+                    load_a_slice<BK, MN_BOX, true>(p, &tm_a, sa, fb, m0, k0, ba);
                     if (!p.b_mn_major) {
                         tma_load_3d_pair(sb, &tm_b, fb, k0, n0, bb);
                     } else {

@@ -27,6 +27,9 @@ struct GemmRequest {
     int causal;
     int64_t causal_offset;
     const float* row_scale;   // [rows] output-row multipliers (count 1), or nullptr
+    bool deterministic;       // split-K partials summed in a fixed order (SNB_GEMM_DETERMINISTIC)
+    const snb_head_layout* a_heads;  // left operand read from its head-major form, or nullptr (snb_gemm_args)
+    const snb_head_layout* c_heads;  // output written head-major, or nullptr
 };
 
 struct DeviceInfo {
@@ -89,6 +92,11 @@ int fused_attention_backward(cudaStream_t stream, const void* q, const void* k, 
                              int out_type, const void* d_out, const float* lse, uint64_t count, uint64_t queries,
                              uint64_t keys, float scale, uint64_t query_offset, float* dq, float* dk, float* dv,
                              bool static_scratch_only, std::string* err);
+
+// The attention head permutes (heads.cu): split = packed -> head-major, else head-major -> packed; element types
+// SNB_TYPE_*; the layout is checked by the caller.
+int permute_heads_launch(cudaStream_t stream, bool split, const void* src, int src_type, void* dst, int dst_type,
+                         const snb_head_layout& layout, std::string* err);
 
 // Launches a one-thread kernel whose mbarrier wait nothing completes; it gives up after limit_ns.
 int bounded_wait_probe(cudaStream_t stream, uint64_t limit_ns, std::string* err);

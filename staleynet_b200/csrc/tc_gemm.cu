@@ -94,6 +94,35 @@ bool encode_3d(CUtensorMap* map, CUtensorMapDataType dt, int esize, const void* 
     return true;
 }
 
+// A tiled map of rank 4 or 5 (head-major operands): dims[0] contiguous, strides in elements for dims 1.., box
+// extents per dim.
+bool encode_nd(CUtensorMap* map, CUtensorMapDataType dt, int esize, const void* base, int rank, const uint64_t* dims,
+               const uint64_t* strides_elems, const uint32_t* box, std::string* err,
+               CUtensorMapSwizzle swizzle = CU_TENSOR_MAP_SWIZZLE_128B) {
+    EncodeTiledFn fn = encode_fn();
+    if (!fn) {
+        *err = "cuTensorMapEncodeTiled is not available from the CUDA driver";
+        return false;
+    }
+    cuuint64_t d[5];
+    cuuint64_t st[4];
+    cuuint32_t b[5];
+    cuuint32_t estr[5] = {1, 1, 1, 1, 1};
+    for (int i = 0; i < rank; ++i) {
+        d[i] = dims[i];
+        b[i] = box[i];
+        if (i > 0) st[i - 1] = strides_elems[i - 1] * esize;
+    }
+    CUresult r = fn(map, dt, rank, const_cast<void*>(base), d, st, b, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, swizzle,
+                    CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) {
+        *err = "cuTensorMapEncodeTiled (rank " + std::to_string(rank) + ") failed with CUresult " +
+               std::to_string(static_cast<int>(r));
+        return false;
+    }
+    return true;
+}
+
 template <typename E, int BN, bool OUT_BF16, int EPI>
 int launch(cudaStream_t stream, const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& tc,
            const CUtensorMap& tp, const CUtensorMap& tr, const CUtensorMap& tg, const CUtensorMap& tx,
@@ -169,6 +198,25 @@ int launch_pair(cudaStream_t stream, const CUtensorMap* m, const TcParams& p, in
     return SNB_OK;
 }
 
+// The deterministic split-K reduction: C = (accumulate ? C : 0) + slab_0 + slab_1 + ... in that order, for C
+// [n] f32 and `splits` slabs of n floats each (16-byte aligned, n a multiple of 4). Every element is summed by one
+// thread in a fixed order, so the result does not depend on scheduling.
+__global__ void split_slab_sum_kernel(const float4* __restrict__ slabs, int64_t slab4, int32_t splits, float4* c,
+                                      int32_t accumulate, int64_t n4) {
+    for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < n4;
+         i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+        float4 acc = accumulate ? c[i] : make_float4(0.f, 0.f, 0.f, 0.f);
+        for (int32_t s = 0; s < splits; ++s) {
+            const float4 v = __ldcs(slabs + s * slab4 + i);
+            acc.x += v.x;
+            acc.y += v.y;
+            acc.z += v.z;
+            acc.w += v.w;
+        }
+        c[i] = acc;
+    }
+}
+
 // K splits for a problem of `tiles` output tiles and `kb` K slices on `workers` SMs (or SM pairs): minimises the
 // critical path ceil(tiles*s/workers) * ceil(kb/s) (waves times slices per unit, in slice times of one worker),
 // keeping at least 4 K slices per split, plus what a split costs in output traffic at HBM speed in the same units:
@@ -220,6 +268,29 @@ int tc_gemm_try(cudaStream_t stream, const GemmRequest& r, bool* launched, int* 
     const OperandLayout lb = classify(p.cols, p.inner, p.right.col_stride, p.right.row_stride, p.right.batch_stride,
                                       r.count, esize, r.B);
     if (!la.ok || !lb.ok) return SNB_OK;
+    // Head-major operands (checked against the product by snb_gemm): the TMA boxes must not straddle a head or a
+    // sequence. A K-major A box is BK features x 128 tokens, an MN-major one MN_BOX features x BK tokens; an output
+    // box is 64 (bf16) or 32 (f32) columns x 32 rows.
+    const snb_head_layout* ah = r.a_heads;
+    const snb_head_layout* ch = r.c_heads;
+    if (ah != nullptr) {
+        const uint64_t need_hd = 128 / esize;  // BK or MN_BOX elements (128 bytes)
+        const uint64_t need_time = la.mn_major ? 128 / esize : TC_BM;
+        if (r.count != 1 || ah->head_dim % need_hd != 0 || ah->time % need_time != 0) {
+            *err = "head-major left operand: needs count 1, head_dim a multiple of " + std::to_string(need_hd) +
+                   " and time a multiple of " + std::to_string(need_time) + " for this storage";
+            return SNB_OK;
+        }
+    }
+    if (ch != nullptr) {
+        const uint64_t chunk_cols = r.c_type == SNB_TYPE_BF16 ? 64 : 32;
+        if (r.count != 1 || p.accumulate != 0 || r.residual != nullptr || r.gelu_input != nullptr ||
+            r.pre != nullptr || r.causal != SNB_CAUSAL_NONE || ch->head_dim % chunk_cols != 0 || ch->time % 32 != 0) {
+            *err = "head-major output: needs count 1, an overwrite without residual, GELU input or pre-activation, "
+                   "head_dim a multiple of " + std::to_string(chunk_cols) + " and time a multiple of 32";
+            return SNB_OK;
+        }
+    }
 
     // Output (and every tensor laid out like it): row-major [rows, cols] with rows `cols` apart.
     const int csize = out_bf16 ? 2 : 4;
@@ -259,18 +330,23 @@ int tc_gemm_try(cudaStream_t stream, const GemmRequest& r, bool* launched, int* 
     const int64_t k_blocks = (p.inner + bk - 1) / bk;
     const int64_t tiles = static_cast<int64_t>(r.count) * m_tiles * n_tiles;
     if (tiles > (1ll << 30)) return SNB_OK;
-    const bool plain_epilogue =
-        !out_bf16 && r.activation == SNB_ACTIVATION_NONE && r.pre == nullptr && r.causal == SNB_CAUSAL_NONE;
+    const bool plain_epilogue = !out_bf16 && r.activation == SNB_ACTIVATION_NONE && r.pre == nullptr &&
+                                r.causal == SNB_CAUSAL_NONE && ch == nullptr;
     // Tensor rate of one worker (one SM, or an SM pair) and the FLOPs of one K slice of one tile.
     const double sm_flops = (bf16_in ? 8192.0 : 4096.0) * 1.8e9;
     const double slice_flops = 2.0 * bm * bn * bk;
     const double out_bytes = static_cast<double>(r.count) * static_cast<double>(p.rows) * static_cast<double>(p.cols) *
                              static_cast<double>(csize);
-    const int splits = plain_epilogue ? choose_splits(tiles, k_blocks, workers, slice_flops,
-                                                      pair ? 2.0 * sm_flops : sm_flops, out_bytes, p.accumulate == 0)
-                                      : 1;
+    // The deterministic mode gives each split its own workspace slab (count 1 only): a split then costs its output
+    // bytes twice (slab store, then the ordered sum's read), and C is read and written once more.
+    const bool slab_mode = r.deterministic && r.count == 1;
+    const int splits = plain_epilogue && (!r.deterministic || slab_mode)
+                           ? choose_splits(tiles, k_blocks, workers, slice_flops, pair ? 2.0 * sm_flops : sm_flops,
+                                           slab_mode ? 2.0 * out_bytes : out_bytes, slab_mode || p.accumulate == 0)
+                           : 1;
     const int64_t kb_per_split = (k_blocks + splits - 1) / splits;
     const int64_t splits_used = (k_blocks + kb_per_split - 1) / kb_per_split;  // every split has >= 1 slice
+    const bool slabs = slab_mode && splits_used > 1;
 
     CUtensorMap maps[7];
     CUtensorMap &ta = maps[0], &tb = maps[1], &tc = maps[2], &tp = maps[3], &tr = maps[4], &tg = maps[5],
@@ -281,7 +357,17 @@ int tc_gemm_try(cudaStream_t stream, const GemmRequest& r, bool* launched, int* 
     // operands); everything else 16-byte atoms.
     const CUtensorMapSwizzle mn_swizzle = bf16_in ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B;
     // A: (mn = rows, k = inner)
-    if (la.mn_major) {
+    if (ah != nullptr) {
+        // [batch, heads, capacity, head_dim] -> dims (head_dim, capacity, heads, batch)
+        const uint64_t dims[4] = {ah->head_dim, ah->time_capacity, ah->heads, ah->batch};
+        const uint64_t strides[3] = {ah->head_dim, ah->time_capacity * ah->head_dim,
+                                     ah->heads * ah->time_capacity * ah->head_dim};
+        const uint32_t box_k[4] = {static_cast<uint32_t>(bk), TC_BM, 1, 1};
+        const uint32_t box_mn[4] = {mn_box, static_cast<uint32_t>(bk), 1, 1};
+        if (!encode_nd(&ta, in_dt, esize, r.A, 4, dims, strides, la.mn_major ? box_mn : box_k, err,
+                       la.mn_major ? mn_swizzle : CU_TENSOR_MAP_SWIZZLE_128B))
+            return SNB_OK;
+    } else if (la.mn_major) {
         if (!encode_3d(&ta, in_dt, esize, r.A, p.rows, p.inner, la.batched ? r.count : 1, la.ld,
                        la.batched ? p.left.batch_stride : la.ld * p.inner, mn_box, bk, err, mn_swizzle))
             return SNB_OK;
@@ -304,9 +390,43 @@ int tc_gemm_try(cudaStream_t stream, const GemmRequest& r, bool* launched, int* 
     const CUtensorMapDataType out_dt = out_bf16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT32;
     const uint32_t chunk = out_bf16 ? 64 : 32;
     const uint64_t c_bstride = c_batched ? p.output_batch_stride : p.rows * p.cols;
-    if (!encode_3d(&tc, out_dt, csize, r.C, p.cols, p.rows, c_batched ? r.count : 1, p.cols, c_bstride, chunk, 32,
-                   err))
+    // Deterministic split-K: the splits' partial tiles go to slabs [splits, rows, cols] of a stream-ordered
+    // workspace, freed (stream-ordered) when this call returns, after the kernels that use it are queued.
+    float* slab_base = nullptr;
+    struct SlabRelease {
+        float*& ptr;
+        cudaStream_t stream;
+        ~SlabRelease() {
+            if (ptr != nullptr) cudaFreeAsync(ptr, stream);
+        }
+    } slab_release{slab_base, stream};
+    if (slabs) {
+        uint64_t slab_bytes = 0;
+        if (__builtin_mul_overflow(static_cast<uint64_t>(splits_used), p.rows * p.cols * sizeof(float), &slab_bytes))
+            return SNB_OK;
+        cudaError_t e = cudaMallocAsync(reinterpret_cast<void**>(&slab_base), slab_bytes, stream);
+        if (e != cudaSuccess) {
+            slab_base = nullptr;
+            *err = cuda_message("cudaMallocAsync(split-K slabs)", e);
+            return SNB_ERR_CUDA;
+        }
+        if (!encode_3d(&tc, out_dt, csize, slab_base, p.cols, p.rows, static_cast<uint64_t>(splits_used), p.cols,
+                       p.rows * p.cols, chunk, 32, err))
+            return SNB_OK;
+    } else if (ch != nullptr) {
+        // P head-major tensors [batch, heads, capacity, head_dim] side by side -> dims (head_dim, capacity, heads,
+        // batch, P)
+        const uint64_t per = ch->batch * ch->heads * ch->time_capacity * ch->head_dim;
+        const uint64_t dims[5] = {ch->head_dim, ch->time_capacity, ch->heads, ch->batch,
+                                  p.cols / (ch->heads * ch->head_dim)};
+        const uint64_t strides[4] = {ch->head_dim, ch->time_capacity * ch->head_dim,
+                                     ch->heads * ch->time_capacity * ch->head_dim, per};
+        const uint32_t box[5] = {chunk, 32, 1, 1, 1};
+        if (!encode_nd(&tc, out_dt, csize, r.C, 5, dims, strides, box, err)) return SNB_OK;
+    } else if (!encode_3d(&tc, out_dt, csize, r.C, p.cols, p.rows, c_batched ? r.count : 1, p.cols, c_bstride, chunk,
+                          32, err)) {
         return SNB_OK;
+    }
     if (r.pre) {
         if (!encode_3d(&tp, out_dt, csize, r.pre, p.cols, p.rows, c_batched ? r.count : 1, p.cols, c_bstride, chunk,
                        32, err))
@@ -345,9 +465,10 @@ int tc_gemm_try(cudaStream_t stream, const GemmRequest& r, bool* launched, int* 
                               p.rows, c_batched ? r.count : 1, p.cols, c_bstride, chunk, 32, err))
         return SNB_OK;
 
-    // An overwrite computed in several K splits reaches C by reduce-add, so C starts at zero.
-    const bool reduce = p.accumulate != 0 || splits_used > 1;
-    if (p.accumulate == 0 && splits_used > 1) {
+    // An overwrite computed in several K splits reaches C by reduce-add, so C starts at zero (slab stores need no
+    // zeroing: the ordered sum writes C).
+    const bool reduce = !slabs && (p.accumulate != 0 || splits_used > 1);
+    if (!slabs && p.accumulate == 0 && splits_used > 1) {
         cudaError_t e;
         if (!c_batched || p.output_batch_stride == p.rows * p.cols) {
             e = cudaMemsetAsync(r.C, 0, r.count * p.rows * p.cols * csize, stream);
@@ -394,6 +515,35 @@ int tc_gemm_try(cudaStream_t stream, const GemmRequest& r, bool* launched, int* 
     kp.out_batch_stride = static_cast<int64_t>(c_batched ? p.output_batch_stride : 0);
     kp.causal = r.causal;
     kp.causal_offset = r.causal_offset;
+    kp.split_slabs = slabs ? 1 : 0;
+    if (ah != nullptr) {
+        kp.a_heads = 1;
+        kp.a_hd = static_cast<int32_t>(ah->head_dim);
+        kp.a_time = static_cast<int32_t>(ah->time);
+        kp.a_toff = static_cast<int32_t>(ah->time_offset);
+    }
+    if (ch != nullptr) {
+        kp.c_heads = 1;
+        kp.c_hd = static_cast<int32_t>(ch->head_dim);
+        kp.c_nheads = static_cast<int32_t>(ch->heads);
+        kp.c_time = static_cast<int32_t>(ch->time);
+        kp.c_toff = static_cast<int32_t>(ch->time_offset);
+    }
+    // After the GEMM, the slabs are summed into C in split order.
+    auto sum_slabs = [&]() -> int {
+        if (!slabs) return SNB_OK;
+        const int64_t n4 = static_cast<int64_t>(p.rows * p.cols / 4);
+        const int64_t blocks = std::min<int64_t>((n4 + 255) / 256, static_cast<int64_t>(dev.sm_count) * 8);
+        split_slab_sum_kernel<<<static_cast<unsigned>(blocks), 256, 0, stream>>>(
+            reinterpret_cast<const float4*>(slab_base), n4, static_cast<int32_t>(splits_used),
+            reinterpret_cast<float4*>(r.C), p.accumulate != 0 ? 1 : 0, n4);
+        const cudaError_t e = cudaGetLastError();
+        if (e != cudaSuccess) {
+            *err = cuda_message("split_slab_sum_kernel launch", e);
+            return SNB_ERR_CUDA;
+        }
+        return SNB_OK;
+    };
 
     // Staging mode of the epilogue (gemm_tc.cuh, epilogue_tile).
     const bool heavy = r.activation != SNB_ACTIVATION_NONE;
@@ -414,6 +564,7 @@ int tc_gemm_try(cudaStream_t stream, const GemmRequest& r, bool* launched, int* 
         } else {
             rc = launch_pair<float, false, TC_EPI_ONE_BOX>(stream, maps, kp, grid, err);
         }
+        if (rc == SNB_OK) rc = sum_slabs();
         if (rc == SNB_OK) {
             *launched = true;
             *path = SNB_PATH_TENSOR_CORE_PAIR;
@@ -427,6 +578,7 @@ int tc_gemm_try(cudaStream_t stream, const GemmRequest& r, bool* launched, int* 
     } else {
         rc = launch_bn<float, false>(bn, epi, stream, maps, kp, grid, err);
     }
+    if (rc == SNB_OK) rc = sum_slabs();
     if (rc == SNB_OK) *launched = true;
     return rc;
 }

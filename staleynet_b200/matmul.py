@@ -222,16 +222,22 @@ class Gpu:
 
     def gemm(self, spec: MatmulSpec, left, right, output, *, bias=None, activation: int = _ffi.ACTIVATION_NONE,
              pre_activation=None, gelu_input=None, residual=None, causal: int = _ffi.CAUSAL_NONE,
-             causal_offset: int = 0, row_scale=None) -> None:
-        """`Gpu.matmul` with the caller's elementwise follow-up fused into the epilogue (snb_gemm)."""
+             causal_offset: int = 0, row_scale=None, deterministic: bool = False, left_heads=None,
+             output_heads=None) -> None:
+        """`Gpu.matmul` with the caller's elementwise follow-up fused into the epilogue (snb_gemm). deterministic:
+        split-K partial sums added in a fixed order (SNB_GEMM_DETERMINISTIC), bit-identical between runs.
+        left_heads / output_heads (HeadLayout): the left operand is read from, or the output written to, the
+        head-major form of the packed tensor the spec describes (the split/merge permutes fused into the product)."""
         args = self.gemm_args(spec, left, right, output, bias=bias, activation=activation,
                               pre_activation=pre_activation, gelu_input=gelu_input, residual=residual, causal=causal,
-                              causal_offset=causal_offset, row_scale=row_scale)
+                              causal_offset=causal_offset, row_scale=row_scale, deterministic=deterministic,
+                              left_heads=left_heads, output_heads=output_heads)
         check(self.lib.snb_gemm(self._stream_handle(), ctypes.byref(args)))
 
     def gemm_args(self, spec: MatmulSpec, left, right, output, *, bias=None, activation: int = _ffi.ACTIVATION_NONE,
                   pre_activation=None, gelu_input=None, residual=None, causal: int = _ffi.CAUSAL_NONE,
-                  causal_offset: int = 0, row_scale=None) -> _ffi.GemmArgs:
+                  causal_offset: int = 0, row_scale=None, deterministic: bool = False, left_heads=None,
+                  output_heads=None) -> _ffi.GemmArgs:
         """The snb_gemm_args of `gemm` (for entry points that take a GEMM as an argument)."""
         import torch
 
@@ -260,6 +266,11 @@ class Gpu:
         args.causal = causal
         args.causal_offset = causal_offset
         args.row_scale = _ptr(row_scale) if row_scale is not None else None
+        args.flags = _ffi.GEMM_DETERMINISTIC if deterministic else 0
+        # The layouts must outlive the call: keep them on the argument block.
+        args._heads = (left_heads, output_heads)
+        args.left_heads = ctypes.pointer(left_heads) if left_heads is not None else None
+        args.output_heads = ctypes.pointer(output_heads) if output_heads is not None else None
         return args
 
     def cross_entropy(self, logits, targets, head: "CrossEntropyHead", losses, logits_grad) -> None:
@@ -394,6 +405,46 @@ class Gpu:
         check(self.lib.snb_head_cross_entropy(self._stream_handle(), ctypes.byref(args), _ptr(t), t.numel(),
                                               codebooks, spec.cols // codebooks, _ptr(grad_scales), _ptr(loss_sums),
                                               _ptr(logits_grad), grad_type))
+
+    def codebook_cross_entropy(self, logits, targets, codebooks: int, grad_scales, loss_sums, logits_grad) -> None:
+        """Every codebook's cross-entropy of logits [rows, codebooks * size] already computed
+        (snb_codebook_cross_entropy): loss_sums[c] = sum of codebook c's row losses, its gradient into logits_grad
+        (which may be `logits` itself). targets: [rows, codebooks] int32/uint32 bits."""
+        import torch
+
+        _require_cuda(logits, targets, grad_scales, loss_sums, logits_grad)
+        t = targets if targets.dtype == torch.int32 else targets.to(torch.int32)
+        rows = t.numel() // codebooks if logits.dim() == 1 else logits.shape[0]
+        size = logits.numel() // rows // codebooks
+        lt = _ffi.TYPE_BF16 if logits.dtype == torch.bfloat16 else _ffi.TYPE_F32
+        gt = _ffi.TYPE_BF16 if logits_grad.dtype == torch.bfloat16 else _ffi.TYPE_F32
+        check(self.lib.snb_codebook_cross_entropy(self._stream_handle(), _ptr(logits), lt, rows, codebooks, size,
+                                                  _ptr(t), t.numel(), _ptr(grad_scales), _ptr(loss_sums),
+                                                  _ptr(logits_grad), gt))
+
+    def split_heads(self, packed, head_major, layout: "_ffi.HeadLayout") -> None:
+        """`Gpu::split_heads` (crates/staleynet-cuda/src/ops/attention.rs:20-36): packed columns -> head-major; f32
+        through snb_split_heads, other dtypes through snb_permute_heads."""
+        self.permute_heads(_ffi.HEADS_SPLIT, packed, head_major, layout)
+
+    def merge_heads(self, head_major, packed, layout: "_ffi.HeadLayout") -> None:
+        """`Gpu::merge_heads` (ops/attention.rs:38-52): head-major -> packed columns, other columns untouched."""
+        self.permute_heads(_ffi.HEADS_MERGE, head_major, packed, layout)
+
+    def permute_heads(self, direction: int, src, dst, layout: "_ffi.HeadLayout") -> None:
+        import torch
+
+        _require_cuda(src, dst)
+        h = self._stream_handle()
+        if src.dtype == torch.float32 and dst.dtype == torch.float32:
+            fn = self.lib.snb_split_heads if direction == _ffi.HEADS_SPLIT else self.lib.snb_merge_heads
+            check(fn(h, _ptr(src), src.numel(), _ptr(dst), dst.numel(), ctypes.byref(layout)))
+            return
+        ty = {torch.float32: _ffi.TYPE_F32, torch.bfloat16: _ffi.TYPE_BF16}
+        if src.dtype not in ty or dst.dtype not in ty:
+            raise SnbError(_ffi.ERR_INVALID_ARGUMENT, "permute_heads: tensors must be float32 or bfloat16")
+        check(self.lib.snb_permute_heads(h, direction, _ptr(src), ty[src.dtype], src.numel(), _ptr(dst),
+                                         ty[dst.dtype], dst.numel(), ctypes.byref(layout)))
 
     def causal_softmax(self, scores, queries: int, scale: float, query_offset: int) -> None:
         """`Gpu::causal_softmax` (ops/attention.rs:57-81) on scores [rows, keys]."""

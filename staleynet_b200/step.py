@@ -10,7 +10,14 @@ Per block (crates/staleynet-model/src/layers/block.rs:160-216) the step runs, in
             expand   dW1 += Xᵀ·dPre ; dX = dPre·W1ᵀ
             output   dWo += Cᵀ·dY ;   dC = dY·Woᵀ
             qkv      dWqkv += Xᵀ·dQKV ; dX = dQKV·Wqkvᵀ
-and the output head (gpt.rs:72; training.rs:201-202, 247-248): logits = X·Wh + b, dWh += Xᵀ·dL, dX = dL·Whᵀ.
+and the output head (gpt.rs:72; training.rs:201-202, 247-248): logits = X·Wh + b, then every codebook's softmax
+cross-entropy with its gradient dL written over the logits (training.rs:209-235, one launch, loss sums on the device),
+then dWh += Xᵀ·dL, dX = dL·Whᵀ.
+
+A step may cover several micro-batches (the reference's gradient accumulation: every dW product accumulates, and the
+gradients are zeroed once per step), each a forward, loss and backward over its own input tokens and targets.
+Inputs come from one seeded stream of the reference's generator: micro-batch g of the global batch takes the g-th
+slice of it, so any rank can rebuild any micro-batch.
 
 Attention scores, softmax and norms are not GEMMs of the linear stack and are not part of this workload (the
 attention products are covered by the tests and by snb_causal_softmax); their activations are stood in for by
@@ -58,21 +65,38 @@ def step_flops(s: ModelShape) -> float:
     return 3.0 * (s.blocks * per_block + head)
 
 
-class TrainingStepGemms:
-    """Device buffers and pre-built C-ABI argument blocks for every GEMM of one step; `run()` issues them."""
+# Seeds of the reference's generator (Random::new, random.rs:27-70) for the step's tensors. Weights and the
+# attention stand-ins use WEIGHT_SEED on every rank (data-parallel replicas hold the same model); micro-batch g of the
+# global batch draws its input activations and targets from slice g of the INPUT_SEED / TARGET_SEED streams.
+WEIGHT_SEED = 1234
+INPUT_SEED = 7
+TARGET_SEED = 8
 
-    def __init__(self, shape: ModelShape, device, seed: int = 0):
+
+class TrainingStepGemms:
+    """Device buffers and pre-built C-ABI argument blocks for every GEMM of one micro-batch's forward and backward,
+    plus the loss between them; `run()` issues them for one micro-batch, `run_step()` for all of a step's.
+
+    micro_batches: micro-batches this process runs per step, global indices first_micro_batch, +1, ... .
+    grad_scale: the loss-gradient scale 1 / (valid targets x codebooks) of the whole step (all micro-batches of
+    all ranks; training.rs:214-221); by default that of this process's micro-batches alone.
+    deterministic: every product runs with SNB_GEMM_DETERMINISTIC (weight gradients bit-identical between runs)."""
+
+    def __init__(self, shape: ModelShape, device, seed: int = WEIGHT_SEED, micro_batches: int = 1,
+                 first_micro_batch: int = 0, grad_scale: float | None = None, deterministic: bool = False):
         import torch
 
         self.shape = shape
         self.device = device
+        self.deterministic = deterministic
         self.lib = _ffi.load()
         s = shape
         T, w, f, V = s.tokens, s.width, s.ffn, s.head_width
         bf16, f32 = torch.bfloat16, torch.float32
-        # Inputs and weights come from the reference's generator (Random::new(seed), random.rs:27-70), drawn on the
-        # device in the order they are created here.
-        rng = DeviceRandom(Gpu(device.index if device.index is not None else 0), seed)
+        self.gpu = Gpu(device.index if device.index is not None else 0)
+        # Weights and stand-ins come from the reference's generator (Random::new(seed), random.rs:27-70), drawn on
+        # the device in the order they are created here.
+        rng = DeviceRandom(self.gpu, seed)
 
         def normal(n, std, dtype=bf16):
             return rng.normal_(torch.empty(n, device=device, dtype=dtype), std)
@@ -97,7 +121,6 @@ class TrainingStepGemms:
         self.head_grad = self.grads.head
 
         # Activations kept per block, as a training step keeps them for the backward pass.
-        self.x_in = normal(T * w, 1.0)  # the step's input activations (uploaded per step in the end-to-end run)
         self.acts = []
         for _ in range(s.blocks):
             self.acts.append({
@@ -108,7 +131,7 @@ class TrainingStepGemms:
                 "hid": torch.empty(T * f, device=device, dtype=bf16),
                 "out": torch.empty(T * w, device=device, dtype=bf16),
             })
-        self.logits = torch.empty(T * V, device=device, dtype=bf16)
+        self.logits = torch.empty(T * V, device=device, dtype=bf16)   # overwritten in place by the loss gradient
         # Gradient buffers (reused across blocks, as the reference's shared gradient workspace).
         self.g_x = torch.empty(T * w, device=device, dtype=bf16)
         self.g_mid = torch.empty(T * w, device=device, dtype=bf16)
@@ -116,8 +139,32 @@ class TrainingStepGemms:
         self.g_ctx = torch.empty(T * w, device=device, dtype=bf16)
         self.g_qkv = normal(T * 3 * w, 1.0)  # attention's gradient w.r.t. the fused projection (stand-in)
         self.g_in = torch.empty(T * w, device=device, dtype=bf16)
+
+        # The step's micro-batches: input activations and targets, resident on the device.
+        self.micro_batches = micro_batches
+        self.first_micro_batch = first_micro_batch
+        self.inputs = torch.empty(micro_batches, T * w, device=device, dtype=bf16)
+        self.targets = torch.empty(micro_batches, T * s.codebooks, device=device, dtype=torch.int32)
+        for m in range(micro_batches):
+            self.load_micro_batch(first_micro_batch + m, self.inputs[m], self.targets[m])
+        self.x_in = self.inputs[0]
+        if grad_scale is None:
+            grad_scale = 1.0 / (T * micro_batches * s.codebooks)
+        self.grad_scale = grad_scale
+        self.grad_scales = torch.full((s.codebooks,), grad_scale, device=device, dtype=f32)
+        self.loss_sums = torch.zeros(micro_batches, s.codebooks, device=device, dtype=f32)
         self.flops = step_flops(s)
         self._build_plan()
+
+    def load_micro_batch(self, global_index: int, x, targets) -> None:
+        """Fills x ([tokens * width] bf16) and targets ([tokens * codebooks] int32) with micro-batch `global_index`
+        of the global batch: slice global_index of the input stream (N(0,1) activations) and of the target stream
+        (`below(codebook_size)`, as the reference's bench draws targets, bench.rs:152-154)."""
+        s = self.shape
+        n_x = s.tokens * s.width
+        n_t = s.tokens * s.codebooks
+        self.gpu.random_normal(x, INPUT_SEED, first_draw=2 * n_x * global_index, std=1.0)
+        self.gpu.random_below(targets, s.codebook_size, TARGET_SEED, first_draw=n_t * global_index)
 
     # ------------------------------------------------------------------------------------------------ plan
     def _args(self, spec: MatmulSpec, left, right, output, *, bias=None, activation=_ffi.ACTIVATION_NONE,
@@ -139,14 +186,17 @@ class TrainingStepGemms:
         a.pre_activation = pre.data_ptr() if pre is not None else None
         a.gelu_input = gelu_input.data_ptr() if gelu_input is not None else None
         a.residual = residual.data_ptr() if residual is not None else None
+        a.flags = _ffi.GEMM_DETERMINISTIC if self.deterministic else 0
         return a
 
     def use_input(self, x) -> None:
         """Points the step's first-block products at input activations `x` (same shape and type as x_in), so a
-        caller can upload the next step's input into a second buffer while this step runs."""
+        caller can upload the next micro-batch's input into another buffer while this one runs."""
         assert x.numel() == self.x_in.numel() and x.dtype == self.x_in.dtype
         for a in self._input_args:
             a.left = x.data_ptr()
+        for a in self._residual_args:
+            a.residual = x.data_ptr()
 
     def _build_plan(self) -> None:
         s = self.shape
@@ -173,8 +223,7 @@ class TrainingStepGemms:
         fwd.append(("head.fwd", 2.0 * T * w * V,
                     self._args(MatmulSpec.new(T, V, w), x, self.head_w, self.logits, bias=self.head_b)))
         self.final_x = x
-        # Backward: the head's upstream gradient is the logits tensor itself (a synthetic loss whose gradient
-        # has the logits' shape and magnitude).
+        # Backward: the loss gradient dL has overwritten the logits (snb_codebook_cross_entropy between the passes).
         bwd.append(("head.dW", 2.0 * T * w * V,
                     self._args(MatmulSpec.new(w, V, T).left_transposed().accumulate(), x, self.logits,
                                self.head_grad)))
@@ -211,6 +260,8 @@ class TrainingStepGemms:
                         self._args(MatmulSpec.new(T, w, 3 * w).right_transposed(), self.g_qkv, W["qkv"],
                                    self.g_in, residual=self.g_mid)))
             self.block_bwd_end.append((b, len(bwd)))
+        # Block 0's output product reads the input as its residual: repointed with the others.
+        self._residual_args = [fwd[1][2]]
         self.forward_plan = fwd
         self.backward_plan = bwd
         self.plan = fwd + bwd
@@ -218,16 +269,24 @@ class TrainingStepGemms:
 
     # ------------------------------------------------------------------------------------------------ run
     def launches_per_step(self) -> int:
+        """GEMM launches of one micro-batch (the loss kernel is not counted)."""
         return len(self.plan)
 
-    def run(self, stream_handle: int, on_block_done=None, events=None) -> None:
-        """Issues every GEMM of the step on `stream_handle`. `on_block_done(b)` is called after the backward GEMMs
-        of block b have been issued (the data-parallel step starts that block's all-reduce there). With `events`
-        (a list of (start, end) CUDA event pairs, one per GEMM) each launch is bracketed for kernel timing."""
+    def use_micro_batch(self, m: int, x=None) -> None:
+        """Points the products at local micro-batch m's input (or at `x`, a buffer holding it)."""
+        self.use_input(self.inputs[m] if x is None else x)
+
+    def run(self, stream_handle: int, on_block_done=None, events=None, micro_batch: int = 0, x=None) -> None:
+        """Issues the forward, loss and backward of local micro-batch `micro_batch` on `stream_handle`.
+        `on_block_done(b)` is called after the backward GEMMs of block b have been issued (the data-parallel step
+        starts that block's all-reduce there). With `events` (a list of (start, end) CUDA event pairs, one per GEMM)
+        each GEMM launch is bracketed for kernel timing."""
+        self.use_micro_batch(micro_batch, x)
         h = ctypes.c_void_p(stream_handle)
         gemm = self.lib.snb_gemm
         ends = dict((n, b) for b, n in self.block_bwd_end) if on_block_done else {}
         nfwd = len(self.forward_plan)
+        s = self.shape
         for i, (_, _, args) in enumerate(self.plan):
             if events is not None:
                 events[i][0].record()
@@ -236,8 +295,29 @@ class TrainingStepGemms:
                 check(code)
             if events is not None:
                 events[i][1].record()
+            if i == nfwd - 1:
+                # Every codebook's loss and its gradient, written over the bf16 logits (training.rs:209-235).
+                code = self.lib.snb_codebook_cross_entropy(
+                    h, self.logits.data_ptr(), _ffi.TYPE_BF16, s.tokens, s.codebooks, s.codebook_size,
+                    self.targets[micro_batch].data_ptr(), self.targets[micro_batch].numel(),
+                    self.grad_scales.data_ptr(), self.loss_sums[micro_batch].data_ptr(), self.logits.data_ptr(),
+                    _ffi.TYPE_BF16)
+                if code != _ffi.OK:
+                    check(code)
             if on_block_done is not None and (i + 1 - nfwd) in ends:
                 on_block_done(ends[i + 1 - nfwd])
+
+    def run_step(self, stream_handle: int, on_block_done=None, events=None, inputs=None) -> None:
+        """One optimizer step's worth of work: gradients zeroed, then every local micro-batch in turn, each
+        accumulating into the weight gradients; `on_block_done` (the all-reduce hook) fires during the last one's
+        backward only. `events`: one list of event pairs per micro-batch, or None. `inputs`: a callable m -> buffer
+        holding micro-batch m's input (the end-to-end run's upload buffers), or None for the resident inputs."""
+        self.zero_grads()
+        last = self.micro_batches - 1
+        for m in range(self.micro_batches):
+            self.run(stream_handle, on_block_done=on_block_done if m == last else None,
+                     events=events[m] if events is not None else None, micro_batch=m,
+                     x=inputs(m) if inputs is not None else None)
 
     def zero_grads(self) -> None:
         self.grads.zero_()

@@ -67,3 +67,25 @@ def test_a_collective_past_its_deadline_is_an_error_not_a_hang():
     (status, seconds, *detail), = run_ranks(dp_workers.collective_deadline_is_an_error, timeout=90)
     assert status == "collective failed", (status, detail)
     assert seconds < 30, seconds
+
+
+@pytest.mark.parametrize("world", [1, 2, 4, 8])
+def test_config5_micro_batches_tile_the_global_batch(world):
+    # 256 sequences of 2048 tokens split over `world` ranks, each rank running 32-sequence
+    # micro-batches; every micro-batch of the step belongs to exactly one rank, in order.
+    import bench
+
+    plans = [bench.micro_batch_plan(256, world, r) for r in range(world)]
+    assert all(total == 8 for _, _, total in plans)
+    seen = []
+    for first, count, _ in plans:
+        seen.extend(range(first, first + count))
+    assert seen == list(range(8))
+    assert bench.micro_batch_plan(0, world, world - 1) == (world - 1, 1, world)
+
+
+def test_config5_rejects_a_split_into_partial_micro_batches():
+    import bench
+
+    with pytest.raises(SystemExit):
+        bench.micro_batch_plan(256, 3, 0)

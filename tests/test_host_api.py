@@ -71,7 +71,7 @@ def test_library_loads_and_exports_every_declared_symbol():
     for name in declared:
         assert hasattr(lib, name), f"{name} declared in the header but not exported"
     assert sorted(_ffi.EXPORTED_SYMBOLS) == declared
-    assert lib.snb_abi_version() == 102
+    assert lib.snb_abi_version() == 105
 
 
 def call_matmul(rows, cols, inner, left_len, right_len, output_len, count=1, precision=_ffi.PRECISION_F32):
@@ -138,3 +138,28 @@ def test_attention_backward_rejects_sizes_whose_byte_counts_overflow():
                   fake, fake)
         assert code == _ffi.ERR_INVALID_ARGUMENT
         assert "overflow" in _ffi.last_error()
+
+
+def test_deterministic_switch_is_per_thread_and_returns_the_previous_setting():
+    import threading
+
+    lib = _ffi.load()
+    assert lib.snb_set_deterministic(1) == 0
+    seen = []
+    t = threading.Thread(target=lambda: seen.append(lib.snb_set_deterministic(0)))
+    t.start()
+    t.join()
+    assert seen == [0]   # another thread starts from the default
+    assert lib.snb_set_deterministic(0) == 1
+
+
+def test_gemm_rejects_unknown_flags():
+    lib = _ffi.load()
+    a = _ffi.GemmArgs()
+    a.product = MatmulSpec.new(4, 8, 8).product()
+    a.count = 1
+    a.left_type = a.right_type = a.output_type = a.aux_type = _ffi.TYPE_F32
+    a.precision = _ffi.PRECISION_F32
+    a.flags = 2
+    assert lib.snb_gemm(None, ctypes.byref(a)) == _ffi.ERR_INVALID_ARGUMENT
+    assert "flags" in _ffi.last_error()

@@ -221,3 +221,28 @@ def test_adamw_matches_the_reference_parity_formula():
     v = np.full(c["count"], c["initial_variance"], np.float32)
     o.adamw_step(p, g, m, v, c["learning_rate"], c["beta1"], c["beta2"], c["epsilon"], c["weight_decay"], c["step"])
     assert o.relative_error(expected, p) < 1e-5
+
+
+def test_head_permutes_follow_the_reference_formula():
+    # The layout of the reference's split_and_merge_heads_follow_the_layout_formula
+    # (crates/staleynet-cuda/tests/kernels_match_reference.rs:199-231): dense(2, 5, 3, 4, 3*12 + 2, 13).in_cache(9, 2),
+    # inputs random_values(n, 12); every moved element lands at its formula index and a merge restores exactly the
+    # head columns, zero elsewhere.
+    from staleynet_b200._ffi import HeadLayout
+
+    L = HeadLayout.dense(2, 5, 3, 4, 3 * 12 + 2, 13).in_cache(9, 2)
+    packed = o.lcg_values(L.batch * L.time * L.width, 12)
+    head_major = np.zeros(L.batch * L.heads * L.time_capacity * L.head_dim, np.float32)
+    o.split_heads(packed, head_major, L)
+    for b in range(L.batch):
+        for h in range(L.heads):
+            for t in range(L.time):
+                for d in range(L.head_dim):
+                    src = (b * L.time + t) * L.width + L.column_offset + h * L.head_dim + d
+                    dst = ((b * L.heads + h) * L.time_capacity + L.time_offset + t) * L.head_dim + d
+                    assert head_major[dst] == packed[src]
+    merged = np.zeros_like(packed)
+    o.merge_heads(head_major, merged, L)
+    cols = np.arange(packed.size) % L.width
+    inside = (cols >= L.column_offset) & (cols < L.column_offset + L.heads * L.head_dim)
+    assert np.array_equal(merged, np.where(inside, packed, 0.0).astype(np.float32))
