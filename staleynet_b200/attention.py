@@ -206,3 +206,119 @@ class FusedAttention:
     def launches(self) -> int:
         """Kernels of one forward + backward: the forward kernel, the row-statistics and backward kernels."""
         return 3
+
+
+@dataclass(frozen=True)
+class LayerShape:
+    """Geometry of one attention layer call: `batch` sequences of `time` steps, `heads` heads of `head_dim`."""
+
+    batch: int = 32
+    time: int = 2048
+    heads: int = 12
+    head_dim: int = 64
+
+    @property
+    def width(self) -> int:
+        return self.heads * self.head_dim
+
+    @property
+    def tokens(self) -> int:
+        return self.batch * self.time
+
+
+class CausalSelfAttentionLayer:
+    """`CausalSelfAttention::forward` / `backward` (crates/staleynet-model/src/layers/attention.rs:188-267) on the C
+    ABI, bf16 activations and weights W[in, out] (the reference's layout), f32 weight gradients.
+
+    With fused_permutes (the default) the reference's head permutes run inside the products around attention:
+      forward   qkv     = x Wqkv + b, written head-major (snb_gemm output_heads: the three split_heads,
+                          attention.rs:201-204)
+                o, lse  = causal attention of q, k, v (snb_causal_attention_forward: QK^T, causal_softmax, P V,
+                          attention.rs:206-213)
+                y       = o Wo + b, o read head-major (snb_gemm left_heads: merge_heads, attention.rs:214-216)
+      backward  dWo    += o^T dy, o read head-major                      (Linear::backward, linear.rs:55-58)
+                do      = dy Wo^T, written head-major (output_heads: split_heads of the context gradient,
+                          attention.rs:233-237)
+                dq, dk, dv = snb_causal_attention_backward                (attention.rs:239-260)
+                dqkv    = the three merge_heads, f32 -> bf16 (snb_permute_heads, attention.rs:262-264)
+                dWqkv  += x^T dqkv ;  dx = dqkv Wqkv^T                    (attention.rs:266, linear.rs:51-63)
+    Without it, the products write and read packed tensors and snb_permute_heads moves the heads in between, as the
+    reference does. Bias gradients (column sums of dy, not products) are not computed here."""
+
+    def __init__(self, shape: LayerShape, device, seed: int = 0, fused_permutes: bool = True,
+                 deterministic: bool = False):
+        import torch
+
+        s = shape
+        self.shape = s
+        self.fused = fused_permutes
+        self.deterministic = deterministic
+        self.gpu = Gpu(device.index if device.index is not None else 0)
+        T, w, n, S, d = s.tokens, s.width, s.batch * s.heads, s.time, s.head_dim
+        bf16, f32 = torch.bfloat16, torch.float32
+        rng = DeviceRandom(self.gpu, seed)
+        std = 1.0 / (w ** 0.5)
+        self.w_qkv = rng.normal_(torch.empty(w, 3 * w, device=device, dtype=bf16), std)
+        self.b_qkv = rng.normal_(torch.empty(3 * w, device=device, dtype=f32), 0.1)
+        self.w_o = rng.normal_(torch.empty(w, w, device=device, dtype=bf16), std)
+        self.b_o = rng.normal_(torch.empty(w, device=device, dtype=f32), 0.1)
+        self.g_wqkv = torch.zeros(w, 3 * w, device=device, dtype=f32)
+        self.g_wo = torch.zeros(w, w, device=device, dtype=f32)
+        self.qkv_heads = torch.empty(3, n, S, d, device=device, dtype=bf16)   # q, k, v head-major
+        self.o_heads = torch.empty(n, S, d, device=device, dtype=bf16)        # attention output (context)
+        self.lse = torch.empty(n, S, device=device, dtype=f32)
+        self.do_heads = torch.empty(n, S, d, device=device, dtype=bf16)
+        self.dq, self.dk, self.dv = (torch.empty(n, S, d, device=device, dtype=f32) for _ in range(3))
+        self.d_qkv = torch.empty(T, 3 * w, device=device, dtype=bf16)
+        if not fused_permutes:
+            self.qkv = torch.empty(T, 3 * w, device=device, dtype=bf16)
+            self.o = torch.empty(T, w, device=device, dtype=bf16)
+            self.d_o = torch.empty(T, w, device=device, dtype=bf16)
+        self.scale = 1.0 / (d ** 0.5)
+
+    def layout(self, width: int, column_offset: int) -> _ffi.HeadLayout:
+        """`CausalSelfAttention::layout` (attention.rs:170-173): a projection's heads in a packed row of `width`."""
+        s = self.shape
+        return _ffi.HeadLayout.dense(s.batch, s.time, s.heads, s.head_dim, width, column_offset)
+
+    def forward(self, x, y) -> None:
+        """y [tokens, width] (bf16) = the layer's output for x [tokens, width] (bf16)."""
+        s, g = self.shape, self.gpu
+        T, w = s.tokens, s.width
+        if self.fused:
+            g.gemm(MatmulSpec.new(T, 3 * w, w), x, self.w_qkv, self.qkv_heads, bias=self.b_qkv,
+                   output_heads=self.layout(3 * w, 0))
+        else:
+            g.gemm(MatmulSpec.new(T, 3 * w, w), x, self.w_qkv, self.qkv, bias=self.b_qkv)
+            for p in range(3):
+                g.split_heads(self.qkv, self.qkv_heads[p], self.layout(3 * w, p * w))
+        q, k, v = self.qkv_heads
+        g.causal_attention_forward(q, k, v, self.o_heads, self.scale, 0, self.lse)
+        if self.fused:
+            g.gemm(MatmulSpec.new(T, w, w), self.o_heads, self.w_o, y, bias=self.b_o, left_heads=self.layout(w, 0))
+        else:
+            g.merge_heads(self.o_heads, self.o, self.layout(w, 0))
+            g.gemm(MatmulSpec.new(T, w, w), self.o, self.w_o, y, bias=self.b_o)
+
+    def backward(self, x, dy, dx) -> None:
+        """Accumulates g_wqkv and g_wo and writes dx [tokens, width] (bf16) for the output gradient dy (bf16)."""
+        s, g = self.shape, self.gpu
+        T, w = s.tokens, s.width
+        det = self.deterministic
+        if self.fused:
+            g.gemm(MatmulSpec.new(w, w, T).left_transposed().accumulate(), self.o_heads, dy, self.g_wo,
+                   left_heads=self.layout(w, 0), deterministic=det)
+            g.gemm(MatmulSpec.new(T, w, w).right_transposed(), dy, self.w_o, self.do_heads,
+                   output_heads=self.layout(w, 0))
+        else:
+            g.gemm(MatmulSpec.new(w, w, T).left_transposed().accumulate(), self.o, dy, self.g_wo, deterministic=det)
+            g.gemm(MatmulSpec.new(T, w, w).right_transposed(), dy, self.w_o, self.d_o)
+            g.split_heads(self.d_o, self.do_heads, self.layout(w, 0))
+        q, k, v = self.qkv_heads
+        g.causal_attention_backward(q, k, v, self.o_heads, self.do_heads, self.lse, self.dq, self.dk, self.dv,
+                                    self.scale, 0)
+        for p, grad in enumerate((self.dq, self.dk, self.dv)):
+            g.merge_heads(grad, self.d_qkv, self.layout(3 * w, p * w))
+        g.gemm(MatmulSpec.new(w, 3 * w, T).left_transposed().accumulate(), x, self.d_qkv, self.g_wqkv,
+               deterministic=det)
+        g.gemm(MatmulSpec.new(T, w, 3 * w).right_transposed(), self.d_qkv, self.w_qkv, dx)

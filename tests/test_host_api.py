@@ -163,3 +163,64 @@ def test_gemm_rejects_unknown_flags():
     a.flags = 2
     assert lib.snb_gemm(None, ctypes.byref(a)) == _ffi.ERR_INVALID_ARGUMENT
     assert "flags" in _ffi.last_error()
+
+
+def test_head_layout_matches_the_reference_struct_and_builders():
+    # HeadLayout (kernels/attention.rs:19-69) and its unit tests (ops/attention.rs:104-140).
+    from staleynet_b200._ffi import HeadLayout
+
+    assert ctypes.sizeof(HeadLayout) == 64
+    L = HeadLayout.dense(2, 5, 4, 8, 32, 16)
+    assert (L.batch, L.time, L.heads, L.head_dim, L.width, L.column_offset) == (2, 5, 4, 8, 32, 16)
+    assert (L.time_capacity, L.time_offset) == (5, 0)
+    c = L.in_cache(9, 3)
+    assert (c.time, c.time_capacity, c.time_offset, c.heads, c.head_dim) == (5, 9, 3, 4, 8)
+
+
+def test_head_permutes_check_the_layout_in_the_reference_order():
+    # check_layout (ops/attention.rs:11-18): capacity, then the packed tensor, then the head-major tensor; the
+    # messages are the reference's. Fake pointers: every case fails before any device access.
+    from staleynet_b200._ffi import HeadLayout
+
+    lib = _ffi.load()
+    fake = 0x1000
+    L = HeadLayout.dense(2, 5, 3, 4, 38, 13).in_cache(9, 2)
+    packed, heads = 2 * 5 * 38, 2 * 3 * 9 * 4
+    bad_cap = HeadLayout.dense(2, 5, 3, 4, 38, 13).in_cache(6, 2)
+    cases = [(bad_cap, packed, heads, "time range exceeds capacity"),
+             (L, packed - 1, heads - 1, "packed tensor too small"),
+             (L, packed, heads - 1, "head-major tensor too small")]
+    for layout, p_len, h_len, msg in cases:
+        assert lib.snb_split_heads(None, fake, p_len, fake, h_len, ctypes.byref(layout)) == _ffi.ERR_INVALID_ARGUMENT
+        assert _ffi.last_error() == "HeadLayout: " + msg
+        assert lib.snb_merge_heads(None, fake, h_len, fake, p_len, ctypes.byref(layout)) == _ffi.ERR_INVALID_ARGUMENT
+        assert _ffi.last_error() == "HeadLayout: " + msg
+    assert lib.snb_permute_heads(None, 7, fake, 0, packed, fake, 0, heads, ctypes.byref(L)) == \
+        _ffi.ERR_INVALID_ARGUMENT
+
+
+def test_gemm_head_layouts_must_describe_their_operand():
+    from staleynet_b200._ffi import HeadLayout
+
+    lib = _ffi.load()
+    B, S, H, d = 2, 128, 2, 64
+    w, T = H * d, B * S
+    a = _ffi.GemmArgs()
+    a.product = MatmulSpec.new(T, w, w).product()
+    a.count = 1
+    a.left_type = a.right_type = a.output_type = _ffi.TYPE_BF16
+    a.aux_type = _ffi.TYPE_F32
+    a.precision = _ffi.PRECISION_BF16
+    a.left = a.right = a.output = 0x1000
+    a.left_len, a.right_len, a.output_len = T * w, w * w, T * w
+    wrong = HeadLayout.dense(B, S, H, d, 3 * w, 0)       # width of a fused QKV row: not this operand
+    a.left_heads = ctypes.pointer(wrong)
+    assert lib.snb_gemm(None, ctypes.byref(a)) == _ffi.ERR_INVALID_ARGUMENT
+    assert "left_heads" in _ffi.last_error()
+    a.left_heads = None
+    a.output_heads = ctypes.pointer(HeadLayout.dense(B, S + 1, H, d, w, 0))   # rows != batch * time
+    assert lib.snb_gemm(None, ctypes.byref(a)) == _ffi.ERR_INVALID_ARGUMENT
+    assert "output_heads" in _ffi.last_error()
+    big = HeadLayout.dense(B, S, H, d, w, 0).in_cache(2 * S, 0)   # the head-major output holds more than T * w
+    a.output_heads = ctypes.pointer(big)
+    assert lib.snb_gemm(None, ctypes.byref(a)) == _ffi.ERR_OUTPUT_TOO_SMALL
