@@ -25,6 +25,7 @@ the host cores, timed on a sample of every GEMM's output rows and extrapolated b
 from __future__ import annotations
 
 import argparse
+import ctypes
 import json
 import os
 import statistics
@@ -84,8 +85,12 @@ def load_kernel_traffic(kernel: str):
     return load_profile_traffic("fused_attention_cfg4_kernels.json", kernel)
 
 
-def workload_config(shape, n_gpus: int, global_sequences: int = 256, micro_per_rank: int = 8) -> dict:
-    if global_sequences:
+def workload_config(shape, n_gpus: int, global_sequences: int = 256, micro_per_rank: int = 8,
+                    model: str = "cfg3") -> dict:
+    if model == "cfg1":
+        workload = ("cfg1 6-block width-256 decoder: linear + 4x1024 codebook-head GEMMs, fwd+dX+dW with the codebook "
+                    "cross-entropy between them, one 8x512 micro-batch per GPU")
+    elif global_sequences:
         workload = (f"cfg5 data-parallel training step of the cfg3 model (12 blocks, width 768): global batch "
                     f"{global_sequences} x 2048 tokens split over {n_gpus} GPU(s), {micro_per_rank} micro-batch(es) "
                     f"of 32 x 2048 per GPU accumulating dW, linear + 16x1024 codebook-head GEMMs fwd+dX+dW with "
@@ -95,15 +100,16 @@ def workload_config(shape, n_gpus: int, global_sequences: int = 256, micro_per_r
                     "codebook cross-entropy between them, one 32x2048 micro-batch per GPU")
     return {
         "workload": workload,
-        "model": "staleynet width-768 12-block decoder (111.5M), linear/head GEMMs",
+        "model": (f"staleynet width-{shape.width} {shape.blocks}-block decoder, linear/head GEMMs"),
         "blocks": shape.blocks,
         "width": shape.width,
         "ffn": shape.ffn,
         "head": f"{shape.codebooks}x{shape.codebook_size}",
         "tokens_per_micro_batch": shape.tokens,
         "micro_batches_per_gpu": micro_per_rank,
-        "global_batch": global_sequences if global_sequences else 32 * n_gpus,
-        "seq_len": SEQ_LEN,
+        "global_batch": (8 * n_gpus if model == "cfg1" else
+                         global_sequences if global_sequences else 32 * n_gpus),
+        "seq_len": 512 if model == "cfg1" else SEQ_LEN,
         "parallelism": f"dp{n_gpus}",
         "operands": "bf16 in, f32 accumulate; dW f32 via reduce-add; activations bf16",
         "l2": "inputs larger than L2: one micro-batch moves > 20 GB through HBM (126 MB L2 flushed by the work "
@@ -282,7 +288,7 @@ def run_reference(args, shape, rank: int, world: int) -> int:
         "dtype": "f32", "data": "synthetic",
         "config": workload_config(shape, args.gpus, args.global_batch,
                                   max(1, args.global_batch // MICRO_SEQUENCES // max(1, args.gpus))
-                                  if args.global_batch else 1),
+                                  if args.global_batch else 1, args.model),
         "cpu_baseline": {"value": value, "unit": UNIT, "cores": r["cores"], "kind": "port", "sample": r["sample"],
                          "single_thread": single_thread_baseline(shape, args.cpu_sample_flops / 40)},
         "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
@@ -313,6 +319,55 @@ def micro_batch_plan(global_sequences: int, world: int, rank: int) -> tuple[int,
                          f"[{shard.first}, {shard.first + shard.count}), not whole {MICRO_SEQUENCES}-sequence "
                          f"micro-batches")
     return shard.first // MICRO_SEQUENCES, shard.count // MICRO_SEQUENCES, global_sequences // MICRO_SEQUENCES
+
+
+def model_shape(name: str, tokens: int):
+    """BASELINE config 3's model (12 blocks, width 768, 16 x 1024 head, 32 x 2048 tokens per micro-batch) or config
+    1's (6 blocks, width 256, FFN 1024, 4 x 1024 head, 8 x 512 tokens)."""
+    from staleynet_b200.step import ModelShape
+
+    if name == "cfg1":
+        return ModelShape(blocks=6, width=256, ffn=1024, codebooks=4, codebook_size=1024, tokens=8 * 512)
+    return ModelShape(tokens=tokens)
+
+
+def cublas_rate(device, precision: str, seconds: float = 3.0) -> dict:
+    """cuBLAS (torch.matmul) on 8192^3 at the step's precision, as MEASURED_PEAKS.json measures bf16: best of 10
+    launches (burst) and back to back for `seconds` (sustained). A comparison figure only; nothing of the step runs
+    on cuBLAS."""
+    import torch
+
+    n = 8192
+    dtype = torch.bfloat16 if precision == "bf16" else torch.float32
+    prev = torch.backends.cuda.matmul.allow_tf32
+    torch.backends.cuda.matmul.allow_tf32 = precision == "tf32"
+    try:
+        a = torch.randn(n, n, device=device, dtype=dtype)
+        b = torch.randn(n, n, device=device, dtype=dtype)
+        c = torch.empty(n, n, device=device, dtype=dtype)
+        flops = 2.0 * n ** 3
+        for _ in range(3):
+            torch.matmul(a, b, out=c)
+        best = float("inf")
+        for _ in range(10):
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record()
+            torch.matmul(a, b, out=c)
+            e1.record()
+            e1.synchronize()
+            best = min(best, e0.elapsed_time(e1) / 1e3)
+        reps = max(1, int(seconds / best))
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(reps):
+            torch.matmul(a, b, out=c)
+        e1.record()
+        e1.synchronize()
+        sustained = flops * reps / (e0.elapsed_time(e1) / 1e3) / 1e12
+        return {"burst_tflops": flops / best / 1e12, "sustained_tflops": sustained,
+                "how": f"torch.matmul {precision} {n}^3: best of 10 (burst), {reps} back to back (sustained)"}
+    finally:
+        torch.backends.cuda.matmul.allow_tf32 = prev
 
 
 def relative_frobenius(expected, actual) -> float:
@@ -351,16 +406,19 @@ def run_ours(args, shape, rank: int, world: int, local_rank: int) -> int:
     from staleynet_b200.data_parallel import OverlappedAllReduce, global_grad_scale
     from staleynet_b200.step import TrainingStepGemms
 
+    from staleynet_b200 import _ffi
+
     torch.cuda.set_device(local_rank)
     device = torch.device("cuda", local_rank)
     stream = torch.cuda.current_stream(device)
+    precision = {"bf16": _ffi.PRECISION_BF16, "tf32": _ffi.PRECISION_TF32, "f32": _ffi.PRECISION_F32}[args.precision]
     first_micro, n_micro, global_micro = micro_batch_plan(args.global_batch, world, rank)
     # The loss-gradient scale counts the valid targets of the whole global batch (training.rs:214-221 counts the
     # local batch; every target drawn by below(1024) is valid).
     scale = global_grad_scale(n_micro * shape.tokens, shape.codebooks) if world > 1 else \
         1.0 / (n_micro * shape.tokens * shape.codebooks)
     step = TrainingStepGemms(shape, device, micro_batches=n_micro, first_micro_batch=first_micro, grad_scale=scale,
-                             deterministic=args.deterministic)
+                             deterministic=args.deterministic, precision=precision)
     handle = stream.cuda_stream
     reducer = OverlappedAllReduce(compute_stream=stream) if world > 1 else None
 
@@ -493,11 +551,17 @@ def run_ours(args, shape, rank: int, world: int, local_rank: int) -> int:
         cpu = cpu_baseline(shape, budget_flops=args.cpu_sample_flops)
         cpu["single_thread"] = single_thread_baseline(shape, args.cpu_sample_flops / 40)
 
+    cublas = cublas_rate(device, args.precision) if args.precision != "bf16" and rank == 0 else None
     if rank == 0:
         peaks, source = load_peaks()
-        traffic = load_traffic(shape)
+        traffic = load_traffic(shape) if args.precision == "bf16" else {}
         peak_sus = float(peaks.get("bf16_tflops_sustained", FALLBACK_PEAKS["bf16_tflops_sustained"]))
         peak_burst = float(peaks.get("bf16_tflops", FALLBACK_PEAKS["bf16_tflops"]))
+        peak_source = (f"{source} bf16_tflops_sustained (kernel timed inside a long step); burst {peak_burst}")
+        if cublas is not None:
+            # TF32 and f32 have no driver-measured peak: the same cuBLAS measurement, taken in this run.
+            peak_sus, peak_burst = cublas["sustained_tflops"], cublas["burst_tflops"]
+            peak_source = f"cuBLAS {args.precision} measured in this run: {cublas['how']}; burst {peak_burst:.1f}"
         flops_rank = step.plan_flops * n_micro
         ms_step = ms_total / args.steps
         value = flops_rank * world * args.steps / (ms_total / 1e3) / 1e12
@@ -508,23 +572,25 @@ def run_ours(args, shape, rank: int, world: int, local_rank: int) -> int:
             "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": ms_step, "higher_is_better": True,
             "scaling": "strong" if args.global_batch else "weak",
-            "vs_baseline": None, "dtype": "bf16", "data": "synthetic: " + GENERATOR + "; activations "
-                                                           "N(0,1), weights N(0,1/sqrt(768)), targets below(1024)",
-            "config": dict(workload_config(shape, world, args.global_batch, n_micro),
-                           **({"deterministic": True} if args.deterministic else {})),
-            "pct_bf16_peak_sustained": 100.0 * (value / world) / peak_sus,
-            "pct_bf16_peak_burst": 100.0 * (value / world) / peak_burst,
+            "vs_baseline": None, "dtype": args.precision,
+            "data": "synthetic: " + GENERATOR + f"; activations N(0,1), weights N(0,1/sqrt({shape.width})), "
+                                                "targets below(1024)",
+            "config": dict(workload_config(shape, world, args.global_batch, n_micro, args.model),
+                           precision=args.precision, **({"deterministic": True} if args.deterministic else {})),
+            f"pct_{args.precision}_peak_sustained": 100.0 * (value / world) / peak_sus,
+            f"pct_{args.precision}_peak_burst": 100.0 * (value / world) / peak_burst,
             "roofline": {
-                "bound": "tensor", "achieved": achieved, "peak": peak_sus, "unit": "TFLOP/s",
+                "bound": "fp32-fma" if args.precision == "f32" else "tensor", "achieved": achieved, "peak": peak_sus,
+                "unit": "TFLOP/s",
                 "frac": achieved / peak_sus, "traffic": traffic.get("traffic_bytes_per_launch"),
                 "traffic_source": traffic.get("source"),
                 "algorithmic_bytes_per_launch": traffic.get("algorithmic_bytes_per_launch"),
                 "achieved_hbm_gbs": (traffic["algorithmic_bytes_per_launch"] * launches * args.steps /
                                      (kernel_ms / 1e3) / 1e9) if "algorithmic_bytes_per_launch" in traffic else None,
                 "hbm_peak_gbs": float(peaks.get("hbm_gbs", FALLBACK_PEAKS["hbm_gbs"])),
-                "kernel": "snb::tc_gemm_kernel / tc_gemm_pair_kernel (all GEMM launches of a step on rank 0)",
-                "peak_source": f"{source} bf16_tflops_sustained (kernel timed inside a long step); "
-                               f"burst {peak_burst}",
+                "kernel": ("snb::simt_gemm_kernel (exact f32 FMA)" if args.precision == "f32" else
+                           "snb::tc_gemm_kernel / tc_gemm_pair_kernel") + " (all GEMM launches of a step on rank 0)",
+                "peak_source": peak_source,
                 "launches_per_step": launches,
                 "flops_per_step": flops_rank,
             },
@@ -550,6 +616,63 @@ def run_ours(args, shape, rank: int, world: int, local_rank: int) -> int:
             line["cpu_baseline"] = {k: cpu[k] for k in ("value", "unit", "cores", "kind", "sample", "single_thread")}
         print(json.dumps(line), flush=True)
     del step
+    return 0
+
+
+def run_gemm(args, rank: int, world: int, local_rank: int) -> int:
+    """Individual GEMMs of the training step, each timed alone: the step's buffers are built, one full micro-batch
+    pass fills every activation and gradient, then each GEMM named in --names (block 0's instance, the head's for
+    head.*) is launched --warmup times untimed and --steps times between CUDA events. For profiling one product of
+    the step at a chosen token count (e.g. ncu on expand.fwd at 16,384 tokens)."""
+    import torch
+
+    from staleynet_b200 import _ffi
+    from staleynet_b200.step import TrainingStepGemms
+
+    torch.cuda.set_device(local_rank)
+    device = torch.device("cuda", local_rank)
+    stream = torch.cuda.current_stream(device)
+    precision = {"bf16": _ffi.PRECISION_BF16, "tf32": _ffi.PRECISION_TF32, "f32": _ffi.PRECISION_F32}[args.precision]
+    shape = model_shape(args.model, args.tokens)
+    step = TrainingStepGemms(shape, device, precision=precision, deterministic=args.deterministic)
+    handle = stream.cuda_stream
+    step.run(handle)
+    torch.cuda.synchronize()
+    firsts = {}
+    for name, flops, a in step.plan:
+        firsts.setdefault(name, (flops, a))
+    names = [n for n in args.names.split(",") if n] if args.names else list(firsts)
+    unknown = [n for n in names if n not in firsts]
+    if unknown:
+        raise SystemExit(f"unknown GEMM name(s) {unknown}; the step's are {list(firsts)}")
+    h = ctypes.c_void_p(handle)
+    lib = _ffi.load()
+    results = {}
+    clocks = ClockSampler(local_rank)
+    clocks.start()
+    for name in names:
+        flops, a = firsts[name]
+        for _ in range(args.warmup):
+            if lib.snb_gemm(h, ctypes.byref(a)) != _ffi.OK:
+                raise SystemExit(f"{name}: {_ffi.last_error()}")
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for _ in range(args.steps):
+            lib.snb_gemm(h, ctypes.byref(a))
+        e1.record(stream)
+        torch.cuda.synchronize()
+        ms = e0.elapsed_time(e1) / args.steps
+        results[name] = {"ms": ms, "tflops": flops / (ms / 1e3) / 1e12, "path": _ffi.last_path(),
+                         "m_n_k": [a.product.rows, a.product.cols, a.product.inner]}
+    clock_info = clocks.stop()
+    if rank == 0:
+        peaks, source = load_peaks()
+        burst = float(peaks.get("bf16_tflops", FALLBACK_PEAKS["bf16_tflops"]))
+        for r in results.values():
+            r["pct_bf16_burst"] = 100.0 * r["tflops"] / burst
+        print(json.dumps({"workload": "gemm", "tokens": shape.tokens, "precision": args.precision,
+                          "steps": args.steps, "warmup": args.warmup, "gemms": results, "clocks": clock_info,
+                          "peak_source": f"{source} bf16_tflops (burst): isolated launches"}), flush=True)
     return 0
 
 
@@ -1011,16 +1134,23 @@ def main(argv=None) -> int:
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--tokens", type=int, default=32 * 2048, help="tokens per GPU (default: BASELINE config 3)")
     ap.add_argument("--cpu-sample-flops", type=float, default=40e9)
+    ap.add_argument("--precision", choices=["bf16", "tf32", "f32"], default="bf16",
+                    help="step workload: bf16 tensors on bf16 tensor cores (default); f32 tensors on TF32 tensor cores "
+                         "(the reference's MatmulKernel::TensorCore); f32 tensors on the exact-f32 SIMT kernel "
+                         "(MatmulKernel::Blocked)")
+    ap.add_argument("--model", choices=["cfg3", "cfg1"], default="cfg3",
+                    help="step workload's model: BASELINE config 3 (default; config 5 over GPUs) or config 1")
     ap.add_argument("--deterministic", action="store_true",
                     help="step workload: every GEMM with SNB_GEMM_DETERMINISTIC (fixed-order split-K sums)")
     ap.add_argument("--global-batch", type=int, default=256,
                     help="sequences of 2048 tokens per step over all GPUs (config 5: 256, run as 32-sequence "
                          "micro-batches); 0 = one 32-sequence micro-batch per GPU")
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--workload", choices=["step", "attention", "head", "optimizer", "norm"], default="step",
+    ap.add_argument("--names", default="", help="gemm workload: comma-separated GEMMs of the step (default: all)")
+    ap.add_argument("--workload", choices=["step", "attention", "head", "optimizer", "norm", "gemm"], default="step",
                     help="step: the cfg3 training-step GEMMs (default); attention: the cfg4 attention layer; "
                          "head: the cfg3 output layer's forward + cross-entropy; optimizer: the cfg3 AdamW step; "
-                         "norm: RMSNorm into the QKV product")
+                         "norm: RMSNorm into the QKV product; gemm: single products of the step (--names)")
     ap.add_argument("--attention-path", choices=["fused", "materialised"], default="fused",
                     help="attention workload: fused entry points (default) or the six materialised products")
     ap.add_argument("--head-path", choices=["fused", "reference-shaped"], default="fused",
@@ -1031,9 +1161,9 @@ def main(argv=None) -> int:
     if args.warmup < 3:
         ap.error("--warmup must be at least 3")
 
-    from staleynet_b200.step import ModelShape
-
-    shape = ModelShape(tokens=args.tokens)
+    shape = model_shape(args.model, args.tokens)
+    if args.model == "cfg1":
+        args.global_batch = 0   # config 1 is one 8 x 512 micro-batch per GPU
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
     local_rank = int(os.environ.get("LOCAL_RANK", "0"))
@@ -1063,6 +1193,8 @@ def main(argv=None) -> int:
             return run_optimizer(args, rank, world, local_rank)
         if args.workload == "norm":
             return run_norm(args, rank, world, local_rank)
+        if args.workload == "gemm":
+            return run_gemm(args, rank, world, local_rank)
         return run_ours(args, shape, rank, world, local_rank)
     finally:
         if world > 1:

@@ -21,9 +21,9 @@ slice of it, so any rank can rebuild any micro-batch.
 
 Attention scores, softmax and norms are not GEMMs of the linear stack and are not part of this workload (the
 attention products are covered by the tests and by snb_causal_softmax); their activations are stood in for by
-seeded tensors of the same shapes. Operands are bf16 with f32 accumulation; weight gradients accumulate in f32
-through the tensor core's reduce-add epilogue; activations and activation gradients are written in bf16 by the
-producing GEMM's epilogue.
+seeded tensors of the same shapes. Operands are bf16 with f32 accumulation (or f32 tensors on TF32 tensor cores or
+the exact-f32 SIMT kernel); weight gradients accumulate in f32 through the tensor core's reduce-add epilogue;
+activations and activation gradients are written in the operand type by the producing GEMM's epilogue.
 """
 from __future__ import annotations
 
@@ -80,25 +80,32 @@ class TrainingStepGemms:
     micro_batches: micro-batches this process runs per step, global indices first_micro_batch, +1, ... .
     grad_scale: the loss-gradient scale 1 / (valid targets x codebooks) of the whole step (all micro-batches of
     all ranks; training.rs:214-221); by default that of this process's micro-batches alone.
-    deterministic: every product runs with SNB_GEMM_DETERMINISTIC (weight gradients bit-identical between runs)."""
+    deterministic: every product runs with SNB_GEMM_DETERMINISTIC (weight gradients bit-identical between runs).
+    precision: SNB_PRECISION_BF16 (bf16 activations and weights, the default), SNB_PRECISION_TF32 or
+    SNB_PRECISION_F32 (f32 tensors, as the reference holds them, device.rs:245-275, on TF32 tensor cores or on the
+    exact-f32 SIMT kernel: the reference's MatmulKernel::TensorCore and ::Blocked, device.rs:38-67)."""
 
     def __init__(self, shape: ModelShape, device, seed: int = WEIGHT_SEED, micro_batches: int = 1,
-                 first_micro_batch: int = 0, grad_scale: float | None = None, deterministic: bool = False):
+                 first_micro_batch: int = 0, grad_scale: float | None = None, deterministic: bool = False,
+                 precision: int = _ffi.PRECISION_BF16):
         import torch
 
         self.shape = shape
         self.device = device
         self.deterministic = deterministic
+        self.precision = precision
         self.lib = _ffi.load()
         s = shape
         T, w, f, V = s.tokens, s.width, s.ffn, s.head_width
-        bf16, f32 = torch.bfloat16, torch.float32
+        f32 = torch.float32
+        act = torch.bfloat16 if precision == _ffi.PRECISION_BF16 else f32   # element type of every tensor
+        self.elem_type = _ffi.TYPE_BF16 if precision == _ffi.PRECISION_BF16 else _ffi.TYPE_F32
         self.gpu = Gpu(device.index if device.index is not None else 0)
         # Weights and stand-ins come from the reference's generator (Random::new(seed), random.rs:27-70), drawn on
         # the device in the order they are created here.
         rng = DeviceRandom(self.gpu, seed)
 
-        def normal(n, std, dtype=bf16):
+        def normal(n, std, dtype=act):
             return rng.normal_(torch.empty(n, device=device, dtype=dtype), std)
 
         wstd = 1.0 / (w ** 0.5)
@@ -125,25 +132,25 @@ class TrainingStepGemms:
         for _ in range(s.blocks):
             self.acts.append({
                 "ctx": normal(T * w, 1.0),      # attention context (stands in for the attention output)
-                "qkv": torch.empty(T * 3 * w, device=device, dtype=bf16),
-                "mid": torch.empty(T * w, device=device, dtype=bf16),
-                "pre": torch.empty(T * f, device=device, dtype=bf16),
-                "hid": torch.empty(T * f, device=device, dtype=bf16),
-                "out": torch.empty(T * w, device=device, dtype=bf16),
+                "qkv": torch.empty(T * 3 * w, device=device, dtype=act),
+                "mid": torch.empty(T * w, device=device, dtype=act),
+                "pre": torch.empty(T * f, device=device, dtype=act),
+                "hid": torch.empty(T * f, device=device, dtype=act),
+                "out": torch.empty(T * w, device=device, dtype=act),
             })
-        self.logits = torch.empty(T * V, device=device, dtype=bf16)   # overwritten in place by the loss gradient
+        self.logits = torch.empty(T * V, device=device, dtype=act)   # overwritten in place by the loss gradient
         # Gradient buffers (reused across blocks, as the reference's shared gradient workspace).
-        self.g_x = torch.empty(T * w, device=device, dtype=bf16)
-        self.g_mid = torch.empty(T * w, device=device, dtype=bf16)
-        self.g_pre = torch.empty(T * f, device=device, dtype=bf16)
-        self.g_ctx = torch.empty(T * w, device=device, dtype=bf16)
+        self.g_x = torch.empty(T * w, device=device, dtype=act)
+        self.g_mid = torch.empty(T * w, device=device, dtype=act)
+        self.g_pre = torch.empty(T * f, device=device, dtype=act)
+        self.g_ctx = torch.empty(T * w, device=device, dtype=act)
         self.g_qkv = normal(T * 3 * w, 1.0)  # attention's gradient w.r.t. the fused projection (stand-in)
-        self.g_in = torch.empty(T * w, device=device, dtype=bf16)
+        self.g_in = torch.empty(T * w, device=device, dtype=act)
 
         # The step's micro-batches: input activations and targets, resident on the device.
         self.micro_batches = micro_batches
         self.first_micro_batch = first_micro_batch
-        self.inputs = torch.empty(micro_batches, T * w, device=device, dtype=bf16)
+        self.inputs = torch.empty(micro_batches, T * w, device=device, dtype=act)
         self.targets = torch.empty(micro_batches, T * s.codebooks, device=device, dtype=torch.int32)
         for m in range(micro_batches):
             self.load_micro_batch(first_micro_batch + m, self.inputs[m], self.targets[m])
@@ -157,7 +164,7 @@ class TrainingStepGemms:
         self._build_plan()
 
     def load_micro_batch(self, global_index: int, x, targets) -> None:
-        """Fills x ([tokens * width] bf16) and targets ([tokens * codebooks] int32) with micro-batch `global_index`
+        """Fills x ([tokens * width], the step's element type) and targets ([tokens * codebooks] int32) with micro-batch `global_index`
         of the global batch: slice global_index of the input stream (N(0,1) activations) and of the target stream
         (`below(codebook_size)`, as the reference's bench draws targets, bench.rs:152-154)."""
         s = self.shape
@@ -174,15 +181,15 @@ class TrainingStepGemms:
         a = _ffi.GemmArgs()
         a.product = spec.product()
         a.count = spec.batch.count
-        a.left_type = a.right_type = _ffi.TYPE_BF16
+        a.left_type = a.right_type = self.elem_type
         a.output_type = _ffi.TYPE_BF16 if output.dtype == torch.bfloat16 else _ffi.TYPE_F32
-        a.precision = _ffi.PRECISION_BF16
+        a.precision = self.precision
         a.left, a.left_len = left.data_ptr(), left.numel()
         a.right, a.right_len = right.data_ptr(), right.numel()
         a.output, a.output_len = output.data_ptr(), output.numel()
         a.bias = bias.data_ptr() if bias is not None else None
         a.activation = activation
-        a.aux_type = _ffi.TYPE_BF16
+        a.aux_type = self.elem_type
         a.pre_activation = pre.data_ptr() if pre is not None else None
         a.gelu_input = gelu_input.data_ptr() if gelu_input is not None else None
         a.residual = residual.data_ptr() if residual is not None else None
@@ -296,12 +303,12 @@ class TrainingStepGemms:
             if events is not None:
                 events[i][1].record()
             if i == nfwd - 1:
-                # Every codebook's loss and its gradient, written over the bf16 logits (training.rs:209-235).
+                # Every codebook's loss and its gradient, written over the logits (training.rs:209-235).
                 code = self.lib.snb_codebook_cross_entropy(
-                    h, self.logits.data_ptr(), _ffi.TYPE_BF16, s.tokens, s.codebooks, s.codebook_size,
+                    h, self.logits.data_ptr(), self.elem_type, s.tokens, s.codebooks, s.codebook_size,
                     self.targets[micro_batch].data_ptr(), self.targets[micro_batch].numel(),
                     self.grad_scales.data_ptr(), self.loss_sums[micro_batch].data_ptr(), self.logits.data_ptr(),
-                    _ffi.TYPE_BF16)
+                    self.elem_type)
                 if code != _ffi.OK:
                     check(code)
             if on_block_done is not None and (i + 1 - nfwd) in ends:
