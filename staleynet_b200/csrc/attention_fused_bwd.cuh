@@ -20,9 +20,10 @@
 //     warps 0-11   per key row (TMEM lane quadrant warp % 4) and query group (warp / 4: 48, 48 and 32 of the 128
 //                  queries): P = 2^(S c + nl), dS = P (dP - D), causal and range masks applied, P^T stored bf16 into
 //                  TMEM, dS^T into shared memory; at the end warps 0-7 write dV and scale * dK.
-//     warps 8-11   also drain dQ_{i-1} after their share of tile i (queries on lanes): scale it and add it into the
-//                  global dQ (f32, zeroed by the host) with TMA reduce-add, each warp through its own two
-//                  128B-swizzled 32x32 staging boxes, while dV and dK of tile i run.
+//     warps 4-11   also drain dQ_{i-1} after their share of tile i (queries on lanes; warps 4-7 columns 0-31, warps
+//                  8-11 columns 32-63): scale it and add it into the global dQ (f32, zeroed by the host) with TMA
+//                  reduce-add, each warp through its own 128B-swizzled 32x32 staging box, while dV and dK of tile i
+//                  run.
 // Every mbarrier wait is bounded (see sm100_ptx.cuh).
 #pragma once
 
@@ -44,6 +45,8 @@ constexpr int FB_S_COL = 0, FB_DP_COL = 128, FB_DV_COL = 256, FB_DK_COL = 320, F
 struct FbParams {
     int32_t count, sq, sk;   // matrices; queries and keys per matrix
     int32_t q_tiles;         // query tiles per matrix
+    int32_t k_tiles;         // key tiles per matrix
+    int32_t group;           // matrices per scheduling group (see the block order in fb_backward_kernel)
     int64_t offset;          // query q sees keys 0..=q+offset
     float scale;             // softmax scale
     float scale_log2;        // scale * log2(e)
@@ -162,9 +165,16 @@ __global__ void __launch_bounds__(FB_THREADS, 1)
 
     const int warp = threadIdx.x >> 5;
     const int lane = threadIdx.x & 31;
-    // Longest first over the whole grid: key tile 0 of every matrix is seen by the most query tiles.
-    const int32_t key_tile = static_cast<int32_t>(blockIdx.x / p.count);
-    const int32_t matrix = static_cast<int32_t>(blockIdx.x % p.count);
+    // Block order: matrices in groups of p.group, and within a group the longest key tiles first (key tile 0 of
+    // every matrix of the group is seen by the most query tiles). The CTAs running at one time then share a few
+    // matrices, whose Q, dO and dQ (re-read or reduced into once per key tile) stay in L2, while the short tiles
+    // of each group still come last.
+    const int32_t per_group = p.group * p.k_tiles;
+    const int32_t grp = static_cast<int32_t>(blockIdx.x / per_group);
+    const int32_t in_group = static_cast<int32_t>(blockIdx.x % per_group);
+    const int32_t gsz = min(p.group, p.count - grp * p.group);   // the last group may hold fewer matrices
+    const int32_t key_tile = in_group / gsz;
+    const int32_t matrix = grp * p.group + in_group % gsz;
     const int32_t key0 = key_tile * FB_BK;
     // Query tiles with a query q >= key0 - offset (a query that sees some key of this tile), if any query does.
     const int64_t q_lo = static_cast<int64_t>(key0) - p.offset;
@@ -182,7 +192,7 @@ __global__ void __launch_bounds__(FB_THREADS, 1)
         mbar_init(smem_addr(pds_full), FB_ELEM_WARPS);
         mbar_init(smem_addr(pds_empty), 1);
         mbar_init(smem_addr(dq_full), 1);
-        mbar_init(smem_addr(dq_empty), 4);
+        mbar_init(smem_addr(dq_empty), 8);   // the eight draining warps (groups 1 and 2) have loaded dQ
         mbar_init(smem_addr(acc_done), 1);
         mbar_init(smem_addr(drain), 1);
         fence_mbarrier_init();
@@ -317,24 +327,26 @@ __global__ void __launch_bounds__(FB_THREADS, 1)
         const uint32_t lane_base = static_cast<uint32_t>(quad * 32) << 16;
         const uint32_t ds_row = smem_addr(ds_s + r * 128);   // row r of slice 0; slice s is DS/2 * s further
         const float c = p.scale_log2;
-        const bool drains = group == 2;
-        uint8_t* box0 = dq_s + quad * (FbSmem::DQ / 4);   // dQ staging: columns 0-31 of rows 32 quad ..
-        uint8_t* box1 = box0 + FbSmem::DQ / 8;             // columns 32-63
-        // dQ of tile m: scale it and add it into the global dQ through this warp's two 32x32 f32 staging boxes.
+        // dQ is drained by groups 1 and 2, group 1 taking columns 0-31 and group 2 columns 32-63 of its quadrant's 32
+        // queries: split this way the drain adds ~500 cycles to both groups instead of ~1,000 to group 2 alone, whose
+        // two score chunks plus the whole drain were the longest path of a query tile.
+        const bool drains = group >= 1;
+        const int dq_half = group - 1;
+        uint8_t* box = dq_s + quad * (FbSmem::DQ / 4) + (drains ? dq_half : 0) * (FbSmem::DQ / 8);
+        // This warp's half of dQ of tile m: scale it and add it into the global dQ through its 32x32 f32 staging box.
         auto drain = [&](int32_t m) -> bool {
             if (!warp_wait(smem_addr(dq_full), m & 1)) return false;
             tcgen05_fence_after_sync();
-            uint32_t da[32], db[32];
-            tmem_load_32x32b_x32(tmem_base + lane_base + FB_DQ_COL, da);
-            tmem_load_32x32b_x32(tmem_base + lane_base + FB_DQ_COL + 32, db);
+            uint32_t da[32];
+            tmem_load_32x32b_x32(tmem_base + lane_base + FB_DQ_COL + 32 * dq_half, da);
             tmem_load_wait();
             tcgen05_fence_before_sync();
             __syncwarp();
             if (lane == 0) mbar_arrive(smem_addr(dq_empty));
-            // The staging boxes are free once this warp's previous reductions have read them.
+            // The staging box is free once this warp's previous reduction has read it.
             if (lane == 0) bulk_wait_group_read<0>();
             __syncwarp();
-            const uint32_t row0 = smem_addr(box0 + lane * 128), row1 = smem_addr(box1 + lane * 128);
+            const uint32_t row0 = smem_addr(box + lane * 128);
 #pragma unroll
             for (int g = 0; g < 8; ++g) {
                 const uint32_t off = (g ^ (lane & 7)) << 4;
@@ -342,17 +354,12 @@ __global__ void __launch_bounds__(FB_THREADS, 1)
                              __float_as_uint(__uint_as_float(da[4 * g + 1]) * p.scale),
                              __float_as_uint(__uint_as_float(da[4 * g + 2]) * p.scale),
                              __float_as_uint(__uint_as_float(da[4 * g + 3]) * p.scale));
-                st_shared_v4(row1 + off, __float_as_uint(__uint_as_float(db[4 * g]) * p.scale),
-                             __float_as_uint(__uint_as_float(db[4 * g + 1]) * p.scale),
-                             __float_as_uint(__uint_as_float(db[4 * g + 2]) * p.scale),
-                             __float_as_uint(__uint_as_float(db[4 * g + 3]) * p.scale));
             }
             fence_proxy_async_shared();
             __syncwarp();
             if (lane == 0) {
                 const int32_t q0 = (i_first + m) * FB_BQ + 32 * quad;
-                tma_reduce_add_3d(&tm_dq, smem_addr(box0), 0, q0, matrix);
-                tma_reduce_add_3d(&tm_dq, smem_addr(box1), 32, q0, matrix);
+                tma_reduce_add_3d(&tm_dq, smem_addr(box), 32 * dq_half, q0, matrix);
                 bulk_commit_group();
             }
             return true;
@@ -437,7 +444,9 @@ __global__ void __launch_bounds__(FB_THREADS, 1)
         if (drains) {
             if (ok && n_iter > 0) ok = drain(n_iter - 1);
             if (lane == 0) bulk_wait_group<0>();
-        } else if (ok && warp_wait(smem_addr(acc_done), 0)) {
+            __syncwarp();
+        }
+        if (group < 2 && ok && warp_wait(smem_addr(acc_done), 0)) {
             // dV (group 0) or scale * dK (group 1) of this warp's 32 key rows (zero when no query sees them). The
             // TMEM loads are warp-collective; only the stores depend on the row.
             const int h = group;

@@ -815,6 +815,10 @@ int fused_attention_backward(cudaStream_t stream, const void* q, const void* k, 
     fp.sq = static_cast<int32_t>(queries);
     fp.sk = static_cast<int32_t>(keys);
     fp.q_tiles = static_cast<int32_t>((queries + FB_BQ - 1) / FB_BQ);
+    fp.k_tiles = static_cast<int32_t>((keys + FB_BK - 1) / FB_BK);
+    // Scheduling groups of 8 matrices: a group's Q, dO, dQ and K, V (0.8 MB each per matrix at 3,072 x 64) fit in
+    // L2 many times over while one wave of CTAs covers about a group.
+    fp.group = static_cast<int32_t>(std::min<uint64_t>(count, 8));
     fp.offset = static_cast<int64_t>(query_offset);
     fp.scale = scale;
     fp.scale_log2 = scale * 1.4426950408889634f;
