@@ -422,20 +422,32 @@ def run_ours(args, shape, rank: int, world: int, local_rank: int) -> int:
     handle = stream.cuda_stream
     reducer = OverlappedAllReduce(compute_stream=stream) if world > 1 else None
 
+    lib = step.lib
+
     def on_block(b):
-        # The head's gradient is complete before block L-1's; both go out once block L-1's backward is queued.
+        # The head's gradient is complete before block L-1's; both go out once block L-1's backward is queued. From
+        # then on the rest of the backward's GEMMs may run on a reduced grid that leaves the collective its SMs.
         if b == shape.blocks - 1:
             reducer.submit(step.head_grad)
+            if args.gemm_sm_budget:
+                lib.snb_set_sm_budget(args.gemm_sm_budget)
         reducer.submit(step.block_grad_flat[b])
 
-    hook = on_block if world > 1 else None
+    # A captured micro-batch holds no collective: with --graph the all-reduces are issued after the backward.
+    overlap = world > 1 and args.comm == "overlap" and not args.graph
+    hook = on_block if overlap else None
 
     def finish(marks=None):
-        """Ends a step: the compute stream waits for every all-reduce. With `marks` (two events) the exposed
-        communication is bracketed: from the last GEMM's completion to the last all-reduce's."""
+        """Ends a step: the compute stream waits for every all-reduce (with --comm after, they are issued here, once
+        the whole backward is queued). With `marks` (two events) the exposed communication is bracketed: from the
+        last GEMM's completion to the last all-reduce's."""
         if marks is not None:
             marks[0].record(stream)
         if reducer is not None:
+            lib.snb_set_sm_budget(0)
+            if not overlap:
+                for _, t in step.grads.order():
+                    reducer.submit(t)
             reducer.wait()
         if marks is not None:
             marks[1].record(stream)
@@ -454,12 +466,25 @@ def run_ours(args, shape, rank: int, world: int, local_rank: int) -> int:
     timed = lambda: torch.cuda.Event(enable_timing=True)  # noqa: E731
     ev_steps = [[[(timed(), timed()) for _ in range(n_launch)] for _ in range(n_micro)] for _ in range(args.steps)]
     comm_marks = [(timed(), timed()) for _ in range(args.steps)]
+    graphs = [step.capture(m) for m in range(n_micro)] if args.graph else None
+    if graphs is not None:
+        torch.cuda.synchronize()
+        # The GEMM launch times of the roofline come from an uncaptured pass with events around each launch.
+        ev_pass = [[[(timed(), timed()) for _ in range(n_launch)] for _ in range(n_micro)]]
+        step.run_step(handle, events=ev_pass[0])
+        finish()
+        torch.cuda.synchronize()
     clocks = ClockSampler(local_rank)
     clocks.start()
     start, end = timed(), timed()
     start.record(stream)
     for k in range(args.steps):
-        step.run_step(handle, on_block_done=hook, events=ev_steps[k])
+        if graphs is None:
+            step.run_step(handle, on_block_done=hook, events=ev_steps[k])
+        else:
+            step.zero_grads()
+            for g in graphs:
+                g.replay()
         finish(comm_marks[k])
     end.record(stream)
     torch.cuda.synchronize()
@@ -467,7 +492,11 @@ def run_ours(args, shape, rank: int, world: int, local_rank: int) -> int:
     if world > 1:
         dist.barrier()
     ms_total = start.elapsed_time(end)
-    kernel_ms = sum(a.elapsed_time(b) for ev_micro in ev_steps for pairs in ev_micro for a, b in pairs)
+    if graphs is not None:
+        ev_steps = ev_pass
+        kernel_ms = sum(a.elapsed_time(b) for ev_micro in ev_pass for pairs in ev_micro for a, b in pairs) * args.steps
+    else:
+        kernel_ms = sum(a.elapsed_time(b) for ev_micro in ev_steps for pairs in ev_micro for a, b in pairs)
     exposed_ms = sum(a.elapsed_time(b) for a, b in comm_marks) / args.steps
 
     # End-to-end: every micro-batch's input activations come from pinned host memory and the step's per-codebook
@@ -485,6 +514,10 @@ def run_ours(args, shape, rank: int, world: int, local_rank: int) -> int:
     e_start, e_end = timed(), timed()
     copy_stream = torch.cuda.Stream(device)
     bufs = [torch.empty_like(step.x_in), torch.empty_like(step.x_in)]
+    # With --graph, one captured graph per (micro-batch, upload buffer), captured before the timed region.
+    e2e_graphs = ({(m, b): step.capture(m, x=bufs[b]) for m in range(n_micro) for b in range(2)}
+                  if args.graph else None)
+    torch.cuda.synchronize()
     ready = [torch.cuda.Event(), torch.cuda.Event()]
     released = [torch.cuda.Event(), torch.cuda.Event()]
     e_start.record(stream)
@@ -507,7 +540,10 @@ def run_ours(args, shape, rank: int, world: int, local_rank: int) -> int:
             if i + 1 < total_micro:
                 upload(i + 1)
             stream.wait_event(ready[i % 2])
-            step.run(handle, on_block_done=hook if m == n_micro - 1 else None, micro_batch=m, x=bufs[i % 2])
+            if e2e_graphs is None:
+                step.run(handle, on_block_done=hook if m == n_micro - 1 else None, micro_batch=m, x=bufs[i % 2])
+            else:
+                e2e_graphs[(m, i % 2)].replay()
             released[i % 2].record(stream)
         finish()
         host_loss.copy_(step.loss_sums, non_blocking=True)
@@ -519,7 +555,11 @@ def run_ours(args, shape, rank: int, world: int, local_rank: int) -> int:
     local_loss = float(host_loss.sum()) / (n_micro * shape.tokens * shape.codebooks)
 
     stats = torch.tensor([ms_total, e2e_ms_total, kernel_ms, exposed_ms], device=device, dtype=torch.float64)
+    exposed_min = exposed_ms
     if world > 1:
+        low = torch.tensor([exposed_ms], device=device, dtype=torch.float64)
+        dist.all_reduce(low, op=dist.ReduceOp.MIN)
+        exposed_min = float(low.item())
         dist.all_reduce(stats, op=dist.ReduceOp.MAX)
     ms_total, e2e_ms_total, kernel_ms, exposed_max = stats.tolist()
 
@@ -576,7 +616,9 @@ def run_ours(args, shape, rank: int, world: int, local_rank: int) -> int:
             "data": "synthetic: " + GENERATOR + f"; activations N(0,1), weights N(0,1/sqrt({shape.width})), "
                                                 "targets below(1024)",
             "config": dict(workload_config(shape, world, args.global_batch, n_micro, args.model),
-                           precision=args.precision, **({"deterministic": True} if args.deterministic else {})),
+                           precision=args.precision, **({"deterministic": True} if args.deterministic else {}),
+                           **({"cuda_graph": "each micro-batch replayed from a captured CUDA graph"}
+                              if args.graph else {})),
             f"pct_{args.precision}_peak_sustained": 100.0 * (value / world) / peak_sus,
             f"pct_{args.precision}_peak_burst": 100.0 * (value / world) / peak_burst,
             "roofline": {
@@ -605,11 +647,17 @@ def run_ours(args, shape, rank: int, world: int, local_rank: int) -> int:
         if world > 1:
             line["communication"] = {
                 "exposed_ms_per_step": exposed_max,
+                "exposed_ms_per_step_least_rank": exposed_min,
                 "what": "per step, from the last GEMM's completion to the last gradient all-reduce's (CUDA events "
-                        "on the compute stream; max over ranks)",
+                        "on the compute stream; max over ranks, and on the least-exposed rank: the difference is "
+                        "the wait for a slower rank)",
                 "all_reduce_bytes_per_step": 4 * (sum(t.numel() for t in step.block_grad_flat) +
                                                   step.head_grad.numel()),
                 "collective": "NCCL all-reduce (sum, f32) per bucket: head, then blocks L-1..0, on a side stream",
+                "mode": ("overlapped with the last micro-batch's backward" if args.comm == "overlap" else
+                         "issued after the whole backward is queued") +
+                        (f"; GEMM grid capped at {args.gemm_sm_budget} SMs meanwhile" if args.gemm_sm_budget and
+                         args.comm == "overlap" else ""),
             }
             line["dp_parity"] = dp_parity
         if cpu is not None:
@@ -1140,6 +1188,14 @@ def main(argv=None) -> int:
                          "(MatmulKernel::Blocked)")
     ap.add_argument("--model", choices=["cfg3", "cfg1"], default="cfg3",
                     help="step workload's model: BASELINE config 3 (default; config 5 over GPUs) or config 1")
+    ap.add_argument("--graph", action="store_true",
+                    help="step workload: each micro-batch's launches captured once into a CUDA graph and replayed "
+                         "(at N > 1 the all-reduces then follow the backward)")
+    ap.add_argument("--comm", choices=["overlap", "after"], default="overlap",
+                    help="N > 1: all-reduce each gradient bucket while the last micro-batch's backward runs "
+                         "(overlap) or all of them once the backward is queued (after)")
+    ap.add_argument("--gemm-sm-budget", type=int, default=0,
+                    help="N > 1 with --comm overlap: SMs the GEMM grid may use while the all-reduces run (0: all)")
     ap.add_argument("--deterministic", action="store_true",
                     help="step workload: every GEMM with SNB_GEMM_DETERMINISTIC (fixed-order split-K sums)")
     ap.add_argument("--global-batch", type=int, default=256,

@@ -225,6 +225,13 @@ enum {
     SNB_GEMM_DETERMINISTIC = 1
 };
 
+/* Caps, for the calling thread, the SMs that the persistent tensor-core GEMM grid of later snb_matmul,
+ * snb_matmul_bf16 and snb_gemm calls may occupy (sms <= 0: all of them, the default). The GEMM kernels keep one CTA
+ * (or CTA pair) per SM for the whole launch and assign work units to CTAs statically, so a kernel that holds some SMs
+ * meanwhile (a collective on another stream) stretches every GEMM by a whole CTA's share of work; with a budget the
+ * GEMM leaves those SMs free. Returns the previous setting. No reference counterpart. */
+SNB_API int snb_set_sm_budget(int32_t sms);
+
 /* Sets, for the calling thread, whether snb_matmul, snb_matmul_bf16 and snb_gemm run as with SNB_GEMM_DETERMINISTIC
  * (enabled != 0) — the switch for callers of the f32 drop-in, which has no flags argument. Returns the previous
  * setting (0 or 1). Off by default. No reference counterpart. */

@@ -55,6 +55,7 @@ EXPORTED_SYMBOLS = (
     "snb_matmul_bf16",
     "snb_gemm",
     "snb_set_deterministic",
+    "snb_set_sm_budget",
     "snb_causal_softmax",
     "snb_softmax_backward",
     "snb_causal_softmax_bf16",
@@ -194,6 +195,8 @@ def load() -> ctypes.CDLL:
         lib.snb_gemm.restype = c_int
         lib.snb_set_deterministic.argtypes = [c_int32]
         lib.snb_set_deterministic.restype = c_int
+        lib.snb_set_sm_budget.argtypes = [c_int32]
+        lib.snb_set_sm_budget.restype = c_int
         lib.snb_causal_softmax.argtypes = [c_void_p, c_void_p, c_uint64, c_uint64, c_uint64, c_uint64, c_float,
                                            c_uint64]
         lib.snb_causal_softmax.restype = c_int

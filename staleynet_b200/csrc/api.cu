@@ -16,6 +16,7 @@ namespace {
 thread_local std::string t_last_error;
 thread_local int t_last_path = SNB_PATH_NONE;
 thread_local bool t_deterministic = false;   // snb_set_deterministic
+thread_local int t_sm_budget = 0;            // snb_set_sm_budget
 
 int fail(int code, const std::string& message) {
     t_last_error = message;
@@ -140,7 +141,7 @@ using namespace snb;
 
 extern "C" {
 
-int snb_abi_version(void) { return 105; }
+int snb_abi_version(void) { return 106; }
 
 const char* snb_last_error(void) { return t_last_error.c_str(); }
 
@@ -163,6 +164,7 @@ int snb_matmul(void* stream, const snb_product* product, uint64_t count, const f
     r.C = output;
     r.aux_type = SNB_TYPE_F32;
     r.deterministic = t_deterministic;
+    r.sm_budget = t_sm_budget;
     return run(static_cast<cudaStream_t>(stream), r, left_len, right_len, output_len);
 }
 
@@ -181,7 +183,14 @@ int snb_matmul_bf16(void* stream, const snb_product* product, uint64_t count, co
     r.C = output;
     r.aux_type = SNB_TYPE_F32;
     r.deterministic = t_deterministic;
+    r.sm_budget = t_sm_budget;
     return run(static_cast<cudaStream_t>(stream), r, left_len, right_len, output_len);
+}
+
+int snb_set_sm_budget(int32_t sms) {
+    const int previous = t_sm_budget;
+    t_sm_budget = sms > 0 ? sms : 0;
+    return previous;
 }
 
 int snb_set_deterministic(int32_t enabled) {
@@ -263,6 +272,7 @@ int snb_gemm(void* stream, const snb_gemm_args* a) {
     r.deterministic = t_deterministic || (a->flags & SNB_GEMM_DETERMINISTIC) != 0;
     r.a_heads = a->left_heads;
     r.c_heads = a->output_heads;
+    r.sm_budget = t_sm_budget;
     return run(static_cast<cudaStream_t>(stream), r, a->left_len, a->right_len, a->output_len);
 }
 

@@ -30,6 +30,7 @@ struct GemmRequest {
     bool deterministic;       // split-K partials summed in a fixed order (SNB_GEMM_DETERMINISTIC)
     const snb_head_layout* a_heads;  // left operand read from its head-major form, or nullptr (snb_gemm_args)
     const snb_head_layout* c_heads;  // output written head-major, or nullptr
+    int sm_budget;            // SMs the persistent grid may occupy (0: all; snb_set_sm_budget)
 };
 
 struct DeviceInfo {

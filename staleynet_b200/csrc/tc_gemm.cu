@@ -320,11 +320,14 @@ int tc_gemm_try(cudaStream_t stream, const GemmRequest& r, bool* launched, int* 
     // hints are implemented by the single-CTA kernel only.
     constexpr int64_t kPairMinKBytes = 4096;  // K >= 2048 bf16 / 1024 f32
     constexpr int64_t kPairMaxNarrowCols = 1024;
-    const bool pair = bn == 256 && p.rows > TC_BM && r.causal == SNB_CAUSAL_NONE && dev.sm_count >= 2 &&
+    // SMs the persistent grid may occupy: all of them, or the caller's budget (which leaves the rest to kernels on
+    // other streams, e.g. a collective running beside the backward pass).
+    const int sms = r.sm_budget > 0 ? std::min(r.sm_budget, dev.sm_count) : dev.sm_count;
+    const bool pair = bn == 256 && p.rows > TC_BM && r.causal == SNB_CAUSAL_NONE && sms >= 2 &&
                       (static_cast<int64_t>(p.inner) * esize >= kPairMinKBytes ||
                        (bf16_in && static_cast<int64_t>(p.cols) <= kPairMaxNarrowCols));
     const int bm = pair ? TC2_BM : TC_BM;
-    const int workers = pair ? dev.sm_count / 2 : dev.sm_count;
+    const int workers = pair ? sms / 2 : sms;
     const int64_t m_tiles = (p.rows + bm - 1) / bm;
     const int64_t n_tiles = (p.cols + bn - 1) / bn;
     const int64_t k_blocks = (p.inner + bk - 1) / bk;
@@ -571,7 +574,7 @@ int tc_gemm_try(cudaStream_t stream, const GemmRequest& r, bool* launched, int* 
         }
         return rc;
     }
-    const int grid = static_cast<int>(std::min<int64_t>(units, dev.sm_count));
+    const int grid = static_cast<int>(std::min<int64_t>(units, sms));
     if (bf16_in) {
         rc = out_bf16 ? launch_bn<__nv_bfloat16, true>(bn, epi, stream, maps, kp, grid, err)
                       : launch_bn<__nv_bfloat16, false>(bn, epi, stream, maps, kp, grid, err);

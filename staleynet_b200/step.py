@@ -326,5 +326,18 @@ class TrainingStepGemms:
                      events=events[m] if events is not None else None, micro_batch=m,
                      x=inputs(m) if inputs is not None else None)
 
+    def capture(self, micro_batch: int = 0, x=None):
+        """Captures `run()` of local micro-batch `micro_batch` (forward, loss, backward; no collective hook) into a
+        CUDA graph and returns it (torch.cuda.CUDAGraph; `replay()` reissues every launch with one call). Every library
+        call on the path is capturable: kernel launches, split-K zeroing (memset nodes) and the deterministic mode's
+        stream-ordered workspace; per-device set-up happens on the first, uncaptured, run, so run() must have been
+        called once before. The graph holds the operand pointers of the capture: one graph per input buffer."""
+        import torch
+
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph):
+            self.run(torch.cuda.current_stream().cuda_stream, micro_batch=micro_batch, x=x)
+        return graph
+
     def zero_grads(self) -> None:
         self.grads.zero_()

@@ -71,7 +71,7 @@ def test_library_loads_and_exports_every_declared_symbol():
     for name in declared:
         assert hasattr(lib, name), f"{name} declared in the header but not exported"
     assert sorted(_ffi.EXPORTED_SYMBOLS) == declared
-    assert lib.snb_abi_version() == 105
+    assert lib.snb_abi_version() == 106
 
 
 def call_matmul(rows, cols, inner, left_len, right_len, output_len, count=1, precision=_ffi.PRECISION_F32):
@@ -224,3 +224,17 @@ def test_gemm_head_layouts_must_describe_their_operand():
     big = HeadLayout.dense(B, S, H, d, w, 0).in_cache(2 * S, 0)   # the head-major output holds more than T * w
     a.output_heads = ctypes.pointer(big)
     assert lib.snb_gemm(None, ctypes.byref(a)) == _ffi.ERR_OUTPUT_TOO_SMALL
+
+
+def test_sm_budget_is_per_thread_and_returns_the_previous_setting():
+    import threading
+
+    lib = _ffi.load()
+    assert lib.snb_set_sm_budget(100) == 0
+    seen = []
+    t = threading.Thread(target=lambda: seen.append(lib.snb_set_sm_budget(0)))
+    t.start()
+    t.join()
+    assert seen == [0]
+    assert lib.snb_set_sm_budget(-5) == 100      # non-positive: no cap
+    assert lib.snb_set_sm_budget(0) == 0

@@ -496,3 +496,37 @@ def test_empty_inner_dimension(gpu, accumulate):
         torch.cuda.synchronize()
         expected = initial if accumulate else np.zeros(35, np.float32)
         assert np.array_equal(out.cpu().numpy(), expected)
+
+
+@pytest.mark.parametrize("budget", [1, 2, 17, 132])
+def test_gemm_under_an_sm_budget_computes_the_same_product(gpu, budget):
+    # A capped persistent grid (snb_set_sm_budget) walks the same work units with fewer CTAs; the split-K choice may
+    # change with the worker count, so the weight gradient is compared within f32 summation-order tolerance.
+    g = torch.Generator(device="cuda").manual_seed(21)
+    T, i, o = 4096, 256, 768
+    x = torch.randn(T, i, device="cuda", generator=g).bfloat16()
+    w = torch.randn(i, o, device="cuda", generator=g).bfloat16()
+    dy = torch.randn(T, o, device="cuda", generator=g).bfloat16()
+    lib = _ffi.load()
+    outs = []
+    for b in (0, budget):
+        previous = lib.snb_set_sm_budget(b)
+        try:
+            y = torch.empty(T, o, device="cuda", dtype=torch.bfloat16)
+            gpu.gemm(MatmulSpec.new(T, o, i), x, w, y)
+            dw = torch.zeros(i, o, device="cuda")
+            gpu.gemm(MatmulSpec.new(i, o, T).left_transposed().accumulate(), x, dy, dw)
+            assert _ffi.last_path() in _ffi.TENSOR_CORE_PATHS or budget == 1
+        finally:
+            lib.snb_set_sm_budget(previous)
+        outs.append((y, dw))
+    torch.cuda.synchronize()
+    if budget >= 2:
+        assert torch.equal(outs[0][0], outs[1][0])   # same kernel, same tiles, no split: the same values
+    else:
+        # One SM rules out the CTA-pair kernel: the single-CTA tiles may round a few bf16 outputs the other way.
+        ry = (torch.linalg.vector_norm((outs[0][0] - outs[1][0]).float()) /
+              torch.linalg.vector_norm(outs[0][0].float())).item()
+        assert ry < 1e-3
+    rel = (torch.linalg.vector_norm(outs[0][1] - outs[1][1]) / torch.linalg.vector_norm(outs[0][1])).item()
+    assert rel < 1e-5

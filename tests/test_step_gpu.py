@@ -67,3 +67,22 @@ def test_step_loss_is_the_codebook_cross_entropy_of_its_logits():
         expected.append(float(losses.astype(np.float64).sum()))
     got = step.loss_sums[0].cpu().numpy().astype(np.float64)
     assert np.allclose(got, expected, rtol=1e-4)
+
+
+def test_a_captured_micro_batch_replays_the_same_gradients():
+    # The step's launches (GEMMs, split-K zeroing, the loss kernel) captured into a CUDA graph: one replay gives the
+    # gradients and loss of one run() (to f32 rounding: split-K partials land in arrival order).
+    dev = torch.device("cuda", 0)
+    h = torch.cuda.current_stream().cuda_stream
+    step = TrainingStepGemms(SHAPE, dev, micro_batches=1)
+    step.run_step(h)   # first run: per-device set-up outside the capture
+    torch.cuda.synchronize()
+    ref = _grads(step)
+    ref_loss = step.loss_sums.clone()
+    graph = step.capture(0)
+    step.zero_grads()
+    graph.replay()
+    torch.cuda.synchronize()
+    for a, b in zip(_grads(step), ref):
+        assert _rel(a, b) < 1e-6
+    assert torch.allclose(step.loss_sums, ref_loss, rtol=1e-6)
