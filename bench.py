@@ -281,14 +281,14 @@ def run_reference(args, shape, rank: int, world: int) -> int:
         vals.append(r["value"])
         secs.append(r["seconds_per_step_extrapolated"])
     value = statistics.median(vals)
+    # The sample times one micro-batch's GEMMs; a step is every micro-batch of one rank's share of the global batch.
+    micro = max(1, args.global_batch // MICRO_SEQUENCES // max(1, args.gpus)) if args.global_batch else 1
     line = {
         "impl": "reference", "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": args.gpus,
-        "steps": args.steps, "warmup": args.warmup, "ms_per_step": statistics.median(secs) * 1e3,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": statistics.median(secs) * 1e3 * micro,
         "higher_is_better": True, "scaling": "strong" if args.global_batch else "weak", "vs_baseline": None,
         "dtype": "f32", "data": "synthetic",
-        "config": workload_config(shape, args.gpus, args.global_batch,
-                                  max(1, args.global_batch // MICRO_SEQUENCES // max(1, args.gpus))
-                                  if args.global_batch else 1, args.model),
+        "config": workload_config(shape, args.gpus, args.global_batch, micro, args.model),
         "cpu_baseline": {"value": value, "unit": UNIT, "cores": r["cores"], "kind": "port", "sample": r["sample"],
                          "single_thread": single_thread_baseline(shape, args.cpu_sample_flops / 40)},
         "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
