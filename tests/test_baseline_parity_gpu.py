@@ -119,3 +119,30 @@ def test_config3_sampled_rows_of_every_gemm_shape_and_the_head(gpu):
         rows = [(0, n), (M // 2 - n // 2, M // 2 + n // 2), (M - n, M)]
         check_product(gpu, rng, name, M, N, K, lt, rt, stds, rows=rows)
         torch.cuda.empty_cache()
+
+
+@pytest.mark.parametrize("deterministic", [False, True])
+def test_config3_weight_gradients_in_full_against_float64(gpu, deterministic):
+    # Every element of config 3's weight-gradient products (K = 65,536 tokens, split along K up to 19 ways) and the
+    # head's, accumulated into an initial gradient as the step does (linear.rs:55-57), against a float64 product of
+    # the same bf16 operands on the device: what remains is the f32 accumulation of the tensor core and of the
+    # split-K sums, so a lost or doubled K slice at any split boundary shows at once (a lost 16-row slice alone moves
+    # the result by ~1.5e-2). Bound: the file's summation-order bar, 2e-5 * sqrt(K/1024) = 1.6e-4 as a relative
+    # Frobenius error (3.5e-5 measured on expand.dW).
+    T, w = CONFIGS[3]
+    rng = DeviceRandom(gpu, 1)
+    shapes = [("qkv.dW", w, 3 * w), ("output.dW", w, w), ("expand.dW", w, 4 * w), ("project.dW", 4 * w, w),
+              ("head.dW", w, 16 * 1024)]
+    for name, M, N in shapes:
+        x = rng.normal_(torch.empty(T, M, device="cuda")).bfloat16()
+        dy = rng.normal_(torch.empty(T, N, device="cuda")).bfloat16()
+        initial = rng.normal_(torch.empty(M, N, device="cuda"), 100.0)
+        dw = initial.clone()
+        gpu.gemm(MatmulSpec.new(M, N, T).left_transposed().accumulate(), x, dy, dw, deterministic=deterministic)
+        assert _ffi.last_path() in _ffi.TENSOR_CORE_PATHS, name
+        exact = initial.double() + x.double().t() @ dy.double()
+        err = (torch.linalg.vector_norm(dw.double() - exact) / torch.linalg.vector_norm(exact)).item()
+        assert err <= 2e-5 * (T / 1024) ** 0.5, (name, err)
+        del x, dy, initial, dw, exact
+        torch.cuda.empty_cache()
+    gpu.device_status()
