@@ -591,6 +591,10 @@ def run_ours(args, shape, rank: int, world: int, local_rank: int) -> int:
         cpu = cpu_baseline(shape, budget_flops=args.cpu_sample_flops)
         cpu["single_thread"] = single_thread_baseline(shape, args.cpu_sample_flops / 40)
 
+    attention = None
+    if rank == 0 and world == 1 and args.precision == "bf16" and not args.no_attention_record:
+        attention = attention_record(device, args.steps, args.warmup)
+
     cublas = cublas_rate(device, args.precision) if args.precision != "bf16" and rank == 0 else None
     if rank == 0:
         peaks, source = load_peaks()
@@ -660,11 +664,61 @@ def run_ours(args, shape, rank: int, world: int, local_rank: int) -> int:
                          args.comm == "overlap" else ""),
             }
             line["dp_parity"] = dp_parity
+        if attention is not None:
+            line["attention_cfg4"] = attention
         if cpu is not None:
             line["cpu_baseline"] = {k: cpu[k] for k in ("value", "unit", "cores", "kind", "sample", "single_thread")}
         print(json.dumps(line), flush=True)
     del step
     return 0
+
+
+def attention_record(device, steps: int, warmup: int) -> dict:
+    """BASELINE config 4's fused causal attention forward + backward, timed on the device after the step (its own
+    warm-up, CUDA events and clock samples) so that the default step line carries the attention kernels too."""
+    import torch
+
+    from staleynet_b200.attention import AttentionShape, FusedAttention
+
+    stream = torch.cuda.current_stream(device)
+    shape = AttentionShape()
+    att = FusedAttention(shape, device, seed=0)
+    h = stream.cuda_stream
+    for _ in range(max(3, warmup)):
+        att.forward(h)
+        att.backward(h)
+    torch.cuda.synchronize()
+    clocks = ClockSampler(device.index or 0)
+    clocks.start()
+    # ~0.5 s of launches, so that the clock sampler (one sample per 100 ms) sees the timed region.
+    n = max(600, steps)
+    ev = [[torch.cuda.Event(enable_timing=True) for _ in range(3)] for _ in range(n)]
+    for e in ev:
+        e[0].record(stream)
+        att.forward(h)
+        e[1].record(stream)
+        att.backward(h)
+        e[2].record(stream)
+    torch.cuda.synchronize()
+    clock_info = clocks.stop()
+    fwd_ms = sum(e[0].elapsed_time(e[1]) for e in ev) / n
+    bwd_ms = sum(e[1].elapsed_time(e[2]) for e in ev) / n
+    peaks, source = load_peaks()
+    peak = float(peaks.get("bf16_tflops_sustained", FALLBACK_PEAKS["bf16_tflops_sustained"]))
+    bwd = att.backward_flops / (bwd_ms / 1e3) / 1e12
+    record = {
+        "workload": f"cfg4 causal attention (batch {shape.batch}, {shape.heads} heads of {shape.head_dim}, sequence "
+                    f"{shape.time}) fwd+bwd through snb_causal_attention_forward/backward, bf16",
+        "value": att.flops / ((fwd_ms + bwd_ms) / 1e3) / 1e12, "unit": UNIT, "steps": n,
+        "forward_ms": fwd_ms, "backward_ms": bwd_ms,
+        "backward_roofline": {"bound": "tensor", "achieved": bwd, "peak": peak, "unit": "TFLOP/s",
+                              "frac": bwd / peak, "traffic": load_kernel_traffic("fb_backward_kernel"),
+                              "peak_source": f"{source} bf16_tflops_sustained"},
+        "clocks": clock_info,
+    }
+    del att
+    torch.cuda.empty_cache()
+    return record
 
 
 def run_gemm(args, rank: int, world: int, local_rank: int) -> int:
@@ -1202,6 +1256,8 @@ def main(argv=None) -> int:
                     help="sequences of 2048 tokens per step over all GPUs (config 5: 256, run as 32-sequence "
                          "micro-batches); 0 = one 32-sequence micro-batch per GPU")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-attention-record", action="store_true",
+                    help="step workload at N = 1: leave out the config-4 fused attention sub-record")
     ap.add_argument("--names", default="", help="gemm workload: comma-separated GEMMs of the step (default: all)")
     ap.add_argument("--workload", choices=["step", "attention", "head", "optimizer", "norm", "gemm"], default="step",
                     help="step: the cfg3 training-step GEMMs (default); attention: the cfg4 attention layer; "
