@@ -5,7 +5,8 @@
 // Structure (one persistent CTA of 320 threads per SM, work units strided over the grid):
 //   warp 0     TMA producer: one elected thread streams 128-byte-wide K slices of A and B into a STAGES-deep
 //              shared-memory ring (128B swizzle), completion tracked by `full` mbarriers; it also prefetches each
-//              tile's epilogue inputs (residual, GELU input) into L2.
+//              tile's epilogue inputs (residual, GELU input) into L2 and, in SB kernels, copies the tile's bias into
+//              one of two shared-memory buffers (a 1-D bulk copy) once the epilogue has released that buffer.
 //   warp 1     allocates / frees TMEM (2*BN columns); one elected thread issues tcgen05.mma (M=128, N=BN,
 //              K=32 bytes per instruction) into one of two TMEM accumulators and frees ring slots with
 //              tcgen05.commit on `empty` mbarriers.
@@ -88,19 +89,27 @@ constexpr int TC_EPI_TWO_BOX = 2;
 constexpr int TC_EPI_AUX_BOX = 3;
 constexpr int tc_epi_boxes(int epi) { return epi == TC_EPI_ONE_BOX ? 1 : 2; }
 
+// Shared memory of one sm_100 CTA available to a kernel.
+constexpr int TC_SMEM_LIMIT = 232448;
+
 // NBOX = staging boxes per epilogue warp: 2 lets a chunk be staged while the previous chunk's TMA store still reads
-// its box (worth it for GELU epilogues), at the price of one ring stage for BN = 256.
-template <int BN, int NBOX>
+// its box (worth it for GELU epilogues), at the price of one ring stage for BN = 256. SB = the tile's bias is
+// copied into shared memory (one BN-float buffer per accumulator) instead of being read from global memory by every
+// epilogue warp; the ring keeps as many stages as still fit.
+template <int BN, int NBOX, bool SB = false>
 struct TcConfig {
     static constexpr int STAGE_A = TC_BM * 128;
     static constexpr int STAGE_B = BN * 128;
     static constexpr int STAGE = STAGE_A + STAGE_B;
-    static constexpr int STAGES = BN == 256 ? (NBOX == 2 ? 3 : 4) : (BN == 128 ? 4 : 6);
     static constexpr int EPI_BYTES = TC_EPI_WARPS * NBOX * TC_EPI_BOX_BYTES;
+    static constexpr int BIAS_BYTES = SB ? 2 * BN * 4 : 0;
     static constexpr int TMEM_COLS = 2 * BN;
     static constexpr int BARRIER_BYTES = 512;
-    static constexpr int SMEM_BYTES = 1024 + STAGES * STAGE + EPI_BYTES + BARRIER_BYTES;
-    static_assert(SMEM_BYTES <= 232448, "shared memory budget of one sm_100 CTA");
+    static constexpr int BASE_STAGES = BN == 256 ? (NBOX == 2 ? 3 : 4) : (BN == 128 ? 4 : 6);
+    static constexpr int FIT_STAGES = (TC_SMEM_LIMIT - 1024 - EPI_BYTES - BIAS_BYTES - BARRIER_BYTES) / STAGE;
+    static constexpr int STAGES = BASE_STAGES < FIT_STAGES ? BASE_STAGES : FIT_STAGES;
+    static constexpr int SMEM_BYTES = 1024 + STAGES * STAGE + EPI_BYTES + BIAS_BYTES + BARRIER_BYTES;
+    static_assert(SMEM_BYTES <= TC_SMEM_LIMIT, "shared memory budget of one sm_100 CTA");
     static_assert(TMEM_COLS == 128 || TMEM_COLS == 256 || TMEM_COLS == 512, "TMEM allocation is a power of two");
 };
 
@@ -315,11 +324,13 @@ __device__ __forceinline__ void stage_half(uint8_t* box, int lane, int h, const 
 // The first auxiliary input (GELU input, else residual) is requested before waiting for TMEM so the two latencies
 // overlap; only when both are present is the residual read afterwards. With `aux_box` the first auxiliary input is
 // already in shared memory (TMA-loaded into the 128B-swizzled staging box this half is staged into) and is read
-// from this lane's row of it.
-template <bool OUT_BF16>
+// from this lane's row of it. SB: the bias of these 32 columns is read from shared memory at `bias_s` (the tile's
+// bias buffer, offset to column `col`), a broadcast read, instead of from global memory.
+template <bool OUT_BF16, bool SB = false>
 __device__ __forceinline__ void epilogue_half(const TcParams& p, uint32_t taddr, int32_t col, int32_t row,
                                               int64_t out_base, bool first_split, uint8_t* pre_box, int h,
-                                              float2 (&v)[16], bool pre_only, const uint8_t* aux_box = nullptr) {
+                                              float2 (&v)[16], bool pre_only, const uint8_t* aux_box = nullptr,
+                                              uint32_t bias_s = 0) {
     uint32_t x[32];
     tmem_load_32x32b_x32(taddr, x);
     const int valid = p.N - col;  // columns of this piece inside the matrix (a multiple of 4 or 8)
@@ -353,7 +364,8 @@ __device__ __forceinline__ void epilogue_half(const TcParams& p, uint32_t taddr,
         const float4* b4 = reinterpret_cast<const float4*>(p.bias + col);
 #pragma unroll
         for (int j = 0; j < 8; ++j) {
-            const float4 b = (4 * j < valid) ? __ldg(b4 + j) : make_float4(0.f, 0.f, 0.f, 0.f);
+            float4 b = make_float4(0.f, 0.f, 0.f, 0.f);
+            if (4 * j < valid) b = SB ? ld_shared_f4(bias_s + 16 * j) : __ldg(b4 + j);
             v[2 * j] = __fadd2_rn(v[2 * j], make_float2(b.x, b.y));
             v[2 * j + 1] = __fadd2_rn(v[2 * j + 1], make_float2(b.z, b.w));
         }
@@ -460,10 +472,12 @@ __device__ __forceinline__ void request_aux_boxes(const TcParams& p, const CUten
 //                    one; a kept pre-activation fills both boxes from one TMEM read.
 //   TC_EPI_AUX_BOX   two boxes; chunk j's one bf16 auxiliary input (GELU input or residual, map tm_aux) was
 //                    TMA-loaded into box j by request_aux_boxes and its output overwrites it in place.
-template <bool OUT_BF16, int BN, int EPI>
+//   SB               the tile's bias is in shared memory at bias_tile (BN floats).
+template <bool OUT_BF16, int BN, int EPI, bool SB = false>
 __device__ __forceinline__ void epilogue_tile(const TcParams& p, const CUtensorMap* tm_c, const CUtensorMap* tm_pre,
                                               const TcUnit& u, int32_t row0, uint32_t t_lane, int group,
-                                              uint8_t* boxes, int& ebox, uint64_t* aux_bar, uint32_t& aux_phase) {
+                                              uint8_t* boxes, int& ebox, uint64_t* aux_bar, uint32_t& aux_phase,
+                                              uint32_t bias_tile = 0) {
     constexpr int CHUNK = OUT_BF16 ? 64 : 32;
     const int lane = threadIdx.x & 31;
     const int32_t row = row0 + lane;
@@ -483,8 +497,8 @@ __device__ __forceinline__ void epilogue_tile(const TcParams& p, const CUtensorM
 #pragma unroll
             for (int h = 0; h < CHUNK / 32; ++h) {
                 float2 v[16];
-                epilogue_half<OUT_BF16>(p, t_lane + c + 32 * h, col0 + 32 * h, row, out_base, first_split, nullptr,
-                                        h, v, false, box);
+                epilogue_half<OUT_BF16, SB>(p, t_lane + c + 32 * h, col0 + 32 * h, row, out_base, first_split,
+                                            nullptr, h, v, false, box, bias_tile + 4 * (c + 32 * h));
                 stage_half<OUT_BF16>(box, lane, h, v);
             }
             fence_proxy_async_shared();
@@ -504,8 +518,8 @@ __device__ __forceinline__ void epilogue_tile(const TcParams& p, const CUtensorM
 #pragma unroll
             for (int h = 0; h < CHUNK / 32; ++h) {
                 float2 v[16];
-                epilogue_half<OUT_BF16>(p, t_lane + c + 32 * h, col0 + 32 * h, row, out_base, first_split, pre_box,
-                                        h, v, false);
+                epilogue_half<OUT_BF16, SB>(p, t_lane + c + 32 * h, col0 + 32 * h, row, out_base, first_split,
+                                            pre_box, h, v, false, nullptr, bias_tile + 4 * (c + 32 * h));
                 stage_half<OUT_BF16>(box, lane, h, v);
             }
             fence_proxy_async_shared();
@@ -524,8 +538,8 @@ __device__ __forceinline__ void epilogue_tile(const TcParams& p, const CUtensorM
 #pragma unroll
                 for (int h = 0; h < CHUNK / 32; ++h) {
                     float2 v[16];
-                    epilogue_half<OUT_BF16>(p, t_lane + c + 32 * h, col0 + 32 * h, row, out_base, first_split,
-                                            nullptr, h, v, pass == 0);
+                    epilogue_half<OUT_BF16, SB>(p, t_lane + c + 32 * h, col0 + 32 * h, row, out_base, first_split,
+                                                nullptr, h, v, pass == 0, nullptr, bias_tile + 4 * (c + 32 * h));
                     stage_half<OUT_BF16>(box, lane, h, v);
                 }
                 fence_proxy_async_shared();
@@ -540,14 +554,25 @@ __device__ __forceinline__ void epilogue_tile(const TcParams& p, const CUtensorM
     }
 }
 
-template <typename E, int BN, bool OUT_BF16, int EPI>
+// The bias feed of SB kernels: the producer copies tile t's BN bias values into buffer t & 1 of `bias_s` once the
+// epilogue warps have released that buffer from tile t - 2 (bias_empty), completion on bias_full[t & 1].
+template <int BN>
+__device__ __forceinline__ void issue_tile_bias(const TcParams& p, int32_t n0, uint32_t bias_s, uint64_t* bias_full,
+                                                int buf) {
+    const uint32_t bytes = 4u * static_cast<uint32_t>(min(BN, p.N - n0));  // N % 4 == 0: a multiple of 16
+    const uint32_t bar = smem_addr(&bias_full[buf]);
+    mbar_arrive_expect_tx(bar, bytes);
+    bulk_load_1d(bias_s + static_cast<uint32_t>(buf * BN * 4), p.bias + n0, bytes, bar);
+}
+
+template <typename E, int BN, bool OUT_BF16, int EPI, bool SB = false>
 __global__ void __launch_bounds__(TC_THREADS, 1)
     tc_gemm_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constant__ CUtensorMap tm_b,
                    const __grid_constant__ CUtensorMap tm_c, const __grid_constant__ CUtensorMap tm_pre,
                    const __grid_constant__ CUtensorMap tm_res, const __grid_constant__ CUtensorMap tm_gin,
                    const __grid_constant__ CUtensorMap tm_aux, const TcParams p) {
     constexpr int NBOX = tc_epi_boxes(EPI);
-    using Cfg = TcConfig<BN, NBOX>;
+    using Cfg = TcConfig<BN, NBOX, SB>;
     constexpr int ESIZE = sizeof(E);
     constexpr int BK = 128 / ESIZE;      // K elements per ring slot (one 128-byte swizzle row)
     constexpr int UMMA_K = 32 / ESIZE;   // K elements per tcgen05.mma (32 bytes)
@@ -559,14 +584,18 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     uint8_t* ring = smem;
     uint8_t* epi = smem + Cfg::STAGES * Cfg::STAGE;
-    uint64_t* bars = reinterpret_cast<uint64_t*>(epi + Cfg::EPI_BYTES);
+    const uint32_t bias_s = smem_addr(epi + Cfg::EPI_BYTES);  // SB: two BN-float bias buffers
+    uint64_t* bars = reinterpret_cast<uint64_t*>(epi + Cfg::EPI_BYTES + Cfg::BIAS_BYTES);
     uint64_t* full = bars;
     uint64_t* empty = bars + Cfg::STAGES;
     uint64_t* acc_full = bars + 2 * Cfg::STAGES;
     uint64_t* acc_empty = acc_full + 2;
     uint64_t* drain = acc_empty + 2;
     uint64_t* aux_bars = drain + 1;  // two per epilogue warp
-    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(aux_bars + 2 * TC_EPI_WARPS);
+    uint64_t* bias_full = aux_bars + 2 * TC_EPI_WARPS;
+    uint64_t* bias_empty = bias_full + 2;
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bias_empty + 2);
+    const bool feed_bias = SB && p.bias != nullptr;
 
     const int warp = threadIdx.x >> 5;
     const int lane = threadIdx.x & 31;
@@ -579,6 +608,8 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
         for (int a = 0; a < 2; ++a) {
             mbar_init(smem_addr(&acc_full[a]), 1);
             mbar_init(smem_addr(&acc_empty[a]), TC_EPI_WARPS);  // one arrival per epilogue warp
+            mbar_init(smem_addr(&bias_full[a]), 1);
+            mbar_init(smem_addr(&bias_empty[a]), TC_EPI_WARPS);
         }
         mbar_init(smem_addr(drain), 1);
         for (int b = 0; b < 2 * TC_EPI_WARPS; ++b) mbar_init(smem_addr(&aux_bars[b]), 1);
@@ -605,11 +636,17 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
             int stage = 0;
             uint32_t phase = 0;
             bool ok = true;
+            int tile = 0;
             for (TcCursor cur = tc_cursor(p, blockIdx.x, gridDim.x); cur.unit < p.num_units && ok; tc_advance(p, cur)) {
                 const TcUnit u = tc_cursor_unit(p, cur, BN, BK);
                 if (u.skip) continue;
                 const int32_t ba = p.a_batched ? u.batch : 0;
                 const int32_t bb = p.b_batched ? u.batch : 0;
+                // The tile's bias is copied as soon as its buffer is free, checked between K slices without
+                // blocking the operand loads (the buffer's previous tile is finished long before this tile's).
+                const int bbuf = tile & 1;
+                const uint32_t bpar = ((tile >> 1) & 1) ^ 1u;
+                bool bias_pending = feed_bias;
                 // Bring this tile's epilogue inputs into L2 now; the epilogue reads them one main loop later.
                 if (u.split == 0) {
                     if (p.residual != nullptr) tma_prefetch_l2_3d(&tm_res, u.n0, u.m0, u.batch);
@@ -631,7 +668,17 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
                             tma_load_3d(sb + j * (BK * 128), &tm_b, fb, u.n0 + j * MN_BOX, k0, bb);
                     }
                     if (++stage == Cfg::STAGES) { stage = 0; phase ^= 1u; }
+                    if (bias_pending && mbar_test_wait(smem_addr(&bias_empty[bbuf]), bpar)) {
+                        issue_tile_bias<BN>(p, u.n0, bias_s, bias_full, bbuf);
+                        bias_pending = false;
+                    }
                 }
+                if (!ok) break;
+                if (bias_pending) {
+                    if (!mbar_wait(smem_addr(&bias_empty[bbuf]), bpar)) { ok = false; break; }
+                    issue_tile_bias<BN>(p, u.n0, bias_s, bias_full, bbuf);
+                }
+                ++tile;
             }
         }
         __syncwarp();
@@ -719,14 +766,18 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
             const uint32_t acc_phase = (iter >> 1) & 1;
             if (!mbar_wait(smem_addr(&acc_full[acc]), acc_phase)) break;
             tcgen05_fence_after_sync();
+            if (feed_bias && !mbar_wait(smem_addr(&bias_full[acc]), acc_phase)) break;
             const int32_t row0 = u.m0 + q * 32;
             const uint32_t t_lane = tmem_base + (static_cast<uint32_t>(q * 32) << 16) + acc * BN;
 
-            epilogue_tile<OUT_BF16, BN, EPI>(p, &tm_c, &tm_pre, u, row0, t_lane, group, boxes, ebox, aux_bar,
-                                             aux_phase);
+            epilogue_tile<OUT_BF16, BN, EPI, SB>(p, &tm_c, &tm_pre, u, row0, t_lane, group, boxes, ebox, aux_bar,
+                                                 aux_phase, bias_s + static_cast<uint32_t>(acc * BN * 4));
             tcgen05_fence_before_sync();
             __syncwarp();
-            if (lane == 0) mbar_arrive(smem_addr(&acc_empty[acc]));
+            if (lane == 0) {
+                mbar_arrive(smem_addr(&acc_empty[acc]));
+                if (feed_bias) mbar_arrive(smem_addr(&bias_empty[acc]));
+            }
             ++iter;
             // The next tile's auxiliary input is requested as soon as this tile's stores have read the boxes, so
             // its loads overlap the next main loop.

@@ -4,8 +4,10 @@
 // L2 -> SM traffic per FLOP, which is what limits the single-CTA kernel's main loop on B200.
 //
 // Roles per CTA (320 threads, as the single-CTA kernel):
-//   warp 0     TMA producer in both CTAs: loads this CTA's A rows and B columns into its 6-stage ring; the
-//              completion bytes of both CTAs are counted on the first CTA's `full` barrier (cta_group::2 loads).
+//   warp 0     TMA producer in both CTAs: loads this CTA's A rows and B columns into its ring (4-6 stages by
+//              staging mode); the completion bytes of both CTAs are counted on the first CTA's `full` barrier
+//              (cta_group::2 loads). In SB kernels it also copies each tile's 256 bias values into this CTA's
+//              shared memory (two buffers, local barriers), as in the single-CTA kernel.
 //   warp 1     allocates / frees the pair's TMEM (cta_group::2) in both CTAs; in the first CTA one elected thread
 //              issues the pair MMAs and commits each ring slot back to both CTAs' `empty` barriers and each
 //              finished accumulator to both CTAs' `acc_full` barriers (one plain commit per CTA).
@@ -21,28 +23,32 @@ constexpr int TC2_BM = 256;  // rows per CTA pair (128 per CTA)
 constexpr int TC2_BN = 256;  // columns per pair tile (128 staged per CTA)
 
 // NBOX = staging boxes per epilogue warp, as in the single-CTA kernel: two boxes (GELU epilogues) cost one ring
-// stage.
-template <int NBOX>
+// stage. SB = the tile's bias staged in shared memory (each CTA holds its own copy of the tile's 256 values per
+// accumulator), which costs one more stage.
+template <int NBOX, bool SB = false>
 struct Tc2Config {
     static constexpr int STAGE_A = 128 * 128;
     static constexpr int STAGE_B = (TC2_BN / 2) * 128;
     static constexpr int STAGE = STAGE_A + STAGE_B;
-    static constexpr int STAGES = NBOX == 2 ? 5 : 6;
     static constexpr int EPI_BYTES = TC_EPI_WARPS * NBOX * TC_EPI_BOX_BYTES;
+    static constexpr int BIAS_BYTES = SB ? 2 * TC2_BN * 4 : 0;
     static constexpr int TMEM_COLS = 2 * TC2_BN;
     static constexpr int BARRIER_BYTES = 512;
-    static constexpr int SMEM_BYTES = 1024 + STAGES * STAGE + EPI_BYTES + BARRIER_BYTES;
-    static_assert(SMEM_BYTES <= 232448, "shared memory budget of one sm_100 CTA");
+    static constexpr int BASE_STAGES = NBOX == 2 ? 5 : 6;
+    static constexpr int FIT_STAGES = (TC_SMEM_LIMIT - 1024 - EPI_BYTES - BIAS_BYTES - BARRIER_BYTES) / STAGE;
+    static constexpr int STAGES = BASE_STAGES < FIT_STAGES ? BASE_STAGES : FIT_STAGES;
+    static constexpr int SMEM_BYTES = 1024 + STAGES * STAGE + EPI_BYTES + BIAS_BYTES + BARRIER_BYTES;
+    static_assert(SMEM_BYTES <= TC_SMEM_LIMIT, "shared memory budget of one sm_100 CTA");
 };
 
-template <typename E, bool OUT_BF16, int EPI>
+template <typename E, bool OUT_BF16, int EPI, bool SB = false>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(TC_THREADS, 1)
     tc_gemm_pair_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constant__ CUtensorMap tm_b,
                         const __grid_constant__ CUtensorMap tm_c, const __grid_constant__ CUtensorMap tm_pre,
                         const __grid_constant__ CUtensorMap tm_res, const __grid_constant__ CUtensorMap tm_gin,
                         const __grid_constant__ CUtensorMap tm_aux, const TcParams p) {
     constexpr int NBOX = tc_epi_boxes(EPI);
-    using Cfg = Tc2Config<NBOX>;
+    using Cfg = Tc2Config<NBOX, SB>;
     constexpr int BN = TC2_BN;
     constexpr int ESIZE = sizeof(E);
     constexpr int BK = 128 / ESIZE;
@@ -55,14 +61,18 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(TC_THREADS, 1)
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     uint8_t* ring = smem;
     uint8_t* epi = smem + Cfg::STAGES * Cfg::STAGE;
-    uint64_t* bars = reinterpret_cast<uint64_t*>(epi + Cfg::EPI_BYTES);
+    const uint32_t bias_s = smem_addr(epi + Cfg::EPI_BYTES);  // SB: two 256-float bias buffers of this CTA
+    uint64_t* bars = reinterpret_cast<uint64_t*>(epi + Cfg::EPI_BYTES + Cfg::BIAS_BYTES);
     uint64_t* full = bars;
     uint64_t* empty = bars + Cfg::STAGES;
     uint64_t* acc_full = bars + 2 * Cfg::STAGES;
     uint64_t* acc_empty = acc_full + 2;
     uint64_t* drain = acc_empty + 2;
     uint64_t* aux_bars = drain + 1;  // two per epilogue warp
-    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(aux_bars + 2 * TC_EPI_WARPS);
+    uint64_t* bias_full = aux_bars + 2 * TC_EPI_WARPS;  // this CTA's bias feed (local barriers)
+    uint64_t* bias_empty = bias_full + 2;
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bias_empty + 2);
+    const bool feed_bias = SB && p.bias != nullptr;
 
     const int warp = threadIdx.x >> 5;
     const int lane = threadIdx.x & 31;
@@ -79,6 +89,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(TC_THREADS, 1)
         for (int a = 0; a < 2; ++a) {
             mbar_init(smem_addr(&acc_full[a]), 1);
             mbar_init(smem_addr(&acc_empty[a]), 2 * TC_EPI_WARPS);  // every epilogue warp of both CTAs
+            mbar_init(smem_addr(&bias_full[a]), 1);
+            mbar_init(smem_addr(&bias_empty[a]), TC_EPI_WARPS);      // this CTA's epilogue warps
         }
         mbar_init(smem_addr(drain), 1);
         for (int b = 0; b < 2 * TC_EPI_WARPS; ++b) mbar_init(smem_addr(&aux_bars[b]), 1);
@@ -105,8 +117,12 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(TC_THREADS, 1)
             int stage = 0;
             uint32_t phase = 0;
             bool ok = true;
+            int tile = 0;
             for (TcCursor cur = tc_cursor(p, first_unit, unit_step); cur.unit < p.num_units && ok; tc_advance(p, cur)) {
                 const TcUnit u = tc_cursor_unit(p, cur, BN, BK, TC2_BM);
+                const int bbuf = tile & 1;
+                const uint32_t bpar = ((tile >> 1) & 1) ^ 1u;
+                bool bias_pending = feed_bias;
                 const int32_t ba = p.a_batched ? u.batch : 0;
                 const int32_t bb = p.b_batched ? u.batch : 0;
                 const int32_t m0 = u.m0 + 128 * static_cast<int32_t>(rank);  // this CTA's rows
@@ -132,7 +148,17 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(TC_THREADS, 1)
                             tma_load_3d_pair(sb + j * (BK * 128), &tm_b, fb, n0 + j * MN_BOX, k0, bb);
                     }
                     if (++stage == Cfg::STAGES) { stage = 0; phase ^= 1u; }
+                    if (bias_pending && mbar_test_wait(smem_addr(&bias_empty[bbuf]), bpar)) {
+                        issue_tile_bias<BN>(p, u.n0, bias_s, bias_full, bbuf);
+                        bias_pending = false;
+                    }
                 }
+                if (!ok) break;
+                if (bias_pending) {
+                    if (!mbar_wait(smem_addr(&bias_empty[bbuf]), bpar)) { ok = false; break; }
+                    issue_tile_bias<BN>(p, u.n0, bias_s, bias_full, bbuf);
+                }
+                ++tile;
             }
         }
         __syncwarp();
@@ -215,14 +241,18 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(TC_THREADS, 1)
             const uint32_t acc_phase = (iter >> 1) & 1;
             if (!mbar_wait_cluster(smem_addr(&acc_full[acc]), acc_phase)) break;
             tcgen05_fence_after_sync();
+            if (feed_bias && !mbar_wait(smem_addr(&bias_full[acc]), acc_phase)) break;
             const int32_t row0 = u.m0 + row_off;
             const uint32_t t_lane = tmem_base + (static_cast<uint32_t>(q * 32) << 16) + acc * BN;
 
-            epilogue_tile<OUT_BF16, BN, EPI>(p, &tm_c, &tm_pre, u, row0, t_lane, group, boxes, ebox, aux_bar,
-                                             aux_phase);
+            epilogue_tile<OUT_BF16, BN, EPI, SB>(p, &tm_c, &tm_pre, u, row0, t_lane, group, boxes, ebox, aux_bar,
+                                                 aux_phase, bias_s + static_cast<uint32_t>(acc * BN * 4));
             tcgen05_fence_before_sync();
             __syncwarp();
-            if (lane == 0) mbar_arrive_cluster(map_to_cta(smem_addr(&acc_empty[acc]), 0));
+            if (lane == 0) {
+                mbar_arrive_cluster(map_to_cta(smem_addr(&acc_empty[acc]), 0));
+                if (feed_bias) mbar_arrive(smem_addr(&bias_empty[acc]));
+            }
             ++iter;
             TcCursor next = cur;
             tc_advance(p, next);

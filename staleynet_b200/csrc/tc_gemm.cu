@@ -123,11 +123,11 @@ bool encode_nd(CUtensorMap* map, CUtensorMapDataType dt, int esize, const void* 
     return true;
 }
 
-template <typename E, int BN, bool OUT_BF16, int EPI>
+template <typename E, int BN, bool OUT_BF16, int EPI, bool SB = false>
 int launch(cudaStream_t stream, const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& tc,
            const CUtensorMap& tp, const CUtensorMap& tr, const CUtensorMap& tg, const CUtensorMap& tx,
            const TcParams& p, int grid, std::string* err) {
-    constexpr int smem = TcConfig<BN, tc_epi_boxes(EPI)>::SMEM_BYTES;
+    constexpr int smem = TcConfig<BN, tc_epi_boxes(EPI), SB>::SMEM_BYTES;
     static int configured_device = -1;
     static std::mutex mu;
     int dev = 0;
@@ -136,7 +136,7 @@ int launch(cudaStream_t stream, const CUtensorMap& ta, const CUtensorMap& tb, co
         std::lock_guard<std::mutex> lock(mu);
         // cudaFuncSetAttribute is per device; redo it when the current device changes.
         if (configured_device != dev) {
-            cudaError_t e = cudaFuncSetAttribute(tc_gemm_kernel<E, BN, OUT_BF16, EPI>,
+            cudaError_t e = cudaFuncSetAttribute(tc_gemm_kernel<E, BN, OUT_BF16, EPI, SB>,
                                                  cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
             if (e != cudaSuccess) {
                 *err = cuda_message("cudaFuncSetAttribute(tc_gemm_kernel)", e);
@@ -145,7 +145,7 @@ int launch(cudaStream_t stream, const CUtensorMap& ta, const CUtensorMap& tb, co
             configured_device = dev;
         }
     }
-    tc_gemm_kernel<E, BN, OUT_BF16, EPI><<<grid, TC_THREADS, smem, stream>>>(ta, tb, tc, tp, tr, tg, tx, p);
+    tc_gemm_kernel<E, BN, OUT_BF16, EPI, SB><<<grid, TC_THREADS, smem, stream>>>(ta, tb, tc, tp, tr, tg, tx, p);
     cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess) {
         *err = cuda_message("tc_gemm_kernel launch", e);
@@ -169,9 +169,9 @@ int launch_bn(int bn, int epi, cudaStream_t s, const CUtensorMap* m, const TcPar
 #undef SNB_LAUNCH
 }
 
-template <typename E, bool OUT_BF16, int EPI>
+template <typename E, bool OUT_BF16, int EPI, bool SB = false>
 int launch_pair(cudaStream_t stream, const CUtensorMap* m, const TcParams& p, int grid, std::string* err) {
-    constexpr int smem = Tc2Config<tc_epi_boxes(EPI)>::SMEM_BYTES;
+    constexpr int smem = Tc2Config<tc_epi_boxes(EPI), SB>::SMEM_BYTES;
     static int configured_device = -1;
     static std::mutex mu;
     int dev = 0;
@@ -179,7 +179,7 @@ int launch_pair(cudaStream_t stream, const CUtensorMap* m, const TcParams& p, in
     {
         std::lock_guard<std::mutex> lock(mu);
         if (configured_device != dev) {
-            cudaError_t e = cudaFuncSetAttribute(tc_gemm_pair_kernel<E, OUT_BF16, EPI>,
+            cudaError_t e = cudaFuncSetAttribute(tc_gemm_pair_kernel<E, OUT_BF16, EPI, SB>,
                                                  cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
             if (e != cudaSuccess) {
                 *err = cuda_message("cudaFuncSetAttribute(tc_gemm_pair_kernel)", e);
@@ -188,8 +188,8 @@ int launch_pair(cudaStream_t stream, const CUtensorMap* m, const TcParams& p, in
             configured_device = dev;
         }
     }
-    tc_gemm_pair_kernel<E, OUT_BF16, EPI><<<grid, TC_THREADS, smem, stream>>>(m[0], m[1], m[2], m[3], m[4], m[5],
-                                                                               m[6], p);
+    tc_gemm_pair_kernel<E, OUT_BF16, EPI, SB><<<grid, TC_THREADS, smem, stream>>>(m[0], m[1], m[2], m[3], m[4],
+                                                                                   m[5], m[6], p);
     cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess) {
         *err = cuda_message("tc_gemm_pair_kernel launch", e);
@@ -315,17 +315,22 @@ int tc_gemm_try(cudaStream_t stream, const GemmRequest& r, bool* launched, int* 
     // Tall products wider than 128 columns run on CTA pairs (256 x 256 tiles, a third less L2 traffic per FLOP, and a
     // 6-stage ring that covers the longer load latency while output stores are in flight) when K is long, and for
     // bf16 products also when they are at most 1,024 columns wide. Measured on the training step's K=768 shapes:
-    // pairs are 3-7 % faster at 768 columns (output.fwd, output.dX) but 3-7 % slower at 2,304 and 3,072 (qkv.fwd,
-    // expand.fwd, project.dX), where the pair's main loop waits for the slower of two epilogues. The causal attention
-    // hints are implemented by the single-CTA kernel only.
+    // pairs are 3-7 % faster at 768 columns (output.fwd, output.dX) but 3-7 % slower at 2,304 and 3,072 (project.dX;
+    // qkv.fwd and expand.fwd too while each epilogue warp read the bias from global memory), where the pair's main
+    // loop waits for the slower of two epilogues. The causal attention hints are implemented by the single-CTA
+    // kernel only.
     constexpr int64_t kPairMinKBytes = 4096;  // K >= 2048 bf16 / 1024 f32
     constexpr int64_t kPairMaxNarrowCols = 1024;
     // SMs the persistent grid may occupy: all of them, or the caller's budget (which leaves the rest to kernels on
     // other streams, e.g. a collective running beside the backward pass).
     const int sms = r.sm_budget > 0 ? std::min(r.sm_budget, dev.sm_count) : dev.sm_count;
+    // A short-K bf16 product with a bias and a bf16 output runs on pairs with the bias staged in shared memory (SB
+    // kernels, one ring stage fewer). Long-K products keep the deeper ring and read the bias from global memory.
+    const bool bias_pair = bf16_in && out_bf16 && r.bias != nullptr &&
+                           static_cast<int64_t>(p.inner) * esize < kPairMinKBytes;
     const bool pair = bn == 256 && p.rows > TC_BM && r.causal == SNB_CAUSAL_NONE && sms >= 2 &&
                       (static_cast<int64_t>(p.inner) * esize >= kPairMinKBytes ||
-                       (bf16_in && static_cast<int64_t>(p.cols) <= kPairMaxNarrowCols));
+                       (bf16_in && static_cast<int64_t>(p.cols) <= kPairMaxNarrowCols) || bias_pair);
     const int bm = pair ? TC2_BM : TC_BM;
     const int workers = pair ? sms / 2 : sms;
     const int64_t m_tiles = (p.rows + bm - 1) / bm;
@@ -554,7 +559,14 @@ int tc_gemm_try(cudaStream_t stream, const GemmRequest& r, bool* launched, int* 
     if (aux_box) epi = TC_EPI_AUX_BOX;
     if (pair) {
         const int grid = 2 * static_cast<int>(std::min<int64_t>(units, workers));
-        if (bf16_in && out_bf16) {
+        if (bias_pair) {
+            if (epi == TC_EPI_AUX_BOX)
+                rc = launch_pair<__nv_bfloat16, true, TC_EPI_AUX_BOX, true>(stream, maps, kp, grid, err);
+            else if (epi == TC_EPI_TWO_BOX)
+                rc = launch_pair<__nv_bfloat16, true, TC_EPI_TWO_BOX, true>(stream, maps, kp, grid, err);
+            else
+                rc = launch_pair<__nv_bfloat16, true, TC_EPI_ONE_BOX, true>(stream, maps, kp, grid, err);
+        } else if (bf16_in && out_bf16) {
             if (epi == TC_EPI_AUX_BOX)
                 rc = launch_pair<__nv_bfloat16, true, TC_EPI_AUX_BOX>(stream, maps, kp, grid, err);
             else if (epi == TC_EPI_TWO_BOX)

@@ -460,6 +460,51 @@ def test_cta_pair_kernel_fused_epilogues(gpu, epilogue):
     gpu.device_status()
 
 
+@pytest.mark.parametrize("epilogue", ["bias", "bias_gelu_pre", "bias_residual"])
+@pytest.mark.parametrize("rows,cols,inner", [(8192, 2304, 768), (1000, 648, 256), (16392, 776, 64)])
+def test_short_k_bias_products_stage_the_bias_in_shared_memory(gpu, epilogue, rows, cols, inner):
+    """Short-K bf16 products with a bias and a bf16 output (the forward linears: qkv, expand, output, head) run on
+    CTA pairs whose producer copies each tile's bias into one of two shared-memory buffers while the epilogue of the
+    previous tile on that buffer finishes. Every staging mode (plain, GELU with the pre-activation kept, residual by
+    TMA into the staging boxes), ragged rows and columns, and enough tiles per CTA pair (up to ~4) that both buffers
+    are reused; a distinct bias per column, so a tile reading another tile's buffer shows."""
+    T, n, k = rows, cols, inner
+    x = o.lcg_values(T * k, 91)
+    w = o.lcg_values(k * n, 92) * 0.05
+    b = o.lcg_values(n, 93) * 4
+    res = o.lcg_values(T * n, 94)
+    xb, _ = o.round_bf16(x)
+    wb, _ = o.round_bf16(w)
+    spec = MatmulSpec.new(T, n, k)
+    acc = np.zeros(T * n, np.float32)
+    o.matmul(to_oracle(spec), 1, xb, wb, acc)
+    xt, wt = torch.from_numpy(x).cuda().bfloat16(), torch.from_numpy(w).cuda().bfloat16()
+    bt = torch.from_numpy(b).cuda()
+    out = torch.empty(T * n, device="cuda", dtype=torch.bfloat16)
+    lin = acc + np.tile(b, T)
+    if epilogue == "bias":
+        gpu.gemm(spec, xt, wt, out, bias=bt)
+        expected = lin
+    elif epilogue == "bias_gelu_pre":
+        pre = torch.empty(T * n, device="cuda", dtype=torch.bfloat16)
+        gpu.gemm(spec, xt, wt, out, bias=bt, activation=_ffi.ACTIVATION_GELU, pre_activation=pre)
+        expected = o.gelu(lin)
+        torch.cuda.synchronize()
+        assert o.relative_error(lin, pre.float().cpu().numpy()) < 1e-2
+    else:
+        rt = torch.from_numpy(res).cuda().bfloat16()
+        gpu.gemm(spec, xt, wt, out, bias=bt, residual=rt)
+        expected = lin + rt.float().cpu().numpy()
+    assert _ffi.last_path() == _ffi.PATH_TENSOR_CORE_PAIR
+    torch.cuda.synchronize()
+    got = out.float().cpu().numpy()
+    assert o.relative_error(expected, got) < 1e-2
+    # Column by column: a tile whose bias came from the wrong buffer is off by a whole bias difference.
+    col_err = np.abs(expected.reshape(T, n) - got.reshape(T, n)).max(axis=0)
+    assert col_err.max() < 0.05 * max(1.0, float(np.abs(expected).max()))
+    gpu.device_status()
+
+
 GOLDEN = __import__("json").loads((__import__("pathlib").Path(__file__).parent / "golden" / "reference_kats.json").read_text())
 
 
