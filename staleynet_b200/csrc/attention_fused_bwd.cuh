@@ -19,7 +19,8 @@
 //                  it K-major, the dQ product reads the same bytes M-major (queries contiguous).
 //     warps 0-11   per key row (TMEM lane quadrant warp % 4) and query group (warp / 4: 48, 48 and 32 of the 128
 //                  queries): P = 2^(S c + nl), dS = P (dP - D), causal and range masks applied, P^T stored bf16 into
-//                  TMEM, dS^T into shared memory; at the end warps 0-7 write dV and scale * dK.
+//                  TMEM, dS^T into shared memory; at the end warps 0-3 write dV and warps 8-11 scale * dK through
+//                  the dS^T buffer with TMA stores.
 //     warps 4-11   also drain dQ_{i-1} after their share of tile i (queries on lanes; warps 4-7 columns 0-31, warps
 //                  8-11 columns 32-63): scale it and add it into the global dQ (f32, zeroed by the host) with TMA
 //                  reduce-add, each warp through its own 128B-swizzled 32x32 staging box, while dV and dK of tile i
@@ -35,7 +36,7 @@ constexpr int FB_BK = 128;   // keys per CTA (TMEM lanes of S^T, dP^T, dV, dK)
 constexpr int FB_BQ = 128;   // queries per iteration
 constexpr int FB_D = 64;
 constexpr int FB_STAGES = 3;
-constexpr int FB_ELEM_WARPS = 12;   // warps 0-11: P and dS; warps 8-11 also drain dQ
+constexpr int FB_ELEM_WARPS = 12;   // warps 0-11: P and dS; warps 4-11 also drain dQ
 constexpr int FB_PRODUCER_WARP = 12;
 constexpr int FB_MMA_WARP = 13;
 constexpr int FB_THREADS = 14 * 32;
@@ -50,8 +51,6 @@ struct FbParams {
     int64_t offset;          // query q sees keys 0..=q+offset
     float scale;             // softmax scale
     float scale_log2;        // scale * log2(e)
-    float* dk;               // [count, sk, 64] f32
-    float* dv;               // [count, sk, 64] f32
 };
 
 struct FbSmem {
@@ -141,6 +140,7 @@ __global__ void __launch_bounds__(FB_THREADS, 1)
     fb_backward_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
                        const __grid_constant__ CUtensorMap tm_v, const __grid_constant__ CUtensorMap tm_do,
                        const __grid_constant__ CUtensorMap tm_stats, const __grid_constant__ CUtensorMap tm_dq,
+                       const __grid_constant__ CUtensorMap tm_dk, const __grid_constant__ CUtensorMap tm_dv,
                        const FbParams p) {
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -443,33 +443,50 @@ __global__ void __launch_bounds__(FB_THREADS, 1)
         }
         if (drains) {
             if (ok && n_iter > 0) ok = drain(n_iter - 1);
-            if (lane == 0) bulk_wait_group<0>();
+            // The reductions complete on their own; the CTA only has to keep its staging boxes until they are read.
+            if (lane == 0) bulk_wait_group_read<0>();
             __syncwarp();
         }
-        if (group < 2 && ok && warp_wait(smem_addr(acc_done), 0)) {
-            // dV (group 0) or scale * dK (group 1) of this warp's 32 key rows (zero when no query sees them). The
-            // TMEM loads are warp-collective; only the stores depend on the row.
-            const int h = group;
+        if (group != 1 && ok && warp_wait(smem_addr(acc_done), 0)) {
+            // dV (group 0) or scale * dK (group 2, whose last drain ends before group 1's) of this warp's 32 key rows
+            // (zero when no query sees them), staged as two 128B-swizzled 32 x 32 f32 boxes through this warp's 4 KB
+            // of the dS^T buffer (free: every product has finished) and written with TMA stores, which clip the rows
+            // past the last key.
+            const int h = group == 0 ? 0 : 1;
             tcgen05_fence_after_sync();
-            float* dst = (h == 0 ? p.dv : p.dk) + (static_cast<int64_t>(matrix) * p.sk + key) * FB_D;
-            const float mul = n_iter == 0 ? 0.0f : (h == 0 ? 1.0f : p.scale);
+            const float mul = h == 0 ? 1.0f : p.scale;
+            uint8_t* wbox = ds_s + (4 * h + quad) * 4096;
+            const uint32_t wrow = smem_addr(wbox + lane * 128);
             for (int c0 = 0; c0 < FB_D; c0 += 32) {
                 uint32_t o[32];
                 tmem_load_32x32b_x32(tmem_base + lane_base + (h == 0 ? FB_DV_COL : FB_DK_COL) + c0, o);
                 tmem_load_wait();
-                if (key < p.sk) {
-                    float4* d4 = reinterpret_cast<float4*>(dst + c0);
+                if (c0 > 0) {
+                    if (lane == 0) bulk_wait_group_read<0>();   // the first box has been read
+                    __syncwarp();
+                }
 #pragma unroll
-                    for (int g = 0; g < 8; ++g) {
-                        // (n_iter == 0: TMEM holds no product; an explicit zero keeps stale bits out.)
-                        d4[g] = n_iter == 0 ? make_float4(0.0f, 0.0f, 0.0f, 0.0f)
-                                            : make_float4(__uint_as_float(o[4 * g]) * mul,
-                                                          __uint_as_float(o[4 * g + 1]) * mul,
-                                                          __uint_as_float(o[4 * g + 2]) * mul,
-                                                          __uint_as_float(o[4 * g + 3]) * mul);
+                for (int g = 0; g < 8; ++g) {
+                    // (n_iter == 0: TMEM holds no product; an explicit zero keeps stale bits out.)
+                    const uint32_t off = (g ^ (lane & 7)) << 4;
+                    if (n_iter == 0) {
+                        st_shared_v4(wrow + off, 0u, 0u, 0u, 0u);
+                    } else {
+                        st_shared_v4(wrow + off, __float_as_uint(__uint_as_float(o[4 * g]) * mul),
+                                     __float_as_uint(__uint_as_float(o[4 * g + 1]) * mul),
+                                     __float_as_uint(__uint_as_float(o[4 * g + 2]) * mul),
+                                     __float_as_uint(__uint_as_float(o[4 * g + 3]) * mul));
                     }
                 }
+                fence_proxy_async_shared();
+                __syncwarp();
+                if (lane == 0) {
+                    tma_store_3d(h == 0 ? &tm_dv : &tm_dk, smem_addr(wbox), c0, key0 + 32 * quad, matrix);
+                    bulk_commit_group();
+                }
             }
+            if (lane == 0) bulk_wait_group_read<0>();
+            __syncwarp();
         }
     }
 

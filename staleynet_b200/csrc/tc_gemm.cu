@@ -807,9 +807,9 @@ int fused_attention_backward(cudaStream_t stream, const void* q, const void* k, 
         *err = cuda_message("fb_rowstats_kernel launch", e);
         return SNB_ERR_CUDA;
     }
-    CUtensorMap tq, tk, tv, tdo, tst, tdq;
+    CUtensorMap tq, tk, tv, tdo, tst, tdq, tdk, tdv;
     // [count, rows, 64] bf16 tiles of 128 rows (one 128-byte swizzle row each); the statistics as 256-float rows
-    // (128 queries); dQ as f32 boxes of 32 columns x 32 rows (128-byte swizzle rows).
+    // (128 queries); dQ, dK and dV as f32 boxes of 32 columns x 32 rows (128-byte swizzle rows).
     if (!encode_3d(&tq, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, q, FB_D, queries, count, FB_D, queries * FB_D, FB_D,
                    FB_BQ, err) ||
         !encode_3d(&tdo, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, d_out, FB_D, queries, count, FB_D, queries * FB_D, FB_D,
@@ -821,7 +821,9 @@ int fused_attention_backward(cudaStream_t stream, const void* q, const void* k, 
         !encode_3d(&tst, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, stats, 2 * queries, count, 1, stride, stride * count,
                    2 * FB_BQ, 1, err, CU_TENSOR_MAP_SWIZZLE_NONE) ||
         !encode_3d(&tdq, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, dq, FB_D, queries, count, FB_D, queries * FB_D, 32, 32,
-                   err)) {
+                   err) ||
+        !encode_3d(&tdk, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, dk, FB_D, keys, count, FB_D, keys * FB_D, 32, 32, err) ||
+        !encode_3d(&tdv, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, dv, FB_D, keys, count, FB_D, keys * FB_D, 32, 32, err)) {
         release();
         return SNB_ERR_INVALID_ARGUMENT;
     }
@@ -837,8 +839,6 @@ int fused_attention_backward(cudaStream_t stream, const void* q, const void* k, 
     fp.offset = static_cast<int64_t>(query_offset);
     fp.scale = scale;
     fp.scale_log2 = scale * 1.4426950408889634f;
-    fp.dk = dk;
-    fp.dv = dv;
     const int64_t grid = static_cast<int64_t>((keys + FB_BK - 1) / FB_BK) * static_cast<int64_t>(count);
     if (grid > 0x7fffffff) {
         release();
@@ -860,7 +860,7 @@ int fused_attention_backward(cudaStream_t stream, const void* q, const void* k, 
         }
     }
     fb_backward_kernel<<<static_cast<unsigned>(grid), FB_THREADS, FbSmem::BYTES, stream>>>(tq, tk, tv, tdo, tst, tdq,
-                                                                                           fp);
+                                                                                           tdk, tdv, fp);
     e = cudaGetLastError();
     release();
     if (e != cudaSuccess) {
