@@ -9,7 +9,8 @@
 //   fb_rowstats_kernel   per query: (-lse * log2(e), D) into a scratch buffer, one warp per query row.
 //   fb_backward_kernel   one CTA of 448 threads per 128-key tile of one matrix, looping over the query tiles whose
 //                        queries see any of its keys. Keys sit on the TMEM lanes:
-//     warp 12      TMA: K_j, V_j once; then Q_i, dO_i and the row statistics of tile i through a 3-stage ring.
+//     warp 12      TMA: K_j, V_j once; then Q_i, dO_i and the row statistics of tile i through a 3-stage ring
+//                  (K_j, V_j and the first stages requested before the CTA's set-up barrier).
 //     warp 13      allocates TMEM (S^T, dP^T: 128 f32 columns each; dV, dK, dQ: 64 each; P^T: 64 columns of bf16
 //                  pairs) and, on one elected thread, issues per query tile i:
 //                    S^T = K_j Q_i^T, dP^T = V_j dO_i^T          (M=128 keys, N=128 queries, K=64)
@@ -181,12 +182,42 @@ __global__ void __launch_bounds__(FB_THREADS, 1)
     const int32_t i_first = q_lo <= 0 ? 0 : static_cast<int32_t>(q_lo / FB_BQ);
     const int32_t n_iter = q_lo > static_cast<int64_t>(p.sq) - 1 ? 0 : p.q_tiles - i_first;
 
-    if (threadIdx.x == 0) {
+    // The producer starts K, V and the first Q, dO stages before the CTA-wide barrier: it prefetches the tensor
+    // maps, initialises the barriers of its own loads and issues them, so that they overlap the other barriers'
+    // set-up and the TMEM allocation.
+    bool producer = false;
+    if (warp == FB_PRODUCER_WARP) producer = elect_one();
+    int pstage = 0;
+    uint32_t pphase = 0;
+    int32_t pn = 0;   // query tiles whose Q, dO and statistics are requested
+    auto load_stage = [&](int32_t n) {
+        const int32_t q0 = (i_first + n) * FB_BQ;
+        const uint32_t fb = smem_addr(&qdo_full[pstage]);
+        uint8_t* st = stage_s + pstage * FbSmem::STAGE;
+        mbar_arrive_expect_tx(fb, FbSmem::STAGE);
+        tma_load_3d(smem_addr(st), &tm_q, fb, 0, q0, matrix);
+        tma_load_3d(smem_addr(st + FbSmem::QT), &tm_do, fb, 0, q0, matrix);
+        tma_load_3d(smem_addr(st + 2 * FbSmem::QT), &tm_stats, fb, 2 * q0, matrix, 0);
+        if (++pstage == FB_STAGES) { pstage = 0; pphase ^= 1u; }
+    };
+    if (producer) {
+        for (const CUtensorMap* m : {&tm_k, &tm_v, &tm_q, &tm_do, &tm_stats, &tm_dq, &tm_dk, &tm_dv})
+            tma_prefetch_descriptor(m);
         mbar_init(smem_addr(kv_full), 1);
         for (int s = 0; s < FB_STAGES; ++s) {
             mbar_init(smem_addr(&qdo_full[s]), 1);
             mbar_init(smem_addr(&qdo_empty[s]), 1);
         }
+        fence_mbarrier_init();
+        if (n_iter > 0) {
+            const uint32_t kb = smem_addr(kv_full);
+            mbar_arrive_expect_tx(kb, 2 * FbSmem::KV);
+            tma_load_3d(smem_addr(k_s), &tm_k, kb, 0, key0, matrix);
+            tma_load_3d(smem_addr(v_s), &tm_v, kb, 0, key0, matrix);
+            for (; pn < n_iter && pn < FB_STAGES; ++pn) load_stage(pn);   // the ring starts empty
+        }
+    }
+    if (threadIdx.x == 0) {
         mbar_init(smem_addr(sdp_full), 1);
         mbar_init(smem_addr(sdp_empty), FB_ELEM_WARPS);
         mbar_init(smem_addr(pds_full), FB_ELEM_WARPS);
@@ -208,24 +239,11 @@ __global__ void __launch_bounds__(FB_THREADS, 1)
     const uint32_t tmem_base = *tmem_slot;
 
     if (warp == FB_PRODUCER_WARP) {
-        // ------------------------------------------------------------------ TMA producer
-        if (elect_one() && n_iter > 0) {
-            const uint32_t kb = smem_addr(kv_full);
-            mbar_arrive_expect_tx(kb, 2 * FbSmem::KV);
-            tma_load_3d(smem_addr(k_s), &tm_k, kb, 0, key0, matrix);
-            tma_load_3d(smem_addr(v_s), &tm_v, kb, 0, key0, matrix);
-            int stage = 0;
-            uint32_t phase = 0;
-            for (int32_t n = 0; n < n_iter; ++n) {
-                const int32_t q0 = (i_first + n) * FB_BQ;
-                if (!mbar_wait(smem_addr(&qdo_empty[stage]), phase ^ 1u)) break;
-                const uint32_t fb = smem_addr(&qdo_full[stage]);
-                uint8_t* st = stage_s + stage * FbSmem::STAGE;
-                mbar_arrive_expect_tx(fb, FbSmem::STAGE);
-                tma_load_3d(smem_addr(st), &tm_q, fb, 0, q0, matrix);
-                tma_load_3d(smem_addr(st + FbSmem::QT), &tm_do, fb, 0, q0, matrix);
-                tma_load_3d(smem_addr(st + 2 * FbSmem::QT), &tm_stats, fb, 2 * q0, matrix, 0);
-                if (++stage == FB_STAGES) { stage = 0; phase ^= 1u; }
+        // ------------------------------------------------------------------ TMA producer: the remaining stages
+        if (producer) {
+            for (; pn < n_iter; ++pn) {
+                if (!mbar_wait(smem_addr(&qdo_empty[pstage]), pphase ^ 1u)) break;
+                load_stage(pn);
             }
         }
         __syncwarp();
