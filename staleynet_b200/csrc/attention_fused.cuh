@@ -110,12 +110,37 @@ __global__ void __launch_bounds__(FA_THREADS, 1)
     const int32_t nsteps = max(steps0, steps1);
     constexpr uint32_t kSoftmaxArrivals = FA_SOFTMAX_WARPS / 2;  // warps per tile
 
-    if (threadIdx.x == 0) {
+    // The producer starts Q and the first K/V stages before the CTA-wide barrier: it prefetches the tensor maps,
+    // initialises the barriers of its own loads and issues them, so that they overlap the other barriers' set-up
+    // and the TMEM allocation.
+    bool producer = false;
+    if (warp == FA_PRODUCER_WARP) producer = elect_one();
+    int pstage = 0;
+    uint32_t pphase = 0;
+    int32_t pj = 0;   // key steps whose K and V are requested
+    auto load_kv = [&](int32_t j) {
+        const uint32_t fb = smem_addr(&kv_full[pstage]);
+        mbar_arrive_expect_tx(fb, 2 * FaSmem::KV);
+        uint8_t* kt = kv_s + pstage * 2 * FaSmem::KV;
+        tma_load_3d(smem_addr(kt), &tm_k, fb, 0, j * FA_BN, matrix);
+        tma_load_3d(smem_addr(kt + FaSmem::KV), &tm_v, fb, 0, j * FA_BN, matrix);
+        if (++pstage == FA_KV_STAGES) { pstage = 0; pphase ^= 1u; }
+    };
+    if (producer) {
+        for (const CUtensorMap* m : {&tm_q, &tm_k, &tm_v}) tma_prefetch_descriptor(m);
         mbar_init(smem_addr(q_full), 1);
         for (int i = 0; i < FA_KV_STAGES; ++i) {
             mbar_init(smem_addr(&kv_full[i]), 1);
             mbar_init(smem_addr(&kv_empty[i]), 1);
         }
+        fence_mbarrier_init();
+        const uint32_t qb = smem_addr(q_full);
+        mbar_arrive_expect_tx(qb, 2 * FaSmem::Q);
+        tma_load_3d(smem_addr(q_s), &tm_q, qb, 0, q_first, matrix);
+        tma_load_3d(smem_addr(q_s + FaSmem::Q), &tm_q, qb, 0, q_first + FA_BM, matrix);
+        for (; pj < nsteps && pj < FA_KV_STAGES; ++pj) load_kv(pj);   // the ring starts empty
+    }
+    if (threadIdx.x == 0) {
         for (int i = 0; i < 2; ++i) {
             mbar_init(smem_addr(&s_full[i]), 1);
             mbar_init(smem_addr(&s_empty[i]), kSoftmaxArrivals);
@@ -137,21 +162,10 @@ __global__ void __launch_bounds__(FA_THREADS, 1)
 
     if (warp == FA_PRODUCER_WARP) {
         // ------------------------------------------------------------------ TMA producer
-        if (elect_one()) {
-            const uint32_t qb = smem_addr(q_full);
-            mbar_arrive_expect_tx(qb, 2 * FaSmem::Q);
-            tma_load_3d(smem_addr(q_s), &tm_q, qb, 0, q_first, matrix);
-            tma_load_3d(smem_addr(q_s + FaSmem::Q), &tm_q, qb, 0, q_first + FA_BM, matrix);
-            int stage = 0;
-            uint32_t phase = 0;
-            for (int32_t j = 0; j < nsteps; ++j) {
-                if (!mbar_wait(smem_addr(&kv_empty[stage]), phase ^ 1u)) break;
-                const uint32_t fb = smem_addr(&kv_full[stage]);
-                mbar_arrive_expect_tx(fb, 2 * FaSmem::KV);
-                uint8_t* kt = kv_s + stage * 2 * FaSmem::KV;
-                tma_load_3d(smem_addr(kt), &tm_k, fb, 0, j * FA_BN, matrix);
-                tma_load_3d(smem_addr(kt + FaSmem::KV), &tm_v, fb, 0, j * FA_BN, matrix);
-                if (++stage == FA_KV_STAGES) { stage = 0; phase ^= 1u; }
+        if (producer) {
+            for (; pj < nsteps; ++pj) {
+                if (!mbar_wait(smem_addr(&kv_empty[pstage]), pphase ^ 1u)) break;
+                load_kv(pj);
             }
         }
         __syncwarp();
