@@ -464,15 +464,17 @@ def run_ours(args, shape, rank: int, world: int, local_rank: int) -> int:
     # Timed region: device-resident inputs.
     n_launch = step.launches_per_step()
     timed = lambda: torch.cuda.Event(enable_timing=True)  # noqa: E731
-    ev_steps = [[[(timed(), timed()) for _ in range(n_launch)] for _ in range(n_micro)] for _ in range(args.steps)]
     comm_marks = [(timed(), timed()) for _ in range(args.steps)]
+    # The GEMM launch times of the roofline and of the per-GEMM breakdown come from one step run just before the
+    # timed region with events around each launch. The timed steps carry no per-launch events: an event between two
+    # GEMMs would make the second wait for the first to finish completely, where otherwise its CTAs start their
+    # set-up during the first's tail (programmatic dependent launch).
+    ev_pass = [[[(timed(), timed()) for _ in range(n_launch)] for _ in range(n_micro)]]
+    step.run_step(handle, events=ev_pass[0])
+    finish()
+    torch.cuda.synchronize()
     graphs = [step.capture(m) for m in range(n_micro)] if args.graph else None
     if graphs is not None:
-        torch.cuda.synchronize()
-        # The GEMM launch times of the roofline come from an uncaptured pass with events around each launch.
-        ev_pass = [[[(timed(), timed()) for _ in range(n_launch)] for _ in range(n_micro)]]
-        step.run_step(handle, events=ev_pass[0])
-        finish()
         torch.cuda.synchronize()
     clocks = ClockSampler(local_rank)
     clocks.start()
@@ -480,7 +482,7 @@ def run_ours(args, shape, rank: int, world: int, local_rank: int) -> int:
     start.record(stream)
     for k in range(args.steps):
         if graphs is None:
-            step.run_step(handle, on_block_done=hook, events=ev_steps[k])
+            step.run_step(handle, on_block_done=hook)
         else:
             step.zero_grads()
             for g in graphs:
@@ -492,11 +494,8 @@ def run_ours(args, shape, rank: int, world: int, local_rank: int) -> int:
     if world > 1:
         dist.barrier()
     ms_total = start.elapsed_time(end)
-    if graphs is not None:
-        ev_steps = ev_pass
-        kernel_ms = sum(a.elapsed_time(b) for ev_micro in ev_pass for pairs in ev_micro for a, b in pairs) * args.steps
-    else:
-        kernel_ms = sum(a.elapsed_time(b) for ev_micro in ev_steps for pairs in ev_micro for a, b in pairs)
+    ev_steps = ev_pass
+    kernel_ms = sum(a.elapsed_time(b) for ev_micro in ev_pass for pairs in ev_micro for a, b in pairs) * args.steps
     exposed_ms = sum(a.elapsed_time(b) for a, b in comm_marks) / args.steps
 
     # End-to-end: every micro-batch's input activations come from pinned host memory and the step's per-codebook
@@ -635,7 +634,8 @@ def run_ours(args, shape, rank: int, world: int, local_rank: int) -> int:
                                      (kernel_ms / 1e3) / 1e9) if "algorithmic_bytes_per_launch" in traffic else None,
                 "hbm_peak_gbs": float(peaks.get("hbm_gbs", FALLBACK_PEAKS["hbm_gbs"])),
                 "kernel": ("snb::simt_gemm_kernel (exact f32 FMA)" if args.precision == "f32" else
-                           "snb::tc_gemm_kernel / tc_gemm_pair_kernel") + " (all GEMM launches of a step on rank 0)",
+                           "snb::tc_gemm_kernel / tc_gemm_pair_kernel") + " (all GEMM launches of a step on rank 0, timed by "
+                                                                   "events in one step run before the timed region)",
                 "peak_source": peak_source,
                 "launches_per_step": launches,
                 "flops_per_step": flops_rank,

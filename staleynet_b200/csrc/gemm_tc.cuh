@@ -599,6 +599,9 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
 
     const int warp = threadIdx.x >> 5;
     const int lane = threadIdx.x & 31;
+    // The next GEMM of the stream may start its set-up as this grid's CTAs finish (programmatic dependent launch);
+    // it touches no global memory before its own griddep_wait below.
+    griddep_launch_dependents();
 
     if (threadIdx.x == 0) {
         for (int s = 0; s < Cfg::STAGES; ++s) {
@@ -629,6 +632,8 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
     __syncthreads();
     tcgen05_fence_after_sync();
     const uint32_t tmem_base = *tmem_slot;
+    // Everything above is local set-up; the operands, epilogue inputs and outputs may belong to the previous kernel.
+    griddep_wait();
 
     if (warp == 0) {
         // ------------------------------------------------------------------ TMA producer

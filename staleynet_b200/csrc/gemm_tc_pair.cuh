@@ -80,6 +80,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(TC_THREADS, 1)
     const bool leader = rank == 0;
     const int32_t first_unit = static_cast<int32_t>(blockIdx.x >> 1);
     const int32_t unit_step = static_cast<int32_t>(gridDim.x >> 1);
+    griddep_launch_dependents();   // as in the single-CTA kernel
 
     if (threadIdx.x == 0) {
         for (int s = 0; s < Cfg::STAGES; ++s) {
@@ -110,6 +111,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(TC_THREADS, 1)
     cluster_sync();  // both CTAs' barriers exist before either CTA signals the other's
     tcgen05_fence_after_sync();
     const uint32_t tmem_base = *tmem_slot;
+    griddep_wait();  // no global memory before the previous kernel of the stream has completed
 
     if (warp == 0) {
         // ------------------------------------------------------------------ TMA producer (both CTAs)

@@ -70,6 +70,14 @@ __device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
     return done != 0;
 }
 
+// Programmatic dependent launch: let the next kernel of the stream (launched with programmatic stream
+// serialisation) be scheduled now; its CTAs still run only where this grid's CTAs have left room.
+__device__ __forceinline__ void griddep_launch_dependents() {
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+// Wait until every grid this one depends on has completed and its memory operations are visible.
+__device__ __forceinline__ void griddep_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+
 // Non-blocking probe: true if the phase with the given parity has completed.
 __device__ __forceinline__ bool mbar_test_wait(uint32_t bar, uint32_t parity) {
     uint32_t done;

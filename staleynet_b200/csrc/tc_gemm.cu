@@ -4,6 +4,7 @@
 #include <cuda_runtime.h>
 
 #include <algorithm>
+#include <utility>
 #include <mutex>
 
 #include "attention_fused.cuh"
@@ -123,6 +124,26 @@ bool encode_nd(CUtensorMap* map, CUtensorMapDataType dt, int esize, const void* 
     return true;
 }
 
+// Launches a GEMM kernel with programmatic stream serialisation: its CTAs may be scheduled while the previous
+// kernel of the stream finishes (the kernels call griddepcontrol.wait before touching global memory, and let their
+// own dependents start early with griddepcontrol.launch_dependents), so the set-up of one GEMM (barriers, TMEM,
+// tensor-map prefetch) overlaps the tail of the one before.
+template <typename... KArgs, typename... Args>
+cudaError_t launch_with_dependents(void (*kernel)(KArgs...), int grid, int threads, int smem, cudaStream_t stream,
+                                   Args&&... args) {
+    cudaLaunchConfig_t cfg{};
+    cfg.gridDim = dim3(static_cast<unsigned>(grid));
+    cfg.blockDim = dim3(static_cast<unsigned>(threads));
+    cfg.dynamicSmemBytes = static_cast<size_t>(smem);
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...);
+}
+
 template <typename E, int BN, bool OUT_BF16, int EPI, bool SB = false>
 int launch(cudaStream_t stream, const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& tc,
            const CUtensorMap& tp, const CUtensorMap& tr, const CUtensorMap& tg, const CUtensorMap& tx,
@@ -145,8 +166,8 @@ int launch(cudaStream_t stream, const CUtensorMap& ta, const CUtensorMap& tb, co
             configured_device = dev;
         }
     }
-    tc_gemm_kernel<E, BN, OUT_BF16, EPI, SB><<<grid, TC_THREADS, smem, stream>>>(ta, tb, tc, tp, tr, tg, tx, p);
-    cudaError_t e = cudaGetLastError();
+    cudaError_t e = launch_with_dependents(tc_gemm_kernel<E, BN, OUT_BF16, EPI, SB>, grid, TC_THREADS, smem, stream,
+                                           ta, tb, tc, tp, tr, tg, tx, p);
     if (e != cudaSuccess) {
         *err = cuda_message("tc_gemm_kernel launch", e);
         return SNB_ERR_CUDA;
@@ -188,9 +209,8 @@ int launch_pair(cudaStream_t stream, const CUtensorMap* m, const TcParams& p, in
             configured_device = dev;
         }
     }
-    tc_gemm_pair_kernel<E, OUT_BF16, EPI, SB><<<grid, TC_THREADS, smem, stream>>>(m[0], m[1], m[2], m[3], m[4],
-                                                                                   m[5], m[6], p);
-    cudaError_t e = cudaGetLastError();
+    cudaError_t e = launch_with_dependents(tc_gemm_pair_kernel<E, OUT_BF16, EPI, SB>, grid, TC_THREADS, smem, stream,
+                                           m[0], m[1], m[2], m[3], m[4], m[5], m[6], p);
     if (e != cudaSuccess) {
         *err = cuda_message("tc_gemm_pair_kernel launch", e);
         return SNB_ERR_CUDA;
