@@ -21,7 +21,12 @@
  * Conventions shared by every entry point:
  *   - All pointers are caller-owned device pointers; nothing is allocated or freed inside a call.
  *   - `stream` is a cudaStream_t passed as void* (NULL = the legacy default stream). Calls are asynchronous and
- *     ordered on that stream, like the reference's single `Gpu::stream` (device.rs:129-145).
+ *     ordered on that stream, like the reference's single `Gpu::stream` (device.rs:129-145). The tensor-core GEMM
+ *     kernels use programmatic dependent launch: each waits (griddepcontrol.wait) for the previous kernel of the
+ *     stream to complete before touching global memory, and lets the next one be scheduled early
+ *     (griddepcontrol.launch_dependents). A caller's own kernel launched right after with programmatic stream
+ *     serialisation must therefore call griddepcontrol.wait before reading a GEMM's output; ordinary launches,
+ *     events and copies are ordered exactly as without it.
  *   - Lengths are element counts, the `len()` of the reference's `Tensor` (device.rs:262-265).
  *   - Return value: SNB_OK or a positive SNB_ERR_* code. The reference panics on undersized operands
  *     (ops/matmul.rs:147-149) and returns `DriverError` on launch failure; here both become status codes, and
