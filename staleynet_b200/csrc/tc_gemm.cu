@@ -348,8 +348,12 @@ int tc_gemm_try(cudaStream_t stream, const GemmRequest& r, bool* launched, int* 
     // kernels, one ring stage fewer). Long-K products keep the deeper ring and read the bias from global memory.
     const bool bias_pair = bf16_in && out_bf16 && r.bias != nullptr &&
                            static_cast<int64_t>(p.inner) * esize < kPairMinKBytes;
+    // TF32 products move twice the operand bytes per FLOP of bf16 ones while their epilogue stays the same, so pairs
+    // pay at every K except where the epilogue reads an f32 GELU input row by row (project.dX): measured on the
+    // step's K=768 shapes, qkv.fwd +18 %, head.fwd +24 %, output.dX +18 %, expand.fwd +4 %, project.dX -8 %.
+    const bool tf32_pair = !bf16_in && r.activation != SNB_ACTIVATION_GELU_GRAD;
     const bool pair = bn == 256 && p.rows > TC_BM && r.causal == SNB_CAUSAL_NONE && sms >= 2 &&
-                      (static_cast<int64_t>(p.inner) * esize >= kPairMinKBytes ||
+                      (tf32_pair || static_cast<int64_t>(p.inner) * esize >= kPairMinKBytes ||
                        (bf16_in && static_cast<int64_t>(p.cols) <= kPairMaxNarrowCols) || bias_pair);
     const int bm = pair ? TC2_BM : TC_BM;
     const int workers = pair ? sms / 2 : sms;
